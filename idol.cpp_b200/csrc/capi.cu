@@ -1,0 +1,286 @@
+// capi.cu - the extern "C" entry points declared in include/idol_b200.h, and the host helpers they share.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+
+namespace idol {
+
+namespace {
+thread_local std::string g_last_error;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int g_sms[64] = {0};
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return IDOL_ERR_CUDA;
+}
+
+int num_sms(int device) {
+    if (device < 0 || device >= 64) return 148;
+    if (!g_sms[device]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+        g_sms[device] = v;
+    }
+    return g_sms[device];
+}
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(IDOL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(IDOL_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return IDOL_OK;
+}
+
+}  // namespace idol
+
+using idol::fail;
+
+struct idol_q8_matrix {
+    idol::Q8Matrix m;
+};
+
+namespace {
+
+bool shape_ok(int out, int in) { return out >= 1 && in >= 32 && in % 32 == 0; }
+
+int alloc_matrix(int out, int in, int device, idol_q8_matrix** result) {
+    auto* h = new idol_q8_matrix();
+    h->m.device = device;
+    h->m.n = out;
+    h->m.k = in;
+    h->m.groups = (out + 31) / 32;
+    cudaError_t e = cudaMalloc(&h->m.codes, idol::codes_bytes(out, in));
+    if (e == cudaSuccess) e = cudaMalloc(&h->m.scales, idol::scales_bytes(out, in));
+    if (e != cudaSuccess) {
+        cudaFree(h->m.codes);
+        delete h;
+        return idol::cuda_fail(e, "cudaMalloc (Q8_0 matrix)");
+    }
+    *result = h;
+    return IDOL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* idol_b200_last_error(void) { return idol::g_last_error.c_str(); }
+
+int idol_b200_version(void) { return 100; }
+
+int idol_b200_device_status(int device, unsigned int* flags) {
+    if (!flags) return fail(IDOL_ERR_INVALID, "device_status: flags is NULL");
+    IDOL_CUDA(cudaSetDevice(device));
+    unsigned int v = 0, all = 0;
+    IDOL_CUDA(idol::take_device_error_gemm(&v));
+    all |= v;
+    *flags = all;
+    return IDOL_OK;
+}
+
+int64_t idol_b200_q8_bytes(int out, int in) { return shape_ok(out, in) ? (int64_t)out * (in / 32) * 34 : -1; }
+int64_t idol_b200_q8_codes_bytes(int out, int in) { return shape_ok(out, in) ? idol::codes_bytes(out, in) : -1; }
+int64_t idol_b200_q8_scales_bytes(int out, int in) { return shape_ok(out, in) ? idol::scales_bytes(out, in) : -1; }
+
+int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, void* stream) {
+    if (rows < 0 || cols < 0 || cols % 32) return fail(IDOL_ERR_INVALID, "q8_quantize: cols must be a multiple of 32");
+    if (rows * cols == 0) return IDOL_OK;
+    if (!w || !q8) return fail(IDOL_ERR_INVALID, "q8_quantize: NULL pointer");
+    IDOL_CUDA(idol::launch_q8_quantize(w, rows, cols, static_cast<uint8_t*>(q8), static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q8_repack(const void* q8, int out, int in, void* codes, void* scales, void* stream) {
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_repack: out >= 1 and in a positive multiple of 32");
+    if (!q8 || !codes || !scales) return fail(IDOL_ERR_INVALID, "q8_repack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(codes) % 16 ||
+        reinterpret_cast<uintptr_t>(scales) % 2)
+        return fail(IDOL_ERR_INVALID, "q8_repack: q8 must be 2-byte, codes 16-byte aligned");
+    IDOL_CUDA(idol::launch_q8_repack(static_cast<const uint8_t*>(q8), out, in, static_cast<int8_t*>(codes),
+                                     static_cast<uint16_t*>(scales), static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q8_unpack(const void* codes, const void* scales, int out, int in, void* q8, void* stream) {
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_unpack: out >= 1 and in a positive multiple of 32");
+    if (!q8 || !codes || !scales) return fail(IDOL_ERR_INVALID, "q8_unpack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(codes) % 16)
+        return fail(IDOL_ERR_INVALID, "q8_unpack: q8 must be 2-byte, codes 16-byte aligned");
+    IDOL_CUDA(idol::launch_q8_unpack(static_cast<const int8_t*>(codes), static_cast<const uint16_t*>(scales), out, in,
+                                     static_cast<uint8_t*>(q8), static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q8_dequantize(const void* codes, const void* scales, int out, int in, void* w, int w_dtype,
+                            void* stream) {
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_dequantize: out >= 1 and in a positive multiple of 32");
+    if (!codes || !scales || !w) return fail(IDOL_ERR_INVALID, "q8_dequantize: NULL pointer");
+    if (w_dtype != IDOL_F32 && w_dtype != IDOL_BF16 && w_dtype != IDOL_F16)
+        return fail(IDOL_ERR_UNSUPPORTED, "q8_dequantize: output must be f32, bf16 or f16");
+    IDOL_CUDA(idol::launch_q8_dequant(static_cast<const int8_t*>(codes), static_cast<const uint16_t*>(scales), out, in,
+                                      w, w_dtype, static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q8_upload(const void* q8_host, int64_t nbytes, int out, int in, const float* bias_host, int device,
+                        idol_q8_matrix** matrix) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_upload: matrix is NULL");
+    *matrix = nullptr;
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_upload: out >= 1 and in a positive multiple of 32");
+    if (!q8_host || nbytes != (int64_t)out * (in / 32) * 34)
+        return fail(IDOL_ERR_INVALID, "q8_upload: Q8_0 byte count does not match the shape");
+    IDOL_CUDA(cudaSetDevice(device));
+    idol_q8_matrix* h = nullptr;
+    int rc = alloc_matrix(out, in, device, &h);
+    if (rc != IDOL_OK) return rc;
+    void* staging = nullptr;
+    cudaError_t e = cudaMalloc(&staging, (size_t)nbytes);
+    if (e == cudaSuccess) e = cudaMemcpy(staging, q8_host, (size_t)nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && bias_host) {
+        e = cudaMalloc(&h->m.bias, sizeof(float) * out);
+        if (e == cudaSuccess) e = cudaMemcpy(h->m.bias, bias_host, sizeof(float) * out, cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess)
+        e = idol::launch_q8_repack(static_cast<const uint8_t*>(staging), out, in, h->m.codes, h->m.scales, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(staging);
+    if (e != cudaSuccess) {
+        idol_b200_q8_free(h);
+        return idol::cuda_fail(e, "q8_upload");
+    }
+    *matrix = h;
+    return IDOL_OK;
+}
+
+int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, const float* bias_dev, int device,
+                        void* stream, idol_q8_matrix** matrix) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_import: matrix is NULL");
+    *matrix = nullptr;
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_import: out >= 1 and in a positive multiple of 32");
+    if (!q8_dev || nbytes != (int64_t)out * (in / 32) * 34)
+        return fail(IDOL_ERR_INVALID, "q8_import: Q8_0 byte count does not match the shape");
+    if (reinterpret_cast<uintptr_t>(q8_dev) % 2) return fail(IDOL_ERR_INVALID, "q8_import: q8 must be 2-byte aligned");
+    IDOL_CUDA(cudaSetDevice(device));
+    idol_q8_matrix* h = nullptr;
+    int rc = alloc_matrix(out, in, device, &h);
+    if (rc != IDOL_OK) return rc;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (bias_dev) {
+        e = cudaMalloc(&h->m.bias, sizeof(float) * out);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(h->m.bias, bias_dev, sizeof(float) * out, cudaMemcpyDeviceToDevice, s);
+    }
+    if (e == cudaSuccess)
+        e = idol::launch_q8_repack(static_cast<const uint8_t*>(q8_dev), out, in, h->m.codes, h->m.scales, s);
+    if (e != cudaSuccess) {
+        idol_b200_q8_free(h);
+        return idol::cuda_fail(e, "q8_import");
+    }
+    *matrix = h;
+    return IDOL_OK;
+}
+
+int idol_b200_q8_view(const void* codes, const void* scales, const float* bias_dev, int out, int in, int device,
+                      idol_q8_matrix** matrix) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_view: matrix is NULL");
+    *matrix = nullptr;
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_view: out >= 1 and in a positive multiple of 32");
+    if (!codes || !scales || reinterpret_cast<uintptr_t>(codes) % 16 || reinterpret_cast<uintptr_t>(scales) % 16)
+        return fail(IDOL_ERR_INVALID, "q8_view: codes and scales must be 16-byte aligned device pointers");
+    auto* h = new idol_q8_matrix();
+    h->m.device = device;
+    h->m.n = out;
+    h->m.k = in;
+    h->m.groups = (out + 31) / 32;
+    h->m.codes = static_cast<int8_t*>(const_cast<void*>(codes));
+    h->m.scales = static_cast<uint16_t*>(const_cast<void*>(scales));
+    h->m.bias = const_cast<float*>(bias_dev);
+    h->m.owns = false;
+    *matrix = h;
+    return IDOL_OK;
+}
+
+int idol_b200_q8_free(idol_q8_matrix* matrix) {
+    if (!matrix) return IDOL_OK;
+    if (matrix->m.owns) {
+        cudaSetDevice(matrix->m.device);
+        cudaFree(matrix->m.codes);
+        cudaFree(matrix->m.scales);
+        cudaFree(matrix->m.bias);
+    }
+    delete matrix;
+    return IDOL_OK;
+}
+
+int idol_b200_q8_info(const idol_q8_matrix* matrix, int* out, int* in, int* device, int64_t* device_bytes) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_info: matrix is NULL");
+    if (out) *out = matrix->m.n;
+    if (in) *in = matrix->m.k;
+    if (device) *device = matrix->m.device;
+    if (device_bytes)
+        *device_bytes = idol::codes_bytes(matrix->m.n, matrix->m.k) + idol::scales_bytes(matrix->m.n, matrix->m.k) +
+                        (matrix->m.bias ? 4 * (int64_t)matrix->m.n : 0);
+    return IDOL_OK;
+}
+
+int idol_b200_q8_export(const idol_q8_matrix* matrix, void* q8_dev, int64_t nbytes, void* stream) {
+    if (!matrix || !q8_dev) return fail(IDOL_ERR_INVALID, "q8_export: NULL pointer");
+    if (nbytes != (int64_t)matrix->m.n * (matrix->m.k / 32) * 34)
+        return fail(IDOL_ERR_INVALID, "q8_export: byte count does not match the shape");
+    IDOL_CUDA(cudaSetDevice(matrix->m.device));
+    IDOL_CUDA(idol::launch_q8_unpack(matrix->m.codes, matrix->m.scales, matrix->m.n, matrix->m.k,
+                                     static_cast<uint8_t*>(q8_dev), static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx, int n_offset,
+                      int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
+                      void* stream) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_gemm: matrix is NULL");
+    if (m > 0 && n > 0 && (!x || !y)) return fail(IDOL_ERR_INVALID, "q8_gemm: NULL pointer");
+    IDOL_CUDA(cudaSetDevice(matrix->m.device));
+    idol::GemmCall c = {&matrix->m, x, x_dtype, m, ldx, n_offset, n, residual, ldr, act, flags, y, y_dtype, ldy,
+                        static_cast<cudaStream_t>(stream)};
+    return idol::q8_gemm(c);
+}
+
+}  // extern "C"

@@ -1,0 +1,439 @@
+// q8_gemm.cu - Y[m, n] = X[m, K] . dequant(W)[n, K]^T + bias (+ residual) (-> act) on sm_100a tensor cores.
+//
+// Replaces the reference's src/kernels.cpp:246-296 gemm_quant (CPU) and tools/idol_triton.py:36-126 fused_linear
+// (GPU). The problem is computed transposed, Y^T = W . X^T, so that the dequantized weights are the tcgen05 A operand
+// and can be written straight from registers into tensor memory (TMEM), never touching shared memory as bf16:
+//
+//   producer warp (1 thread) : TMA loads of the X tile [BN tokens x 64 k] (128-byte swizzle) plus bulk copies of the
+//                              tiled int8 codes [128 rows x 64 k] and their fp16 scales, one mbarrier per stage;
+//   dequant warps (4 x 32)   : lane r of warp q owns weight row 32 q + r (= TMEM lane): reads its 64 codes and two
+//                              scales from shared memory, forms bf16(d * q) exactly as the reference GPU path does
+//                              (tools/idol_triton.py:62,83: fp32 product rounded to the activation dtype), and stores
+//                              32 packed columns into the stage's TMEM A buffer with tcgen05.st;
+//   MMA warp (1 thread)      : tcgen05.mma.kind::f16 D[128 x BN] (fp32, TMEM) += A[128 x 16] (TMEM) x B[16 x BN]
+//                              (shared memory descriptor), four per stage, then tcgen05.commit frees the stage;
+//   epilogue (dequant warps) : tcgen05.ld of the accumulator, bias, residual, activation, store.
+//
+// Split-K: with `splits` > 1 the CTAs that share an output tile form a thread-block cluster along z; each reduces its
+// K range into TMEM, parks the partial tile in its own shared memory, and after a cluster barrier every CTA sums a
+// share of the tile's tokens over the cluster through distributed shared memory. No global scratch is used.
+//
+// Every spin-wait is bounded (ptx.cuh mbar_wait); a timeout raises a sticky device error bit and the kernel winds
+// down instead of hanging.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdlib>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace idol {
+
+IDOL_DEVICE_ERROR_READER(take_device_error_gemm)
+
+namespace {
+
+constexpr int kRowsPerTile = 128;   // weight rows (output features) per CTA = TMEM lanes
+constexpr int kStageK = 64;         // k per pipeline stage: two Q8 blocks, one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;       // warp 0 producer, warp 1 MMA / TMEM owner, warps 2-5 dequant + epilogue
+constexpr int kCodeBytesPerStage = kRowsPerTile * kStageK;          // 8192
+constexpr int kScaleBytesPerStage = kRowsPerTile * 2 * 2;           // 512
+
+struct Params {
+    const int8_t* codes;
+    const uint16_t* scales;
+    const float* bias;
+    const void* residual;
+    void* y;
+    int m, n, k, kb, groups;
+    int row_begin;            // first weight row of tile 0 (the window start rounded down to 32)
+    int n_offset, n_count;    // output columns [n_offset, n_offset + n_count)
+    long long ldy, ldr;
+    int act;
+    int bias_after_round;
+    int stages_per_split, stages_total;
+};
+
+template <int BN, int S>
+struct Config {
+    static constexpr int kXBytes = BN * 128;                         // BN rows of 64 bf16
+    static constexpr int kStageBytes = kXBytes + kCodeBytesPerStage + kScaleBytesPerStage;
+    static constexpr int kACol0 = BN < 32 ? 32 : BN;                 // TMEM column of A stage 0 (D at column 0)
+    static constexpr int kColsNeeded = kACol0 + S * 32;
+    static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
+                                     : kColsNeeded <= 256 ? 256 : 512;
+    static constexpr int kBarBytes = 8 * (3 * S + 1) + 16;
+    // At least 80 KB so that no more than two CTAs share an SM: two TMEM allocations of <= 256 columns always fit,
+    // and a CTA never waits in tcgen05.alloc on a neighbour that is itself waiting for its cluster.
+    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kBarBytes;
+    static constexpr int kSmemBytes = kSmemUsed < 80 * 1024 ? 80 * 1024 : kSmemUsed;
+    static_assert(kColsNeeded <= 512, "TMEM budget");
+    static_assert(S * kXBytes >= BN * kRowsPerTile * 4, "split-K partial tile must fit in the X ring");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+};
+
+template <typename OutT>
+__device__ __forceinline__ float out_round(float v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
+    else return __half2float(__float2half_rn(v));
+}
+template <typename OutT>
+__device__ __forceinline__ OutT to_out(float v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __float2bfloat16_rn(v);
+    else return __float2half_rn(v);
+}
+template <typename OutT>
+__device__ __forceinline__ float from_out(OutT v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(v);
+    else return __half2float(v);
+}
+
+__device__ __forceinline__ float activate(float v, int act) {
+    switch (act) {
+        case IDOL_ACT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+        case IDOL_ACT_GELU_TANH: return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+        case IDOL_ACT_SILU: return v / (1.0f + expf(-v));
+        default: return v;
+    }
+}
+
+// Epilogue for one accumulator value: output (token m, weight row `row`).
+template <typename OutT>
+__device__ __forceinline__ void finish(const Params& p, int m, int row, float acc) {
+    if (m >= p.m || row >= p.n || row < p.n_offset || row >= p.n_offset + p.n_count) return;
+    const float b = p.bias ? p.bias[row] : 0.0f;
+    float v = p.bias_after_round ? out_round<OutT>(acc) + b : acc + b;
+    const int col = row - p.n_offset;
+    if (p.residual) v += from_out<OutT>(static_cast<const OutT*>(p.residual)[(long long)m * p.ldr + col]);
+    v = activate(v, p.act);
+    static_cast<OutT*>(p.y)[(long long)m * p.ldy + col] = to_out<OutT>(v);
+}
+
+// 16 signed codes (one uint4) times d, as 8 packed 2-element registers of the operand type.
+template <bool kBF16>
+__device__ __forceinline__ void dequant16(uint4 c, float d, uint32_t* out) {
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float q0 = (float)(int8_t)(w[i] & 0xffu);
+        const float q1 = (float)(int8_t)((w[i] >> 8) & 0xffu);
+        const float q2 = (float)(int8_t)((w[i] >> 16) & 0xffu);
+        const float q3 = (float)(int8_t)(w[i] >> 24);
+        if constexpr (kBF16) {
+            out[2 * i] = pack_bf16x2(d * q0, d * q1);
+            out[2 * i + 1] = pack_bf16x2(d * q2, d * q3);
+        } else {
+            out[2 * i] = pack_f16x2(d * q0, d * q1);
+            out[2 * i + 1] = pack_f16x2(d * q2, d * q3);
+        }
+    }
+}
+
+template <int BN, int S, bool kBF16, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Params p) {
+    using C = Config<BN, S>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // The 128-byte swizzle needs 1024-aligned tiles in the shared address space.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* xs = smem;                                        // S x kXBytes, each 1024-aligned
+    uint8_t* cs = xs + S * C::kXBytes;                         // S x 8192
+    uint8_t* ss = cs + S * kCodeBytesPerStage;                 // S x 512
+    uint64_t* full = reinterpret_cast<uint64_t*>(ss + S * kScaleBytesPerStage);
+    uint64_t* empty = full + S;
+    uint64_t* afull = empty + S;
+    uint64_t* accfull = afull + S;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accfull + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const int row0 = p.row_begin + blockIdx.x * kRowsPerTile;
+    const int g0 = row0 / 32;
+    const int m0 = blockIdx.y * BN;
+    const int split = blockIdx.z;
+    const int ks_begin = split * p.stages_per_split;
+    const int ks_end = min(ks_begin + p.stages_per_split, p.stages_total);
+    const int nks = ks_end - ks_begin;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 128);
+        }
+        mbar_init(accfull, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&xmap);
+            for (int i = 0; i < nks; ++i) {
+                const int s = i % S, u = i / S;
+                if (i >= S && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) break;
+                const int ks = ks_begin + i;
+                const int b0 = ks * 2;
+                const int nb = min(2, p.kb - b0);
+                int valid = 0;
+                for (int q = 0; q < 4; ++q) valid += (g0 + q < p.groups) ? 1 : 0;
+                const uint32_t tx = C::kXBytes + valid * nb * (1024 + 64);
+                mbar_arrive_expect_tx(&full[s], tx);
+                tma_load_2d(xs + s * C::kXBytes, &xmap, ks * kStageK, m0, &full[s]);
+                for (int q = 0; q < 4; ++q) {
+                    const int g = g0 + q;
+                    if (g >= p.groups) continue;
+                    const long long blk = (long long)g * p.kb + b0;
+                    bulk_load(cs + s * kCodeBytesPerStage + q * 2048, p.codes + blk * 1024, nb * 1024, &full[s]);
+                    bulk_load(ss + s * kScaleBytesPerStage + q * 128, p.scales + blk * 32, nb * 64, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc_f16(kRowsPerTile, BN, kBF16);
+            for (int i = 0; i < nks; ++i) {
+                const int s = i % S, u = i / S;
+                if (!mbar_wait(&full[s], u & 1, abort_flag)) break;
+                if (!mbar_wait(&afull[s], u & 1, abort_flag)) break;
+                tc_fence_after();
+                const int ks = ks_begin + i;
+                const int nk16 = (p.kb - ks * 2) >= 2 ? 4 : 2;
+                const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
+                for (int j = 0; j < nk16; ++j) {
+                    const uint32_t a = tmem + C::kACol0 + s * 32 + j * 8;
+                    mma_ts(tmem, a, make_sdesc_sw128(xaddr + j * 32), idesc, (i > 0 || j > 0) ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(accfull);
+        }
+    } else {
+        // Dequant warps: warp w may only touch TMEM lanes [32 (w % 4), 32 (w % 4) + 32).
+        const int q = warp % 4;
+        const bool valid = (g0 + q) < p.groups;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        for (int i = 0; i < nks; ++i) {
+            const int s = i % S, u = i / S;
+            bool got = mbar_wait(&full[s], u & 1, abort_flag);
+            if (got && i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
+            tc_fence_after();
+            const int ks = ks_begin + i;
+            const int nb = min(2, p.kb - ks * 2);
+            uint32_t regs[32];
+            if (valid) {
+                const uint8_t* cbase = cs + s * kCodeBytesPerStage + q * 2048 + lane * 16;
+                const uint16_t* sbase = reinterpret_cast<const uint16_t*>(ss + s * kScaleBytesPerStage + q * 128);
+                const float d0 = __half2float(__ushort_as_half(sbase[lane]));
+                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), d0, regs);
+                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), d0, regs + 8);
+                if (nb == 2) {
+                    const float d1 = __half2float(__ushort_as_half(sbase[32 + lane]));
+                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 1024), d1, regs + 16);
+                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 1536), d1, regs + 24);
+                } else {
+#pragma unroll
+                    for (int j = 16; j < 32; ++j) regs[j] = 0u;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) regs[j] = 0u;
+            }
+            const uint32_t ta = tmem + lane_base + C::kACol0 + s * 32;
+            tmem_st16(ta, *reinterpret_cast<const uint32_t(*)[16]>(regs));
+            tmem_st16(ta + 16, *reinterpret_cast<const uint32_t(*)[16]>(regs + 16));
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&afull[s]);
+        }
+
+        // Epilogue: the accumulator is ready once the last commit lands.
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(accfull, 0, abort_flag));
+        tc_fence_after();
+        const int row = row0 + 32 * q + lane;
+        if (gridDim.z == 1) {
+            if (ok) {
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + lane_base + c0, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) finish<OutT>(p, m0 + c0 + j, row, __uint_as_float(v[j]));
+                }
+            }
+        } else {
+            // Park the partial tile [token][row] in this CTA's X ring (all loads into it have landed).
+            float* red = reinterpret_cast<float*>(xs);
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_base + c0, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) red[(c0 + j) * kRowsPerTile + 32 * q + lane] = ok ? __uint_as_float(v[j]) : 0.0f;
+            }
+        }
+        tc_fence_before();
+    }
+
+    __syncthreads();
+    if (gridDim.z > 1) {
+        cluster_sync();
+        if (warp >= 2) {
+            const int q = warp % 4;
+            const int row = row0 + 32 * q + lane;
+            const uint32_t z = cluster_ctarank();
+            const uint32_t nz = gridDim.z;
+            const uint32_t red_local = smem_u32(xs);
+            for (int t = (int)z; t < BN; t += (int)nz) {
+                const uint32_t off = (uint32_t)((t * kRowsPerTile + 32 * q + lane) * 4);
+                float acc = 0.0f;
+                for (uint32_t rk = 0; rk < nz; ++rk) acc += ld_cluster_f32(map_to_rank(red_local + off, rk));
+                finish<OutT>(p, m0 + t, row, acc);
+            }
+        }
+        cluster_sync();
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+template <int BN, int S, bool kBF16, typename OutT>
+int launch(const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits, cudaStream_t stream) {
+    using C = Config<BN, S>;
+    auto kern = q8_gemm_kernel<BN, S, kBF16, OutT>;
+    static unsigned long long configured = 0;  // one bit per device: the shared-memory opt-in is set once
+    int dev = 0;
+    IDOL_CUDA(cudaGetDevice(&dev));
+    if (!(configured >> (dev & 63) & 1ull)) {
+        IDOL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+        configured |= 1ull << (dev & 63);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles_n, tiles_m, splits);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = splits > 1 ? 1 : 0;
+    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, p));
+    return IDOL_OK;
+}
+
+template <bool kBF16, typename OutT>
+int dispatch(int bn, const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits,
+             cudaStream_t stream) {
+    switch (bn) {
+        case 16: return launch<16, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 32: return launch<32, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 64: return launch<64, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 128: return launch<128, 4, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        default: return launch<256, 4, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+    }
+}
+
+int env_int(const char* name, int fallback) {
+    const char* v = std::getenv(name);
+    return v && *v ? std::atoi(v) : fallback;
+}
+
+}  // namespace
+
+// Token-tile width and split-K factor by M (the strategy choice). IDOL_B200_GEMM_BN and IDOL_B200_GEMM_SPLITS force
+// them for tests and sweeps.
+static void choose_tiles(int device, int64_t m, int tiles_n, int stages_total, int* bn, int* splits) {
+    int b = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+    const int forced_bn = env_int("IDOL_B200_GEMM_BN", 0);
+    if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) b = forced_bn;
+    const int tiles = tiles_n * (int)((m + b - 1) / b);
+    const int per_sm = b == 256 ? 1 : 2;
+    const int slots = num_sms(device) * per_sm;
+    int s = 1;
+    while (s < 8 && tiles * s * 2 <= slots && stages_total >= s * 2 * 2) s *= 2;
+    const int forced_s = env_int("IDOL_B200_GEMM_SPLITS", 0);
+    if (forced_s == 1 || forced_s == 2 || forced_s == 4 || forced_s == 8) s = forced_s;
+    if (s > stages_total) s = 1;
+    *bn = b;
+    *splits = s;
+}
+
+int q8_gemm(const GemmCall& c) {
+    const Q8Matrix& w = *c.w;
+    if (c.m < 0 || c.m > 0x7fffffff) return fail(IDOL_ERR_INVALID, "q8_gemm: m out of range");
+    if (c.n < 0 || c.n_offset < 0 || c.n_offset + c.n > w.n) return fail(IDOL_ERR_INVALID, "q8_gemm: column window");
+    if (c.m == 0 || c.n == 0) return IDOL_OK;
+    if (c.x_dtype != IDOL_BF16 && c.x_dtype != IDOL_F16)
+        return fail(IDOL_ERR_UNSUPPORTED, "q8_gemm: activations must be bf16 or f16");
+    if (c.y_dtype != IDOL_BF16 && c.y_dtype != IDOL_F16 && c.y_dtype != IDOL_F32)
+        return fail(IDOL_ERR_UNSUPPORTED, "q8_gemm: output must be bf16, f16 or f32");
+    if (c.ldx < w.k || (c.ldx * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(c.x) % 16) != 0)
+        return fail(IDOL_ERR_INVALID, "q8_gemm: x must be 16-byte aligned with a row stride that is a multiple of 8");
+    if (c.ldy < c.n || (c.residual && c.ldr < c.n)) return fail(IDOL_ERR_INVALID, "q8_gemm: output row stride");
+    if (c.act < IDOL_ACT_NONE || c.act > IDOL_ACT_SILU) return fail(IDOL_ERR_INVALID, "q8_gemm: activation");
+
+    Params p = {};
+    p.codes = w.codes;
+    p.scales = w.scales;
+    p.bias = w.bias;
+    p.residual = c.residual;
+    p.y = c.y;
+    p.m = (int)c.m;
+    p.n = w.n;
+    p.k = w.k;
+    p.kb = w.k / 32;
+    p.groups = w.groups;
+    p.row_begin = (c.n_offset / 32) * 32;
+    p.n_offset = c.n_offset;
+    p.n_count = c.n;
+    p.ldy = c.ldy;
+    p.ldr = c.ldr;
+    p.act = c.act;
+    p.bias_after_round = (c.flags & IDOL_EPI_BIAS_AFTER_ROUND) ? 1 : 0;
+    p.stages_total = (w.k + kStageK - 1) / kStageK;
+
+    const int tiles_n = (c.n_offset + c.n - p.row_begin + kRowsPerTile - 1) / kRowsPerTile;
+    int bn = 0, splits = 1;
+    choose_tiles(w.device, c.m, tiles_n, p.stages_total, &bn, &splits);
+    p.stages_per_split = (p.stages_total + splits - 1) / splits;
+    splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // every split gets >= 1 stage
+    const int tiles_m = (int)((c.m + bn - 1) / bn);
+    if (tiles_m > 65535) return fail(IDOL_ERR_INVALID, "q8_gemm: m too large for one launch (split the batch)");
+
+    CUtensorMap xmap;
+    const int rc = encode_tmap_2d(&xmap, c.x_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                  c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK, bn,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != IDOL_OK) return rc;
+
+    const bool bf16 = c.x_dtype == IDOL_BF16;
+    if (c.y_dtype == IDOL_F32)
+        return bf16 ? dispatch<true, float>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                    : dispatch<false, float>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+    if (c.y_dtype == IDOL_BF16)
+        return bf16 ? dispatch<true, __nv_bfloat16>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                    : dispatch<false, __nv_bfloat16>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+    return bf16 ? dispatch<true, __half>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                : dispatch<false, __half>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+}
+
+}  // namespace idol

@@ -1,0 +1,226 @@
+"""PyTorch boundary of the Q8_0 linear path: the ``idol_b200::q8_linear`` custom op and drop-in mirrors of the
+reference's ``fused_linear`` (tools/idol_triton.py:94-126) and ``PackedLinear`` / ``enable_fused_packed``
+(tools/idol_packed.py:12-94).
+
+Weights live on the GPU in the tiled layout the kernels stream (codes int8 + fp16 scales, made once from the GGUF
+Q8_0 bytes by the repack kernel). Every call goes to libidol_b200.so through its C-ABI on torch's current stream; if
+the library is missing the call raises, it never falls back to another implementation.
+"""
+from __future__ import annotations
+
+import collections
+import ctypes
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _capi as C
+
+Q8_0_KIND = 8  # tools/idol_triton.py kind code for GGML Q8_0
+_GGML_Q8_0 = 8  # gguf.GGMLQuantizationType.Q8_0 enum value
+
+_DTYPES = {torch.float32: C.F32, torch.float16: C.F16, torch.bfloat16: C.BF16}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+# ------------------------------------------------------------------------------------------------ format kernels
+def q8_bytes(n: int, k: int) -> int:
+    return n * (k // 32) * 34
+
+
+def quantize(w: torch.Tensor) -> torch.Tensor:
+    """fp32 CUDA weights [rows, cols] -> Q8_0 bytes [rows * cols / 32 * 34] (uint8), byte-equal to gguf-py 0.19.0."""
+    if not w.is_cuda or w.dtype != torch.float32 or w.dim() != 2 or w.shape[1] % 32:
+        raise ValueError("quantize: expected a 2-D float32 CUDA tensor with a multiple of 32 columns")
+    w = w.contiguous()
+    out = torch.empty(w.shape[0] * (w.shape[1] // 32) * 34, dtype=torch.uint8, device=w.device)
+    C.check(C.lib().idol_b200_q8_quantize(_ptr(w), w.shape[0], w.shape[1], _ptr(out), _stream(w.device)))
+    return out
+
+
+def repack(packed: torch.Tensor, n: int, k: int):
+    """GGUF Q8_0 bytes (CUDA uint8) -> (codes int8, scales int16 holding fp16 bits) in the tiled device layout."""
+    if not packed.is_cuda or packed.dtype != torch.uint8 or packed.numel() != q8_bytes(n, k):
+        raise ValueError("repack: expected CUDA uint8 Q8_0 bytes of the given shape")
+    packed = packed.contiguous()
+    L = C.lib()
+    codes = torch.empty(L.idol_b200_q8_codes_bytes(n, k), dtype=torch.int8, device=packed.device)
+    scales = torch.empty(L.idol_b200_q8_scales_bytes(n, k) // 2, dtype=torch.int16, device=packed.device)
+    C.check(L.idol_b200_q8_repack(_ptr(packed), n, k, _ptr(codes), _ptr(scales), _stream(packed.device)))
+    return codes, scales
+
+
+def unpack(codes: torch.Tensor, scales: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """Tiled layout -> GGUF Q8_0 bytes, the exact inverse of ``repack``."""
+    out = torch.empty(q8_bytes(n, k), dtype=torch.uint8, device=codes.device)
+    C.check(C.lib().idol_b200_q8_unpack(_ptr(codes), _ptr(scales), n, k, _ptr(out), _stream(codes.device)))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------- the custom op
+_views: "collections.OrderedDict[tuple, int]" = collections.OrderedDict()
+_VIEW_CACHE = 4096
+
+
+def _view(codes, scales, bias, n, k, device_index):
+    """A C-ABI matrix handle over tensors the caller holds (cached; a handle is a few host bytes)."""
+    key = (codes.data_ptr(), scales.data_ptr(), 0 if bias is None else bias.data_ptr(), n, k, device_index)
+    h = _views.get(key)
+    if h is not None:
+        _views.move_to_end(key)
+        return h
+    out = ctypes.c_void_p()
+    C.check(C.lib().idol_b200_q8_view(_ptr(codes), _ptr(scales), _ptr(bias), n, k, device_index, ctypes.byref(out)))
+    _views[key] = out.value
+    if len(_views) > _VIEW_CACHE:
+        _, old = _views.popitem(last=False)
+        C.lib().idol_b200_q8_free(ctypes.c_void_p(old))
+    return out.value
+
+
+def gemm_into(y: torch.Tensor, x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+              bias: Optional[torch.Tensor], n: int, k: int, n_offset: int = 0, n_count: Optional[int] = None,
+              residual: Optional[torch.Tensor] = None, act: int = C.ACT_NONE, flags: int = 0) -> torch.Tensor:
+    """y[m, :n_count] = x . W[n_offset:n_offset+n_count]^T + bias (+ residual) (-> act), written into y (2-D, rows of
+    any stride >= n_count). x: 2-D bf16/f16 CUDA tensor with unit column stride. residual may alias y."""
+    n_count = n - n_offset if n_count is None else n_count
+    h = _view(codes, scales, bias, n, k, x.device.index)
+    ldr = 0 if residual is None else residual.stride(0)
+    C.check(C.lib().idol_b200_q8_gemm(ctypes.c_void_p(h), _ptr(x), _DTYPES[x.dtype], x.shape[0], x.stride(0),
+                                      n_offset, n_count, _ptr(residual), ldr, act, flags, _ptr(y), _DTYPES[y.dtype],
+                                      y.stride(0), _stream(x.device)))
+    return y
+
+
+def _aligned_rows(x2: torch.Tensor) -> torch.Tensor:
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    return x2
+
+
+@torch.library.custom_op("idol_b200::q8_linear", mutates_args=())
+def q8_linear(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, bias: Optional[torch.Tensor], n: int,
+              k: int, act: int = 0, flags: int = 0) -> torch.Tensor:
+    """x [..., k] bf16/f16 -> [..., n] in x's dtype; bias is fp32 [n] or None."""
+    x2 = _aligned_rows(x.reshape(-1, k))
+    y = torch.empty((x2.shape[0], n), dtype=x.dtype, device=x.device)
+    if x2.shape[0]:
+        gemm_into(y, x2, codes, scales, bias, n, k, act=act, flags=flags)
+    return y.reshape(*x.shape[:-1], n)
+
+
+@q8_linear.register_fake
+def _(x, codes, scales, bias, n, k, act=0, flags=0):
+    return x.new_empty((*x.shape[:-1], n))
+
+
+# ------------------------------------------------------------------------------------ fused_linear (drop-in)
+_tiled_cache: "collections.OrderedDict[tuple, tuple]" = collections.OrderedDict()
+
+
+def _tiled_for(packed: torch.Tensor, n: int, k: int):
+    key = (packed.data_ptr(), packed.numel(), packed._version, n, k, packed.device.index)
+    hit = _tiled_cache.get(key)
+    if hit is None:
+        hit = repack(packed, n, k)
+        _tiled_cache[key] = hit
+        if len(_tiled_cache) > 256:
+            _tiled_cache.popitem(last=False)
+    return hit
+
+
+def fused_linear(value, packed, shape, kind, bias=None):
+    """Multiply FP16/BF16 activations by Q8_0 weights on CUDA, with the contract of tools/idol_triton.py:94-126:
+    same argument checks and ValueError messages, output in value's dtype, bias added after the product is rounded to
+    that dtype. GGUF kinds other than Q8_0 (4 = Q4_0, 44 = Q4_K) are not part of this build and raise ValueError."""
+    if (not value.is_cuda or not packed.is_cuda or packed.dtype != torch.uint8
+            or value.device != packed.device or value.dtype not in (torch.float16, torch.bfloat16)
+            or len(shape) != 2 or value.shape[-1] != shape[1] or kind not in (4, 8, 44)):
+        raise ValueError('unsupported fused linear input')
+    if torch.is_grad_enabled() and (value.requires_grad or (bias is not None and bias.requires_grad)):
+        raise ValueError('fused linear supports inference only')
+    n, k = shape
+    group, size = (256, 144) if kind == 44 else (32, 18 if kind == 4 else 34)
+    if n < 1 or k < 1 or k % group or packed.numel() != n * (k // group) * size:
+        raise ValueError('invalid packed linear dimensions')
+    if bias is not None and (bias.shape != (n,) or bias.device != value.device or bias.dtype != value.dtype):
+        raise ValueError('invalid fused linear bias')
+    if kind != Q8_0_KIND:
+        raise ValueError('unsupported fused linear input: only Q8_0 is implemented on sm_100a')
+    codes, scales = _tiled_for(packed, n, k)
+    b32 = None if bias is None else bias.float()
+    return torch.ops.idol_b200.q8_linear(value, codes, scales, b32, n, k, C.ACT_NONE, C.EPI_BIAS_AFTER_ROUND)
+
+
+# ----------------------------------------------------------------------------------- PackedLinear (drop-in)
+class PackedLinear(torch.nn.Module):
+    """Mirror of tools/idol_packed.py:12-82 for Q8_0 matrices: keeps the GGUF bytes as the ``packed`` buffer, and when
+    ``fused`` is set and the input is CUDA fp16/bf16 without grad, runs the sm_100a kernel on a tiled copy made once
+    per device. Unfused calls expand the weights (our dequant kernel on CUDA) and use F.linear, as the reference's
+    expansion path does."""
+
+    def __init__(self, source, bias):
+        super().__init__()
+        self.shape = tuple(reversed([int(s) for s in source.shape]))
+        self.kind = int(source.tensor_type)
+        if len(self.shape) != 2 or self.kind != _GGML_Q8_0:
+            raise ValueError("unsupported packed matrix")
+        import numpy as np
+        self.register_buffer("packed", torch.from_numpy(np.array(source.data, copy=True)).reshape(-1))
+        self.bias = torch.nn.Parameter(bias.detach(), requires_grad=False) if bias is not None else None
+        self.fused = False
+        self._tiled = None
+
+    def _tiles(self):
+        dev = self.packed.device
+        if self._tiled is None or self._tiled[0] != dev or self._tiled[1] != self.packed._version:
+            codes, scales = repack(self.packed, *self.shape)
+            self._tiled = (dev, self.packed._version, codes, scales)
+        return self._tiled[2], self._tiled[3]
+
+    def dequantize(self, dtype):
+        n, k = self.shape
+        if self.packed.is_cuda:
+            codes, scales = self._tiles()
+            return dequantize_tiled(codes, scales, n, k, dtype)
+        blocks = self.packed.reshape(-1, 34)
+        scale = blocks[:, :2].contiguous().view(torch.float16).float()
+        codes = blocks[:, 2:].contiguous().view(torch.int8).float()
+        return (codes * scale).reshape(self.shape).to(dtype)
+
+    def forward(self, value):
+        needs_grad = torch.is_grad_enabled() and (value.requires_grad or
+                                                  (self.bias is not None and self.bias.requires_grad))
+        if self.fused and value.is_cuda and value.dtype in (torch.float16, torch.bfloat16) and not needs_grad:
+            return fused_linear(value, self.packed, self.shape, Q8_0_KIND, self.bias)
+        return F.linear(value, self.dequantize(value.dtype), self.bias)
+
+
+def enable_fused_packed(model):
+    """Enable supported packed layers; return the number configured (tools/idol_packed.py:85-94)."""
+    count = 0
+    for layer in model.modules():
+        if isinstance(layer, PackedLinear):
+            layer.fused = True
+            count += 1
+    return count
+
+
+def dequantize_tiled(codes, scales, n, k, dtype=torch.float32):
+    """Dense [n, k] weights d * q from the tiled layout (fp32 exact; bf16/fp16 rounded from the fp32 product)."""
+    out = torch.empty((n, k), dtype=dtype, device=codes.device)
+    _dequant(codes, scales, n, k, out)
+    return out
+
+
+def _dequant(codes, scales, n, k, out):
+    C.check(C.lib().idol_b200_q8_dequantize(_ptr(codes), _ptr(scales), n, k, _ptr(out), _DTYPES[out.dtype],
+                                            _stream(codes.device)))

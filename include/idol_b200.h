@@ -1,0 +1,122 @@
+/*
+ * idol_b200.h - C ABI of the B200 (sm_100a) Q8_0 linear hot path.
+ *
+ * Plain pointers and sizes only. Every entry point returns IDOL_OK (0) or an IDOL_ERR_* status and never throws or
+ * aborts; idol_b200_last_error() gives the message for the calling thread. Device entry points take device pointers
+ * and a cudaStream_t passed as void* (NULL = the legacy default stream) and are asynchronous with respect to the host,
+ * like the kernels they launch. Host entry points (the *_host names) take host pointers and return when the result is
+ * in host memory.
+ *
+ * Each declaration names the reference interface it replaces (file:line inside TimeLordRaps/idol.cpp).
+ */
+#ifndef IDOL_B200_H
+#define IDOL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define IDOL_OK 0
+#define IDOL_ERR_INVALID 1     /* an argument the format or the kernel cannot take (the reference's std::invalid_argument) */
+#define IDOL_ERR_CUDA 2        /* a CUDA runtime or driver call failed */
+#define IDOL_ERR_UNSUPPORTED 3 /* a dtype or option this build does not implement */
+#define IDOL_ERR_DEVICE 4      /* a kernel reported a bounded wait that ran out (see idol_b200_device_status) */
+
+/* Element types. */
+#define IDOL_F32 0
+#define IDOL_F16 1
+#define IDOL_BF16 2
+
+/* Epilogue activations. */
+#define IDOL_ACT_NONE 0
+#define IDOL_ACT_GELU_ERF 1  /* exact GELU, 0.5 x (1 + erf(x / sqrt 2)): src/kernels.cpp:212-241 finish_tile */
+#define IDOL_ACT_GELU_TANH 2 /* tanh GELU: src/decoders.cpp:55-71 gelu_tanh */
+#define IDOL_ACT_SILU 3      /* x sigmoid(x): src/decoders.cpp:88 silu */
+
+/* Epilogue flags. */
+#define IDOL_EPI_BIAS_AFTER_ROUND 0x1 /* round the product to the output type before adding the bias, as
+                                          tools/idol_triton.py:84-89 does; default adds it in fp32 like finish_tile */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* idol_b200_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int idol_b200_version(void);
+
+/* Reads and clears the sticky device error word of `device` (bit 0: a kernel's bounded wait ran out). */
+int idol_b200_device_status(int device, unsigned int* flags);
+
+/* ------------------------------------------------------------------------------------------------ Q8_0 formats */
+
+/* Bytes of GGUF Q8_0 data for an out x in matrix: out * in / 32 * 34 (tools/idol_triton.py:104). */
+int64_t idol_b200_q8_bytes(int out, int in);
+/* Bytes of the tiled device layout: codes (int8) and scales (fp16) planes. */
+int64_t idol_b200_q8_codes_bytes(int out, int in);
+int64_t idol_b200_q8_scales_bytes(int out, int in);
+
+/* fp32 weights [rows, cols] (device) -> Q8_0 blocks (device), byte-equal to gguf-py 0.19.0 gguf.quantize(W, Q8_0)
+ * (called by tools/export_full_gguf.py:335). cols must be a multiple of 32. */
+int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, void* stream);
+
+/* Q8_0 blocks -> tiled layout (device to device), and the exact inverse. Replaces the GGUF->native conversion
+ * tools/gguf_to_decoder.py:16-40 + tools/idolq.py:137-166 (pack_blob) with a layout the kernels stream coalesced. */
+int idol_b200_q8_repack(const void* q8, int out, int in, void* codes, void* scales, void* stream);
+int idol_b200_q8_unpack(const void* codes, const void* scales, int out, int in, void* q8, void* stream);
+
+/* Tiled layout -> dense out x in weights d * q (w_dtype IDOL_F32 exact; IDOL_BF16 / IDOL_F16 rounded from the fp32
+ * product). Replaces src/kernels.cpp:535-550 dequantize_linear and tools/idol_packed.py:25-31 dequantize. */
+int idol_b200_q8_dequantize(const void* codes, const void* scales, int out, int in, void* w, int w_dtype,
+                            void* stream);
+
+/* ------------------------------------------------------------------------------------------- resident matrices */
+
+/* A Q8_0 weight matrix (plus optional fp32 bias) resident in one GPU's memory in the tiled layout. */
+typedef struct idol_q8_matrix idol_q8_matrix;
+
+/* Uploads host Q8_0 bytes (nbytes == idol_b200_q8_bytes(out, in)) and an optional host fp32 bias[out] to `device`,
+ * once. Replaces src/kernels.cpp:516-533 quantized_linear and the qtensor load of src/weights.cpp:67-80. Returns when
+ * the matrix is ready. */
+int idol_b200_q8_upload(const void* q8_host, int64_t nbytes, int out, int in, const float* bias_host, int device,
+                        idol_q8_matrix** matrix);
+
+/* The same from Q8_0 bytes and an optional fp32 bias already on `device` (PackedLinear.packed,
+ * tools/idol_packed.py:21). Ordered on `stream`. */
+int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, const float* bias_dev, int device,
+                        void* stream, idol_q8_matrix** matrix);
+
+/* A matrix handle over tiled codes/scales (and an optional fp32 bias) that the caller already holds on `device`, e.g.
+ * tensors of a PyTorch module; nothing is allocated on the device and idol_b200_q8_free releases only the handle. */
+int idol_b200_q8_view(const void* codes, const void* scales, const float* bias_dev, int out, int in, int device,
+                      idol_q8_matrix** matrix);
+
+int idol_b200_q8_free(idol_q8_matrix* matrix);
+
+/* Shape and device footprint. */
+int idol_b200_q8_info(const idol_q8_matrix* matrix, int* out, int* in, int* device, int64_t* device_bytes);
+
+/* Writes the matrix back as Q8_0 blocks into q8_dev (device), the bit-exact inverse of the upload. */
+int idol_b200_q8_export(const idol_q8_matrix* matrix, void* q8_dev, int64_t nbytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- the GEMM */
+
+/* y[m, 0:n] = x[m, in] . W[n_offset : n_offset + n]^T + bias (+ residual) (-> act), on the matrix's device.
+ * Replaces src/kernels.cpp:75-76 gemm_packed (window, residual that may alias y, activation after the residual) and
+ * tools/idol_triton.py:94-126 fused_linear.
+ *   x        : device, x_dtype IDOL_BF16 or IDOL_F16, rows ldx elements apart (ldx >= in, ldx % 8 == 0, 16-byte base).
+ *   residual : device, y_dtype, rows ldr apart, or NULL. May alias y.
+ *   y        : device, y_dtype IDOL_BF16, IDOL_F16 or IDOL_F32, rows ldy apart.
+ *   flags    : IDOL_EPI_* bits.
+ * m == 0 or n == 0 is a no-op. */
+int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx, int n_offset,
+                      int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IDOL_B200_H */

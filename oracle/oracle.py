@@ -1,0 +1,265 @@
+"""ctypes front end for the CPU checkers (test infrastructure, never the product).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's ``cpu_baseline`` / ``--impl reference`` legs import this
+module. It wraps two libraries built by ``oracle/Makefile``:
+
+* ``liboracle.so`` - the C restatement of the reference's Q8_0 path (q8_oracle.c; each function cites the reference
+  file:line it follows).
+* ``_ref/libidolref.so`` - the reference's own CPU kernels (src/kernels.cpp, src/weights.cpp, src/decoders.cpp)
+  compiled from the reference tree. Present only where that tree was available at build time; ``have_ref()`` says so.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ACT_NONE, ACT_GELU_ERF, ACT_GELU_TANH, ACT_SILU = 0, 1, 2, 3
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_lib = None
+_ref = None
+
+
+def _ptr(a, kind=_f32p):
+    return None if a is None else a.ctypes.data_as(kind)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = HERE / "liboracle.so"
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing: run `make -C oracle`")
+        L = ctypes.CDLL(str(path))
+        L.orc_q8_quantize.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _u8p]
+        L.orc_q8_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+        L.orc_panel_blob_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.orc_panel_blob_bytes.restype = ctypes.c_int64
+        L.orc_q8_to_panels.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p]
+        L.orc_gemm_q8.argtypes = [_f32p, ctypes.c_int, _u8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, _f32p, ctypes.c_int, _f32p]
+        L.orc_activate.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int]
+        L.orc_norm_rows.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p, _f32p, _f32p,
+                                    _f32p]
+        L.orc_rms_heads.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
+        L.orc_attention.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        L.orc_gaussian_heads.argtypes = [_f32p, ctypes.c_int64, _f32p]
+        L.orc_f32_to_f16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_f16.restype = ctypes.c_uint16
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_f16_to_f32.restype = ctypes.c_float
+        for name in ("orc_gelu_erf", "orc_gelu_tanh", "orc_silu"):
+            getattr(L, name).argtypes = [ctypes.c_float]
+            getattr(L, name).restype = ctypes.c_float
+        _lib = L
+    return _lib
+
+
+def have_ref() -> bool:
+    return (HERE / "_ref" / "libidolref.so").exists()
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        path = HERE / "_ref" / "libidolref.so"
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing: run `make -C oracle ref REF=<reference checkout>`")
+        R = ctypes.CDLL(str(path))
+        R.ref_last_error.restype = ctypes.c_char_p
+        R.ref_set_threads.argtypes = [ctypes.c_int]
+        R.ref_max_threads.restype = ctypes.c_int
+        R.ref_q8_linear_create.argtypes = [_u8p, _f32p, ctypes.c_int, ctypes.c_int]
+        R.ref_q8_linear_create.restype = ctypes.c_void_p
+        R.ref_blob_linear_create.argtypes = [_u8p, ctypes.c_int64, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int]
+        R.ref_blob_linear_create.restype = ctypes.c_void_p
+        R.ref_linear_free.argtypes = [ctypes.c_void_p]
+        R.ref_gemm.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int,
+                               _f32p, ctypes.c_int]
+        R.ref_dequantize.argtypes = [ctypes.c_void_p, _f32p]
+        R.ref_norm_rows.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p, _f32p, _f32p,
+                                    _f32p]
+        R.ref_layer_norm.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p]
+        R.ref_rms_heads.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
+        R.ref_gelu_tanh.argtypes = [_f32p, ctypes.c_int64]
+        R.ref_silu.argtypes = [ctypes.c_float]
+        R.ref_silu.restype = ctypes.c_float
+        R.ref_gelu_scalar.argtypes = [ctypes.c_float]
+        R.ref_gelu_scalar.restype = ctypes.c_float
+        R.ref_attention.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        _ref = R
+    return _ref
+
+
+# ---------------------------------------------------------------------------------------------------- the restatement
+def c32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def q8_quantize(w: np.ndarray) -> np.ndarray:
+    """fp32 [rows, cols] -> Q8_0 bytes [rows, cols/32*34] with gguf-py 0.19.0 semantics."""
+    w = c32(w)
+    rows, cols = w.shape
+    out = np.empty((rows, cols // 32 * 34), np.uint8)
+    lib().orc_q8_quantize(_ptr(w), rows, cols, _ptr(out, _u8p))
+    return out
+
+
+def q8_dequantize(q8: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_q8_dequantize(_ptr(q8, _u8p), rows, cols, _ptr(out))
+    return out
+
+
+def q8_to_panels(q8: np.ndarray, out: int, inp: int) -> np.ndarray:
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    blob = np.empty(lib().orc_panel_blob_bytes(out, inp), np.uint8)
+    rc = lib().orc_q8_to_panels(_ptr(q8, _u8p), out, inp, _ptr(blob, _u8p))
+    if rc != 0:
+        raise ValueError(f"Q8_0 -> panel conversion failed ({rc})")
+    return blob
+
+
+def gemm_q8(a, q8, bias, N, K, n_offset=0, n=None, residual=None, act=ACT_NONE):
+    """C = A . W[n_offset:n_offset+n]^T + bias (+ residual) (-> act), the reference float kernel's summation order."""
+    a = c32(a)
+    m = a.shape[0]
+    n = N - n_offset if n is None else n
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    bias = None if bias is None else c32(bias)
+    residual = None if residual is None else c32(residual)
+    c = np.empty((m, n), np.float32)
+    lib().orc_gemm_q8(_ptr(a), m, _ptr(q8, _u8p), _ptr(bias), N, K, n_offset, n, _ptr(residual), act, _ptr(c))
+    return c
+
+
+def activate(x, act):
+    x = c32(x).copy()
+    lib().orc_activate(_ptr(x), x.size, act)
+    return x
+
+
+def norm_rows(x, eps, gamma=None, beta=None, shift=None, scale=None):
+    x = c32(x)
+    rows, dim = x.shape
+    y = np.empty_like(x)
+    lib().orc_norm_rows(_ptr(x), _ptr(y), rows, dim, eps, _ptr(None if gamma is None else c32(gamma)),
+                        _ptr(None if beta is None else c32(beta)), _ptr(None if shift is None else c32(shift)),
+                        _ptr(None if scale is None else c32(scale)))
+    return y
+
+
+def rms_heads(x, heads, hd, gamma, col0=0, ld=None):
+    """Per-head L2 norm over columns [col0, col0 + heads*hd) of each row; returns a copy."""
+    x = c32(x).copy()
+    rows = x.shape[0]
+    ld = x.shape[1] if ld is None else ld
+    gamma = c32(gamma)
+    base = x.ctypes.data + 4 * col0
+    lib().orc_rms_heads(ctypes.cast(base, _f32p), rows, ld, heads, hd, _ptr(gamma))
+    return x
+
+
+def attention(q, k, v, heads, head_dim):
+    """q [lq, >=dim], k/v [lk, >=dim] (rows of their own strides) -> out [lq, dim]."""
+    q, k, v = c32(q), c32(k), c32(v)
+    dim = heads * head_dim
+    out = np.empty((q.shape[0], dim), np.float32)
+    lib().orc_attention(_ptr(q), q.shape[0], q.shape[1], _ptr(k), _ptr(v), k.shape[0], k.shape[1], heads, head_dim,
+                        _ptr(out), dim)
+    return out
+
+
+def gaussian_heads(raw):
+    raw = c32(raw)
+    out = np.empty_like(raw)
+    lib().orc_gaussian_heads(_ptr(raw), raw.shape[0], _ptr(out))
+    return out
+
+
+def f32_to_bf16_round(x):
+    """fp32 values rounded to bf16 (round to nearest even), returned as fp32."""
+    x = c32(x)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+# ------------------------------------------------------------------------------------------- composed block oracles
+def block_forward(x, layers, heads, eps=1e-6, images=1):
+    """The denoiser-style block of the scope table (src/decoders.cpp:296-313 without the cross-attention):
+    LN -> QKV -> rms q,k -> self-attention per image -> out + res -> LN -> ff1 -> gelu_tanh -> ff2 + res.
+    x: [images * L, D] fp32; layers: dict of (q8, bias, N, K) for qkv/out/ff1/ff2 plus q_gamma/k_gamma."""
+    x = c32(x)
+    rows, D = x.shape
+    hd = D // heads
+    L = rows // images
+    h = norm_rows(x, eps)
+    qkv = gemm_q8(h, *layers["qkv"])
+    qkv = rms_heads(qkv, heads, hd, layers["q_gamma"], col0=0)
+    qkv = rms_heads(qkv, heads, hd, layers["k_gamma"], col0=D)
+    a = np.empty((rows, D), np.float32)
+    for i in range(images):
+        blk = qkv[i * L:(i + 1) * L]
+        a[i * L:(i + 1) * L] = attention(blk[:, :D], np.ascontiguousarray(blk[:, D:2 * D]),
+                                         np.ascontiguousarray(blk[:, 2 * D:]), heads, hd)
+    x = gemm_q8(a, *layers["out"], residual=x)
+    h = norm_rows(x, eps)
+    f = gemm_q8(h, *layers["ff1"], act=ACT_GELU_TANH)
+    x = gemm_q8(f, *layers["ff2"], residual=x)
+    return x
+
+
+def gaussian_mlp(x, layers):
+    """Synthetic Gaussian MLP: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the activated heads."""
+    h = gemm_q8(x, *layers[0], act=ACT_SILU)
+    h = gemm_q8(h, *layers[1], act=ACT_SILU)
+    raw = gemm_q8(h, *layers[2])
+    return raw, gaussian_heads(raw)
+
+
+# --------------------------------------------------------------------------------------- the reference, as compiled
+class RefLinear:
+    """The reference's own PackedLinear built from Q8_0 blocks (tools/gguf_to_decoder.py -> quantized_linear)."""
+
+    def __init__(self, q8, bias, out, inp):
+        self.q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+        self.bias = c32(bias if bias is not None else np.zeros(out, np.float32))
+        self.out, self.inp = out, inp
+        self.h = ref().ref_q8_linear_create(_ptr(self.q8, _u8p), _ptr(self.bias), out, inp)
+        if not self.h:
+            raise ValueError(ref().ref_last_error().decode())
+
+    def gemm(self, a, n_offset=0, n=None, residual=None, gelu=False, mode=0):
+        a = c32(a)
+        n = self.out - n_offset if n is None else n
+        c = np.empty((a.shape[0], n), np.float32)
+        ref().ref_gemm(self.h, _ptr(a), a.shape[0], n_offset, n, _ptr(None if residual is None else c32(residual)),
+                       int(gelu), _ptr(c), mode)
+        return c
+
+    def dequantize(self):
+        w = np.empty((self.out, self.inp), np.float32)
+        ref().ref_dequantize(self.h, _ptr(w))
+        return w
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().ref_linear_free(self.h)
+            self.h = None
+
+
+def ref_threads(n=None):
+    if n is None:
+        n = os.cpu_count() or 1
+    ref().ref_set_threads(int(n))
+    return int(n)
