@@ -86,14 +86,13 @@ __global__ void q8_quantize_kernel(const float* __restrict__ w, int64_t blocks, 
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
     const float q = round_half_away(__fmul_rn(x, id));
-    uint8_t* dst = out + blk * 34;
-    dst[2 + lane] = (uint8_t)(int8_t)(int)q;
-    if (lane == 0) {
-        const __half dh = __float2half_rn(d);
-        const uint16_t bits = __half_as_ushort(dh);
-        dst[0] = (uint8_t)(bits & 0xffu);
-        dst[1] = (uint8_t)(bits >> 8);
-    }
+    // The block is 17 halfwords (it starts on a 2-byte boundary): halfword 0 is the fp16 scale, halfword 1 + i holds
+    // codes 2 i and 2 i + 1. Even lanes pair their code with the next lane's and store one halfword each.
+    const uint32_t code = (uint32_t)(uint8_t)(int8_t)(int)q;
+    const uint32_t next = __shfl_down_sync(0xffffffffu, code, 1);
+    uint16_t* dst = reinterpret_cast<uint16_t*>(out + blk * 34);
+    if ((lane & 1) == 0) dst[1 + lane / 2] = (uint16_t)(code | (next << 8));
+    if (lane == 1) dst[0] = __half_as_ushort(__float2half_rn(d));
 }
 
 // Tiled layout -> dense [n, k] weights d * q in fp32, bf16 or fp16 (bf16/fp16 rounded from the exact fp32 product).
