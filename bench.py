@@ -1,0 +1,406 @@
+"""Benchmark of the Q8_0 linear hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the Q8_0 GEMM shape sweep): one step = one pass over the 18 GEMMs
+M in {1, 16, 128, 1024, 4096, 16384} x (K, N) in {(1024, 3072), (1024, 4096), (4096, 1024)}: bf16 activations ~N(0,1),
+weights ~N(0,0.02) quantized to Q8_0 on the device, fp32 accumulation, bf16 out, seeded synthetic data. Every GEMM of
+a step has its own weights and activations; a step streams ~1.3 GB, so no operand is still in the 126 MB L2 when it
+is used again one step later.
+
+value      : whole-job TFLOP/s = sum over ranks of 2 M N K per step x K steps / max-over-ranks device time, with all
+             operands resident in HBM (the K steps replay a CUDA graph of the 18 launches; timed by CUDA events).
+e2e        : the same metric through the drop-in API (fused_linear over GGUF Q8_0 bytes) with each step's activations
+             copied host->device from pinned memory and its outputs copied back inside the timed region.
+roofline   : the GEMM kernel on the tensor-bound shapes (M >= 4096): 2 M N K per launch / CUDA-event duration, against
+             the measured dense bf16 peak; roofline_small_m: the HBM-bound shapes (M <= 16), algorithmic bytes
+             1.0625 N K + 2 M K + 2 M N + 4 N per launch against the measured HBM bandwidth.
+cpu_baseline: the reference's own CPU kernel (src/kernels.cpp gemm_packed, float kernel, OpenMP, compiled into
+             oracle/_ref) on a bounded sample (M capped at 256 rows per shape), rank 0 at N=1.
+--impl reference: that CPU kernel alone, as the reference arm (rank 0 only under torchrun).
+N > 1: one process per GPU (torchrun), each GPU runs the full sweep on its own data; the path shards by request with
+no collective ("weak" scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+MS = (1, 16, 128, 1024, 4096, 16384)
+KNS = ((1024, 3072), (1024, 4096), (4096, 1024))
+METRIC = "Q8_0 GEMM TFLOP/s (config 2 shape sweep)"
+UNIT = "TFLOP/s"
+
+
+def shapes():
+    return [(m, k, n) for (k, n) in KNS for m in MS]
+
+
+def flops(m, k, n):
+    return 2.0 * m * n * k
+
+
+def alg_bytes(m, k, n):
+    return 1.0625 * n * k + 2.0 * m * k + 2.0 * m * n + 4.0 * n
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------------ CPU (reference)
+def cpu_reference_sample(seconds=12.0, m_cap=256):
+    """The reference's gemm_packed float kernel over the sweep with M capped at m_cap rows; returns (TFLOP/s, cores,
+    kind, sample description)."""
+    from oracle import oracle as O
+    kind = "reference" if O.have_ref() else "port"
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    cases = []
+    for (m, k, n) in shapes():
+        mm = min(m, m_cap)
+        q8 = O.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+        x = O.f32_to_bf16_round(rng.normal(0, 1, (mm, k)).astype(np.float32))
+        b = np.zeros(n, np.float32)
+        cases.append((mm, k, n, q8, x, b))
+    if kind == "reference":
+        O.ref_threads(cores)
+        lins = [O.RefLinear(q8, b, n, k) for (mm, k, n, q8, x, b) in cases]
+        run = lambda i: lins[i].gemm(cases[i][4], mode=0)  # noqa: E731
+    else:
+        cores = 1
+        run = lambda i: O.gemm_q8(cases[i][4], cases[i][3], cases[i][5], cases[i][2], cases[i][1])  # noqa: E731
+    for i in range(len(cases)):  # warm-up pass
+        run(i)
+    total_flops, passes, t0 = 0.0, 0, time.perf_counter()
+    while True:
+        for i, (mm, k, n, *_) in enumerate(cases):
+            run(i)
+            total_flops += flops(mm, k, n)
+        passes += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{passes} passes of the 18-shape sweep with M capped at {m_cap} rows "
+              f"({total_flops / passes / 1e9:.1f} GFLOP per pass), {'OpenMP' if kind == 'reference' else 'scalar'}")
+    return total_flops / dt / 1e12, cores, kind, sample
+
+
+# ------------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, gpus):
+        self.path = Path(tempfile.mkstemp(prefix="clocks_", suffix=".csv")[1])
+        self.gpus = gpus
+        self.proc = None
+
+    def start(self):
+        q = ("index,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.t_start = time.time()
+
+    def mark(self):
+        return time.time()
+
+    def stop(self, t0, t1):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+                ts = time.mktime(time.strptime(parts[1].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                rows.append((idx, ts, float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        rows = [r for r in rows if r[0] in self.gpus]
+        inside = [r for r in rows if t0 - 1.0 <= r[1] <= t1 + 1.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v.lower() == "active"})
+        self.path.unlink(missing_ok=True)
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(r[2] for r in inside), "sm_max_mhz": max(r[3] for r in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ------------------------------------------------------------------------------------------------------ ours
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm_peak, tc_peak, peak_kind = peaks()
+
+    # Operands: one weight matrix and one activation batch per GEMM, resident in HBM.
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    ops = []
+    for (m, k, n) in shapes():
+        w = torch.randn((n, k), device=dev, generator=g) * 0.02
+        packed = pkg.quantize(w)
+        codes, scales = pkg.repack(packed, n, k)
+        del w
+        x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
+        bias = (torch.randn(n, device=dev, generator=g) * 0.01)
+        y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+        ops.append(dict(m=m, k=k, n=n, packed=packed, codes=codes, scales=scales, x=x, bias=bias, y=y,
+                        bias_bf16=bias.to(torch.bfloat16)))
+    step_flops = sum(flops(o["m"], o["k"], o["n"]) for o in ops)
+    stream = torch.cuda.Stream(device=dev)
+
+    def launch_step():
+        for o in ops:
+            pkg.gemm_into(o["y"], o["x"], o["codes"], o["scales"], o["bias"], o["n"], o["k"])
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            launch_step()
+    stream.synchronize()
+    assert pkg._capi.device_status(local_rank) == 0
+
+    # Region A (value): a CUDA graph of G whole steps, replayed; timed by events outside the graph.
+    G = min(10, args.steps)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(G):
+                launch_step()
+    rest = args.steps % G
+    graph_rest = None
+    if rest:
+        graph_rest = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph_rest, stream=stream):
+                for _ in range(rest):
+                    launch_step()
+    with torch.cuda.stream(stream):
+        graph.replay()  # warm the graph itself (not timed)
+    stream.synchronize()
+    assert pkg._capi.device_status(local_rank) == 0
+
+    clocks = ClockSampler([local_rank] if world == 1 else list(range(world)))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.5)
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        t_begin.record(stream)
+        for _ in range(args.steps // G):
+            graph.replay()
+        if graph_rest is not None:
+            graph_rest.replay()
+        t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    wall1 = time.time()
+    ms = t_begin.elapsed_time(t_end)
+    status = pkg._capi.device_status(local_rank)
+
+    # Region B (per-launch durations for the roofline): per shape, a graph of R back-to-back launches over R distinct
+    # copies of its operands (R copies total > 256 MB, so each launch reads its operands from HBM), timed by events.
+    mean_ms = []
+    reps = []
+    for o in ops:
+        per_copy = o["codes"].numel() + o["scales"].numel() * 2 + o["x"].numel() * 2
+        R = int(min(32, max(2, -(-256e6 // per_copy))))
+        copies = []
+        for _ in range(R):
+            copies.append((o["codes"].clone(), o["scales"].clone(), o["x"].clone(), torch.empty_like(o["y"])))
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for (c_, s_, x_, y_) in copies[:1]:
+                pkg.gemm_into(y_, x_, c_, s_, o["bias"], o["n"], o["k"])
+            with torch.cuda.graph(gs, stream=stream):
+                for (c_, s_, x_, y_) in copies:
+                    pkg.gemm_into(y_, x_, c_, s_, o["bias"], o["n"], o["k"])
+            gs.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(3):
+                gs.replay()
+            e1.record(stream)
+        stream.synchronize()
+        mean_ms.append(e0.elapsed_time(e1) / (3 * R))
+        reps.append(R)
+        del copies, gs
+    torch.cuda.empty_cache()
+
+    # e2e through the drop-in API with host buffers
+    host_x = [o["x"].cpu().pin_memory() for o in ops]
+    host_y = [torch.empty(o["y"].shape, dtype=o["y"].dtype).pin_memory() for o in ops]
+    dev_x = [torch.empty_like(o["x"]) for o in ops]
+    e2e_steps = max(1, min(args.steps, 10))
+    fused = pkg.fused_linear
+    with torch.cuda.stream(stream):
+        for i, o in enumerate(ops):  # warm: builds the tiled copies fused_linear caches
+            fused(o["x"], o["packed"], (o["n"], o["k"]), 8, o["bias_bf16"])
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            for i, o in enumerate(ops):
+                dev_x[i].copy_(host_x[i], non_blocking=True)
+                out = fused(dev_x[i], o["packed"], (o["n"], o["k"]), 8, o["bias_bf16"])
+                host_y[i].copy_(out, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = sum(t.numel() * t.element_size() for t in host_x)
+    d2h = sum(t.numel() * t.element_size() for t in host_y)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, float(status)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, status = float(t[0]), float(t[1]), int(t[2])
+    clk = clocks.stop(wall0, wall1) if rank == 0 else None
+    if rank != 0:
+        return
+
+    value = step_flops * args.steps * world / (ms / 1e3) / 1e12
+    e2e_value = step_flops * e2e_steps * world / (e2e_ms / 1e3) / 1e12
+    shape_rows = []
+    for i, o in enumerate(ops):
+        t = mean_ms[i] / 1e3
+        tf = flops(o["m"], o["k"], o["n"]) / t / 1e12
+        gb = alg_bytes(o["m"], o["k"], o["n"]) / t / 1e9
+        shape_rows.append({"M": o["m"], "K": o["k"], "N": o["n"], "copies": reps[i], "us": round(mean_ms[i] * 1e3, 2),
+                           "tflops": round(tf, 1), "gbs": round(gb, 1), "frac_tensor": round(tf / tc_peak, 3),
+                           "frac_hbm": round(gb / hbm_peak, 3)})
+    big = [i for i, o in enumerate(ops) if o["m"] >= 4096]
+    small = [i for i, o in enumerate(ops) if o["m"] <= 16]
+    ach_t = sum(flops(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in big) / (sum(mean_ms[i] for i in big) / 1e3) / 1e12
+    ach_b = sum(alg_bytes(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in small) / (
+        sum(mean_ms[i] for i in small) / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "q8_gemm_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_tensor_bound")
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
+        "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
+                   "operands": "resident in HBM", "l2": "each operand used once per step; a step streams "
+                   f"{sum(o['x'].numel() * 2 + o['codes'].numel() + o['y'].numel() * 2 for o in ops) / 1e9:.2f} GB "
+                   "> 126 MB L2", "timing": f"CUDA graph of {G} steps replayed; CUDA events",
+                   "per_launch_timing": "per shape, a CUDA graph of R launches over R operand copies (> 256 MB in "
+                   "total) replayed 3 times between CUDA events; R per shape in shapes[].copies",
+                   "parallelism": f"replicas x{world} (shard by request, no collective)"},
+        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "fused_linear(value, packed, shape, 8, bias) on host-pinned inputs"},
+        "roofline": {"bound": "tensor", "achieved": round(ach_t, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(ach_t / tc_peak, 3), "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16 burst", "launches": "M in {4096, 16384}"},
+        "roofline_small_m": {"bound": "hbm", "achieved": round(ach_b, 1), "peak": hbm_peak, "unit": "GB/s",
+                             "frac": round(ach_b / hbm_peak, 3), "peak_source": f"{peak_kind} copy",
+                             "launches": "M in {1, 16}"},
+        "shapes": shape_rows,
+        "gpu_launches": len(ops) * args.steps,
+        "device_status": status,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, sample = cpu_reference_sample()
+        line["cpu_baseline"] = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    seconds_per_step = 2.0
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference_sample(seconds=0.5)
+    for _ in range(args.steps):
+        v, cores, kind, sample = cpu_reference_sample(seconds=seconds_per_step)
+        vals.append(v)
+    v = statistics.median(vals)
+    print(json.dumps({
+        "metric": METRIC, "value": round(v, 4), "unit": UNIT, "impl": "reference", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
+        "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
+                   "sample": f"M capped at 256 rows per shape, {seconds_per_step:.0f} s of CPU work per step"},
+        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
