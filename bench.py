@@ -349,6 +349,33 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_shape(args):
+    """One GEMM shape, launched warmup + steps times back to back: the small case an ncu capture targets."""
+    import torch
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    m, k, n = (int(v) for v in args.profile_shape.split(","))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    packed = pkg.quantize(torch.randn((n, k), device=dev, generator=g) * 0.02)
+    codes, scales = pkg.repack(packed, n, k)
+    x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
+    bias = torch.randn(n, device=dev, generator=g) * 0.01
+    y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    for _ in range(args.warmup):
+        pkg.gemm_into(y, x, codes, scales, bias, n, k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        pkg.gemm_into(y, x, codes, scales, bias, n, k)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"profile_shape": [m, k, n], "us_per_launch": round(us, 2),
+                      "tflops": round(flops(m, k, n) / us / 1e6, 1), "device_status": pkg._capi.device_status(0)}))
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -378,6 +405,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-shape", default=None,
+                    help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -386,6 +415,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile_shape:
+        run_profile_shape(args)
         return
     if world > 1:
         import datetime

@@ -37,7 +37,8 @@ namespace {
 
 constexpr int kRowsPerTile = 128;   // weight rows (output features) per CTA = TMEM lanes
 constexpr int kStageK = 64;         // k per pipeline stage: two Q8 blocks, one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;       // warp 0 producer, warp 1 MMA / TMEM owner, warps 2-5 dequant + epilogue
+constexpr int kDequantWarps = 8;    // two per TMEM lane quarter: one per Q8 block of a stage
+constexpr int kThreads = 64 + 32 * kDequantWarps;  // warp 0 producer, warp 1 MMA / TMEM owner, warps 2-9 dequant
 constexpr int kCodeBytesPerStage = kRowsPerTile * kStageK;          // 8192
 constexpr int kScaleBytesPerStage = kRowsPerTile * 2 * 2;           // 512
 
@@ -115,22 +116,53 @@ __device__ __forceinline__ void finish(const Params& p, int m, int row, float ac
 }
 
 // 16 signed codes (one uint4) times d, as 8 packed 2-element registers of the operand type.
+// Exact dequantisation in three steps: PRMT places the byte u = q + 128 into the mantissa of 32768, giving
+// f = 32896 + q exactly; one packed FMA forms f d - 32896 d = q d with a single rounding, which is exact because q d
+// has at most 19 significant bits and 32896 d = 2^7 (2^8 + 1) d at most 20; the pair is then rounded to the operand
+// type (round to nearest even), which is what tools/idol_triton.py:62,83 does to the fp32 product d * q.
 template <bool kBF16>
-__device__ __forceinline__ void dequant16(uint4 c, float d, uint32_t* out) {
-    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+__device__ __forceinline__ void dequant16(uint4 c, float2 dd, float2 ncd, uint32_t* out) {
+    const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float q0 = (float)(int8_t)(w[i] & 0xffu);
-        const float q1 = (float)(int8_t)((w[i] >> 8) & 0xffu);
-        const float q2 = (float)(int8_t)((w[i] >> 16) & 0xffu);
-        const float q3 = (float)(int8_t)(w[i] >> 24);
+        const float f0 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7504));
+        const float f1 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7514));
+        const float f2 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7524));
+        const float f3 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7534));
+        const float2 p01 = __ffma2_rn(make_float2(f0, f1), dd, ncd);
+        const float2 p23 = __ffma2_rn(make_float2(f2, f3), dd, ncd);
         if constexpr (kBF16) {
-            out[2 * i] = pack_bf16x2(d * q0, d * q1);
-            out[2 * i + 1] = pack_bf16x2(d * q2, d * q3);
+            out[2 * i] = pack_bf16x2(p01.x, p01.y);
+            out[2 * i + 1] = pack_bf16x2(p23.x, p23.y);
         } else {
-            out[2 * i] = pack_f16x2(d * q0, d * q1);
-            out[2 * i + 1] = pack_f16x2(d * q2, d * q3);
+            out[2 * i] = pack_f16x2(p01.x, p01.y);
+            out[2 * i + 1] = pack_f16x2(p23.x, p23.y);
         }
+    }
+}
+
+// Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row.
+template <typename OutT, int kCols>
+__device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
+                                            bool row_ok) {
+    if (!row_ok) return;
+    const int col = row - p.n_offset;
+    OutT* y = static_cast<OutT*>(p.y) + col;
+    const OutT* res = static_cast<const OutT*>(p.residual);
+    const bool fast = !p.residual && p.act == IDOL_ACT_NONE && !p.bias_after_round && m + kCols <= p.m;
+    if (fast) {
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) y[(long long)(m + j) * p.ldy] = to_out<OutT>(__uint_as_float(v[j]) + bias);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+        if (m + j >= p.m) break;
+        const float acc = __uint_as_float(v[j]);
+        float x = p.bias_after_round ? out_round<OutT>(acc) + bias : acc + bias;
+        if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
+        x = activate(x, p.act);
+        y[(long long)(m + j) * p.ldy] = to_out<OutT>(x);
     }
 }
 
@@ -163,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 128);
+            mbar_init(&afull[s], 32 * kDequantWarps);
         }
         mbar_init(accfull, 1);
         *abort_flag = 0;
@@ -221,8 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             mma_commit(accfull);
         }
     } else {
-        // Dequant warps: warp w may only touch TMEM lanes [32 (w % 4), 32 (w % 4) + 32).
+        // Dequant warps: warp w may only touch TMEM lanes [32 (w % 4), 32 (w % 4) + 32); warps 2-5 take the stage's
+        // first Q8 block, warps 6-9 its second.
         const int q = warp % 4;
+        const int half = (warp - 2) / 4;
         const bool valid = (g0 + q) < p.groups;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         for (int i = 0; i < nks; ++i) {
@@ -232,57 +266,55 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
             tc_fence_after();
             const int ks = ks_begin + i;
-            const int nb = min(2, p.kb - ks * 2);
-            uint32_t regs[32];
-            if (valid) {
-                const uint8_t* cbase = cs + s * kCodeBytesPerStage + q * 2048 + lane * 16;
+            const bool present = half < min(2, p.kb - ks * 2);
+            uint32_t regs[16];
+            if (valid && present) {
+                const uint8_t* cbase = cs + s * kCodeBytesPerStage + q * 2048 + half * 1024 + lane * 16;
                 const uint16_t* sbase = reinterpret_cast<const uint16_t*>(ss + s * kScaleBytesPerStage + q * 128);
-                const float d0 = __half2float(__ushort_as_half(sbase[lane]));
-                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), d0, regs);
-                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), d0, regs + 8);
-                if (nb == 2) {
-                    const float d1 = __half2float(__ushort_as_half(sbase[32 + lane]));
-                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 1024), d1, regs + 16);
-                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 1536), d1, regs + 24);
-                } else {
-#pragma unroll
-                    for (int j = 16; j < 32; ++j) regs[j] = 0u;
-                }
+                const float d = __half2float(__ushort_as_half(sbase[half * 32 + lane]));
+                const float2 dd = make_float2(d, d);
+                const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
+                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs);
+                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 8);
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) regs[j] = 0u;
+                for (int j = 0; j < 16; ++j) regs[j] = 0u;
             }
-            const uint32_t ta = tmem + lane_base + C::kACol0 + s * 32;
-            tmem_st16(ta, *reinterpret_cast<const uint32_t(*)[16]>(regs));
-            tmem_st16(ta + 16, *reinterpret_cast<const uint32_t(*)[16]>(regs + 16));
+            tmem_st16(tmem + lane_base + C::kACol0 + s * 32 + half * 16, *reinterpret_cast<const uint32_t(*)[16]>(regs));
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&afull[s]);
         }
 
-        // Epilogue: the accumulator is ready once the last commit lands.
+        // Epilogue: the accumulator is ready once the last commit lands. Warp half h covers tokens
+        // [h BN / 2, (h + 1) BN / 2) of its 32 rows.
         const bool ok = __all_sync(0xffffffffu, mbar_wait(accfull, 0, abort_flag));
         tc_fence_after();
         const int row = row0 + 32 * q + lane;
+        constexpr int kHalf = BN / 2;
+        constexpr int kChunk = kHalf >= 16 ? 16 : 8;
+        const int c_begin = half * kHalf;
         if (gridDim.z == 1) {
-            if (ok) {
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + lane_base + c0, v);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) finish<OutT>(p, m0 + c0 + j, row, __uint_as_float(v[j]));
-                }
+            const bool row_ok = ok && row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
+            const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
+            for (int c0 = c_begin; c0 < c_begin + kHalf && m0 + c0 < p.m; c0 += kChunk) {
+                uint32_t v[kChunk];
+                if constexpr (kChunk == 16) tmem_ld16(tmem + lane_base + c0, v);
+                else tmem_ld8(tmem + lane_base + c0, v);
+                tmem_ld_wait();
+                finish_cols<OutT, kChunk>(p, m0 + c0, row, v, bias, row_ok);
             }
         } else {
             // Park the partial tile [token][row] in this CTA's X ring (all loads into it have landed).
             float* red = reinterpret_cast<float*>(xs);
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + lane_base + c0, v);
+            for (int c0 = c_begin; c0 < c_begin + kHalf; c0 += kChunk) {
+                uint32_t v[kChunk];
+                if constexpr (kChunk == 16) tmem_ld16(tmem + lane_base + c0, v);
+                else tmem_ld8(tmem + lane_base + c0, v);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) red[(c0 + j) * kRowsPerTile + 32 * q + lane] = ok ? __uint_as_float(v[j]) : 0.0f;
+                for (int j = 0; j < kChunk; ++j)
+                    red[(c0 + j) * kRowsPerTile + 32 * q + lane] = ok ? __uint_as_float(v[j]) : 0.0f;
             }
         }
         tc_fence_before();
@@ -293,11 +325,12 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         cluster_sync();
         if (warp >= 2) {
             const int q = warp % 4;
+            const int half = (warp - 2) / 4;
             const int row = row0 + 32 * q + lane;
             const uint32_t z = cluster_ctarank();
             const uint32_t nz = gridDim.z;
             const uint32_t red_local = smem_u32(xs);
-            for (int t = (int)z; t < BN; t += (int)nz) {
+            for (int t = (int)z + half * (int)nz; t < BN; t += 2 * (int)nz) {
                 const uint32_t off = (uint32_t)((t * kRowsPerTile + 32 * q + lane) * 4);
                 float acc = 0.0f;
                 for (uint32_t rk = 0; rk < nz; ++rk) acc += ld_cluster_f32(map_to_rank(red_local + off, rk));
