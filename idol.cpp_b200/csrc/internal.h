@@ -7,7 +7,7 @@
 
 #include <string>
 
-#include "../../include/idol_b200.h"
+#include "idol_b200.h"  // include/ (on the compiler include path)
 
 namespace idol {
 
