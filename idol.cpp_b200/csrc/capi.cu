@@ -55,6 +55,18 @@ int num_sms(int device) {
     return g_sms[device];
 }
 
+int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(IDOL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(IDOL_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return IDOL_OK;
+}
+
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
@@ -112,6 +124,8 @@ int idol_b200_device_status(int device, unsigned int* flags) {
     IDOL_CUDA(cudaSetDevice(device));
     unsigned int v = 0, all = 0;
     IDOL_CUDA(idol::take_device_error_gemm(&v));
+    all |= v;
+    IDOL_CUDA(idol::take_device_error_attention(&v));
     all |= v;
     *flags = all;
     return IDOL_OK;
@@ -281,6 +295,44 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
     idol::GemmCall c = {&matrix->m, x, x_dtype, m, ldx, n_offset, n, residual, ldr, act, flags, y, y_dtype, ldy,
                         static_cast<cudaStream_t>(stream)};
     return idol::q8_gemm(c);
+}
+
+int idol_b200_norm_rows(const void* x, int x_dtype, int64_t rows, int dim, int64_t ldx, float eps, const float* gamma,
+                        const float* beta, const float* shift, const float* scale, void* y, int y_dtype, int64_t ldy,
+                        void* stream) {
+    if (rows < 0) return fail(IDOL_ERR_INVALID, "norm_rows: rows < 0");
+    if (!idol::norm_dim_ok(dim)) return fail(IDOL_ERR_UNSUPPORTED, "norm_rows: dim must be 256, 512, 768, 1024, 1536 or 2048");
+    if (rows == 0) return IDOL_OK;
+    if (!x || !y || (gamma && !beta) || (!gamma && beta) || (shift && !scale) || (!shift && scale))
+        return fail(IDOL_ERR_INVALID, "norm_rows: NULL pointer (gamma/beta and shift/scale come in pairs)");
+    const int xs = x_dtype == IDOL_F32 ? 4 : 2, ys = y_dtype == IDOL_F32 ? 4 : 2;
+    if (ldx < dim || ldy < dim || (ldx * xs) % 16 || (ldy * ys) % 16 || reinterpret_cast<uintptr_t>(x) % 16 ||
+        reinterpret_cast<uintptr_t>(y) % 16)
+        return fail(IDOL_ERR_INVALID, "norm_rows: rows must be 16-byte aligned");
+    const cudaError_t e = idol::launch_norm_rows(x, x_dtype, ldx, y, y_dtype, ldy, rows, dim, eps, gamma, beta, shift,
+                                                 scale, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue) return fail(IDOL_ERR_UNSUPPORTED, "norm_rows: dtype pair not implemented");
+    IDOL_CUDA(e);
+    return IDOL_OK;
+}
+
+int idol_b200_rms_heads(void* x, int dtype, int64_t rows, int64_t ld, int heads, int head_dim, const float* gamma,
+                        void* stream) {
+    if (head_dim != 64) return fail(IDOL_ERR_UNSUPPORTED, "rms_heads: only head_dim 64 is implemented");
+    if (rows < 0 || heads < 1 || ld < (int64_t)heads * head_dim) return fail(IDOL_ERR_INVALID, "rms_heads: sizes");
+    if (rows == 0) return IDOL_OK;
+    if (!x || !gamma) return fail(IDOL_ERR_INVALID, "rms_heads: NULL pointer");
+    const cudaError_t e = idol::launch_rms_heads(x, dtype, ld, rows, heads, gamma, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue) return fail(IDOL_ERR_UNSUPPORTED, "rms_heads: dtype not implemented");
+    IDOL_CUDA(e);
+    return IDOL_OK;
+}
+
+int idol_b200_attention(const void* q, int64_t lq, int64_t ldq, const void* k, const void* v, int64_t lk, int64_t ldkv,
+                        int heads, int head_dim, void* out, int64_t ldo, int batch, void* stream) {
+    idol::AttentionCall c = {q, k, v, out, lq, lk, ldq, ldkv, ldo, heads, head_dim, batch,
+                             static_cast<cudaStream_t>(stream)};
+    return idol::attention(c);
 }
 
 }  // extern "C"

@@ -63,12 +63,35 @@ struct GemmCall {
 int q8_gemm(const GemmCall& c);
 
 // Tensor-map creation through the driver entry point (no link-time dependency on libcuda).
+int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swizzle);
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
 
 int num_sms(int device);
 
+// Row norms (norms.cu).
+bool norm_dim_ok(int dim);
+cudaError_t launch_norm_rows(const void* x, int x_dtype, long long ldx, void* y, int y_dtype, long long ldy,
+                             long long rows, int dim, float eps, const float* gamma, const float* beta,
+                             const float* shift, const float* scale, cudaStream_t s);
+cudaError_t launch_rms_heads(void* x, int dtype, long long ld, long long rows, int heads, const float* gamma,
+                             cudaStream_t s);
+
+// Attention (attention.cu).
+struct AttentionCall {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+    long long lq, lk, ldq, ldkv, ldo;
+    int heads, head_dim, batch;
+    cudaStream_t stream;
+};
+int attention(const AttentionCall& c);
+
 // Per translation unit readers of the sticky device error word (ptx.cuh IDOL_DEVICE_ERROR_READER).
 cudaError_t take_device_error_gemm(unsigned int* flags);
+cudaError_t take_device_error_attention(unsigned int* flags);
 
 }  // namespace idol

@@ -115,6 +115,28 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
                       int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
                       void* stream);
 
+/* ------------------------------------------------------------------------------------------ norms and attention */
+
+/* y = LayerNorm(x) per row of `dim` values (eps as given), then optionally * gamma + beta, then optionally
+ * * (1 + scale) + shift: src/decoders.cpp:23-42 norm_rows (gamma/beta and shift/scale come in pairs; fp32 vectors of
+ * dim on the device, or NULL). x/y dtypes: bf16->bf16, f32->bf16, f32->f32, f16->f16, bf16->f32. y may alias x.
+ * dim in {256, 512, 768, 1024, 1536, 2048}; rows 16-byte aligned. */
+int idol_b200_norm_rows(const void* x, int x_dtype, int64_t rows, int dim, int64_t ldx, float eps, const float* gamma,
+                        const float* beta, const float* shift, const float* scale, void* y, int y_dtype, int64_t ldy,
+                        void* stream);
+
+/* In place: each of `heads` groups of head_dim columns of each row (rows ld apart) becomes
+ * x * sqrt(hd) / max(|x|, 1e-12) * gamma[h * hd + d]: src/decoders.cpp:74-86 rms_heads. head_dim 64. */
+int idol_b200_rms_heads(void* x, int dtype, int64_t rows, int64_t ld, int heads, int head_dim, const float* gamma,
+                        void* stream);
+
+/* Multi-head attention, bf16: for each of `batch` independent sequences (q rows b*lq.., k/v rows b*lk..), per head h
+ * out[:, h*hd:(h+1)*hd] = softmax(q_h k_h^T / sqrt(hd)) v_h. Replaces src/kernels.cpp:737-746 attention
+ * (q lq rows ldq apart; k, v lk rows ldkv apart, e.g. k = kv and v = kv + dim as src/decoders.cpp:239 passes them; out
+ * rows ldo apart). head_dim 64; pointers 16-byte aligned; strides multiples of 8 elements. */
+int idol_b200_attention(const void* q, int64_t lq, int64_t ldq, const void* k, const void* v, int64_t lk, int64_t ldkv,
+                        int heads, int head_dim, void* out, int64_t ldo, int batch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
