@@ -1,0 +1,144 @@
+"""Resident weights and the layer compositions of the hot path, over the C-ABI of libidol_b200.so.
+
+* ``Q8Weight``     - one Q8_0 matrix (+ fp32 bias) resident on a GPU in the tiled layout (idol_b200_q8_import),
+                     made once from GGUF Q8_0 bytes, as src/weights.cpp + quantized_linear make theirs once.
+* ``DenoiserBlock`` - scope row A14: LN -> QKV -> rms q,k -> attention -> out + res -> LN -> ff1 (GELU tanh) -> ff2 +
+                     res (src/decoders.cpp:296-313 without the cross-attention), in place on the residual stream.
+* ``GaussianMLP``  - scope row A15: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14 -> activated heads.
+
+Workspaces are device tensors owned by the Python objects and reused across calls.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _capi as C
+from .q8 import _DTYPES, _ptr, _stream, q8_bytes, quantize
+
+
+class Q8Weight:
+    """A resident Q8_0 matrix. `q8` is GGUF Q8_0 bytes (uint8, out*in/32*34) on the target CUDA device."""
+
+    def __init__(self, q8: torch.Tensor, out: int, inp: int, bias: Optional[torch.Tensor] = None):
+        if not q8.is_cuda or q8.dtype != torch.uint8 or q8.numel() != q8_bytes(out, inp):
+            raise ValueError("Q8Weight: expected CUDA uint8 Q8_0 bytes of the given shape")
+        self.out, self.inp, self.device = out, inp, q8.device
+        b = None if bias is None else bias.detach().to(device=q8.device, dtype=torch.float32).contiguous()
+        h = ctypes.c_void_p()
+        C.check(C.lib().idol_b200_q8_import(_ptr(q8.contiguous()), q8.numel(), out, inp, _ptr(b), q8.device.index,
+                                            _stream(q8.device), ctypes.byref(h)))
+        torch.cuda.current_stream(q8.device).synchronize()
+        self.handle = h.value
+        self.q8 = q8
+
+    @classmethod
+    def from_float(cls, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> "Q8Weight":
+        """Quantize fp32 CUDA weights [out, in] on the device (gguf-py Q8_0 semantics) and upload."""
+        return cls(quantize(w.float().contiguous()), w.shape[0], w.shape[1], bias)
+
+    def __call__(self, x: torch.Tensor, act: int = C.ACT_NONE, residual: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        x2 = x if (x.stride(-1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
+        if out is None:
+            out = torch.empty((x2.shape[0], self.out), dtype=out_dtype or x.dtype, device=x.device)
+        ldr = 0 if residual is None else residual.stride(0)
+        C.check(C.lib().idol_b200_q8_gemm(ctypes.c_void_p(self.handle), _ptr(x2), _DTYPES[x2.dtype], x2.shape[0],
+                                          x2.stride(0), 0, self.out, _ptr(residual), ldr, act, 0, _ptr(out),
+                                          _DTYPES[out.dtype], out.stride(0), _stream(x.device)))
+        return out
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                C.lib().idol_b200_q8_free(ctypes.c_void_p(h))
+            except Exception:
+                pass
+            self.handle = None
+
+
+class _Workspace:
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes: int, device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+class DenoiserBlock:
+    """Scope row A14 on resident Q8_0 weights. `layers` maps qkv/out/ff1/ff2 to Q8Weight; gammas are [D] tensors."""
+
+    def __init__(self, qkv: Q8Weight, out: Q8Weight, ff1: Q8Weight, ff2: Q8Weight, q_gamma: torch.Tensor,
+                 k_gamma: torch.Tensor, heads: int, eps: float = 1e-6):
+        self.weights = (qkv, out, ff1, ff2)
+        dev = qkv.device
+        self.q_gamma = q_gamma.detach().to(device=dev, dtype=torch.float32).contiguous()
+        self.k_gamma = k_gamma.detach().to(device=dev, dtype=torch.float32).contiguous()
+        h = ctypes.c_void_p()
+        C.check(C.lib().idol_b200_block_create(*(ctypes.c_void_p(w.handle) for w in self.weights), _ptr(self.q_gamma),
+                                               _ptr(self.k_gamma), heads, float(eps), ctypes.byref(h)))
+        self.handle = h.value
+        self.dim, self.heads, self.device = out.out, heads, dev
+        self.ws = _Workspace()
+
+    def workspace_bytes(self, rows: int) -> int:
+        return int(C.lib().idol_b200_block_workspace_bytes(ctypes.c_void_p(self.handle), rows))
+
+    def forward_(self, x: torch.Tensor, images: int = 1) -> torch.Tensor:
+        """In place on x: [images * tokens, D], fp32 or bf16, contiguous."""
+        if not x.is_contiguous() or x.dim() != 2 or x.shape[1] != self.dim or x.shape[0] % images:
+            raise ValueError("DenoiserBlock: x must be a contiguous [images * tokens, D] tensor")
+        rows = x.shape[0]
+        nbytes = self.workspace_bytes(rows)
+        ws = self.ws.get(nbytes, x.device)
+        C.check(C.lib().idol_b200_block_forward(ctypes.c_void_p(self.handle), _ptr(x), _DTYPES[x.dtype],
+                                                rows // images, images, _ptr(ws), ws.numel(), _stream(x.device)))
+        return x
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                C.lib().idol_b200_block_free(ctypes.c_void_p(h))
+            except Exception:
+                pass
+            self.handle = None
+
+
+class GaussianMLP:
+    """Scope row A15 on resident Q8_0 weights: returns (raw [P, 14] fp32, activated [P, 14] fp32)."""
+
+    def __init__(self, layers: Sequence[Q8Weight]):
+        self.layers = tuple(layers)
+        h = ctypes.c_void_p()
+        C.check(C.lib().idol_b200_gaussian_mlp_create(*(ctypes.c_void_p(w.handle) for w in self.layers),
+                                                      ctypes.byref(h)))
+        self.handle = h.value
+        self.ws = _Workspace()
+
+    def __call__(self, x: torch.Tensor, raw: bool = True):
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+            raise ValueError("GaussianMLP: x must be a 2-D bf16 tensor with unit column stride")
+        points = x.shape[0]
+        nbytes = int(C.lib().idol_b200_gaussian_mlp_workspace_bytes(ctypes.c_void_p(self.handle), points))
+        ws = self.ws.get(nbytes, x.device)
+        out = torch.empty((points, 14), dtype=torch.float32, device=x.device)
+        raw_t = torch.empty((points, 14), dtype=torch.float32, device=x.device) if raw else None
+        C.check(C.lib().idol_b200_gaussian_mlp_forward(ctypes.c_void_p(self.handle), _ptr(x), points, x.stride(0),
+                                                       _ptr(ws), ws.numel(), _ptr(raw_t), _ptr(out),
+                                                       _stream(x.device)))
+        return raw_t, out
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                C.lib().idol_b200_gaussian_mlp_free(ctypes.c_void_p(h))
+            except Exception:
+                pass
+            self.handle = None

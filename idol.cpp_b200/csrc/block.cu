@@ -1,0 +1,233 @@
+// block.cu - compositions of the hot-path kernels, for callers that hand over a whole layer stack.
+//
+//   denoiser block (scope row A14; src/decoders.cpp:296-313 without the cross-attention, which the synthetic
+//   config-3 block leaves out):
+//       h = LN(x, eps)                                   norm_rows
+//       qkv = h W_qkv^T + b                              q8 GEMM          (rows x 3D, bf16)
+//       q, k <- rms_heads(q, gamma_q), rms_heads(k, gamma_k)
+//       a = attention(q, k, v) per image                 tcgen05 flash attention
+//       x = a W_out^T + b + x                            q8 GEMM, residual in place
+//       h = LN(x, eps)
+//       f = gelu_tanh(h W_ff1^T + b)                     q8 GEMM, activation in the epilogue
+//       x = f W_ff2^T + b + x                            q8 GEMM, residual in place
+//   The residual stream x is fp32 (as the reference's X) or bf16; everything a GEMM reads is bf16.
+//
+//   Gaussian MLP (scope row A15, config 4): 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the output heads
+//   (pos identity, scale exp, rotation f * 0.1 + (1, 0, 0, 0) normalised as src/decoders.cpp:422-428, colour and
+//   opacity sigmoid as :429).
+//
+// Both take a caller-provided device workspace (idol_b200_*_workspace_bytes) and allocate nothing themselves.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "internal.h"
+
+namespace idol {
+
+namespace {
+
+__device__ __forceinline__ float load_f(const void* p, int dtype, long long i) {
+    if (dtype == IDOL_F32) return static_cast<const float*>(p)[i];
+    if (dtype == IDOL_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+// One thread per point: 14 raw values -> 14 activated values (fp32).
+__global__ void gaussian_heads_kernel(const void* __restrict__ raw, int dtype, long long points, long long ld,
+                                      float* __restrict__ out) {
+    const long long pt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (pt >= points) return;
+    float f[14];
+#pragma unroll
+    for (int c = 0; c < 14; ++c) f[c] = load_f(raw, dtype, pt * ld + c);
+    float* o = out + pt * 14;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) o[c] = f[c];
+#pragma unroll
+    for (int c = 3; c < 6; ++c) o[c] = expf(f[c]);
+    // Rotation as src/decoders.cpp:422-428: r = f * lr_rotation + (1, 0, 0, 0), lr_rotation = 0.1 (the
+    // Representation default, src/weights.hpp:27), then divided by max(|r|, 1e-12).
+    float r[4], nrm = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        r[c] = f[6 + c] * 0.1f + (c == 0 ? 1.0f : 0.0f);
+        nrm += r[c] * r[c];
+    }
+    nrm = fmaxf(sqrtf(nrm), 1e-12f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[6 + c] = r[c] / nrm;
+#pragma unroll
+    for (int c = 10; c < 14; ++c) o[c] = 1.0f / (1.0f + expf(-f[c]));
+}
+
+}  // namespace
+
+cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
+                                  cudaStream_t s) {
+    if (points == 0) return cudaSuccess;
+    gaussian_heads_kernel<<<(unsigned)((points + 255) / 256), 256, 0, s>>>(raw, raw_dtype, points, ld, out);
+    return cudaGetLastError();
+}
+
+}  // namespace idol
+
+using idol::fail;
+
+struct idol_block {
+    const idol_q8_matrix* qkv;
+    const idol_q8_matrix* out;
+    const idol_q8_matrix* ff1;
+    const idol_q8_matrix* ff2;
+    const float* q_gamma;
+    const float* k_gamma;
+    int heads, dim, hidden, device;
+    float eps;
+};
+
+struct idol_gaussian_mlp {
+    const idol_q8_matrix* l0;
+    const idol_q8_matrix* l1;
+    const idol_q8_matrix* l2;
+    int device;
+};
+
+namespace {
+
+inline int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+int gemm(const idol_q8_matrix* w, const void* x, int64_t m, int64_t ldx, const void* residual, int64_t ldr, int act,
+         void* y, int y_dtype, int64_t ldy, cudaStream_t s, int x_dtype = IDOL_BF16) {
+    idol::GemmCall c = {&w->m, x, x_dtype, m, ldx, 0, w->m.n, residual, ldr, act, 0, y, y_dtype, ldy, s};
+    return idol::q8_gemm(c);
+}
+
+}  // namespace
+
+extern "C" {
+
+int idol_b200_block_create(const idol_q8_matrix* qkv, const idol_q8_matrix* out, const idol_q8_matrix* ff1,
+                           const idol_q8_matrix* ff2, const float* q_gamma, const float* k_gamma, int heads,
+                           float eps, idol_block** block) {
+    if (!block) return fail(IDOL_ERR_INVALID, "block_create: block is NULL");
+    *block = nullptr;
+    if (!qkv || !out || !ff1 || !ff2 || !q_gamma || !k_gamma) return fail(IDOL_ERR_INVALID, "block_create: NULL");
+    const int D = out->m.n;
+    if (heads < 1 || D != heads * 64) return fail(IDOL_ERR_UNSUPPORTED, "block_create: head_dim must be 64");
+    if (qkv->m.n != 3 * D || qkv->m.k != D || out->m.k != D || ff1->m.k != D || ff2->m.n != D ||
+        ff2->m.k != ff1->m.n)
+        return fail(IDOL_ERR_INVALID, "block_create: qkv (3D x D), out (D x D), ff1 (H x D), ff2 (D x H) expected");
+    if (!idol::norm_dim_ok(D)) return fail(IDOL_ERR_UNSUPPORTED, "block_create: model width not supported by norm_rows");
+    const int dev = qkv->m.device;
+    if (out->m.device != dev || ff1->m.device != dev || ff2->m.device != dev)
+        return fail(IDOL_ERR_INVALID, "block_create: matrices on different devices");
+    *block = new idol_block{qkv, out, ff1, ff2, q_gamma, k_gamma, heads, D, ff1->m.n, dev, eps};
+    return IDOL_OK;
+}
+
+int idol_b200_block_free(idol_block* block) {
+    delete block;
+    return IDOL_OK;
+}
+
+int64_t idol_b200_block_workspace_bytes(const idol_block* b, int64_t rows) {
+    if (!b || rows < 0) return -1;
+    const int64_t big = b->hidden > 3 * b->dim ? b->hidden : 3 * b->dim;
+    return align256(rows * b->dim * 2) + align256(rows * big * 2);
+}
+
+int idol_b200_block_forward(const idol_block* b, void* x, int x_dtype, int64_t tokens, int images, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+    if (!b || !x) return fail(IDOL_ERR_INVALID, "block_forward: NULL");
+    if (x_dtype != IDOL_F32 && x_dtype != IDOL_BF16) return fail(IDOL_ERR_UNSUPPORTED, "block_forward: x is f32 or bf16");
+    if (tokens < 1 || images < 1) return fail(IDOL_ERR_INVALID, "block_forward: tokens and images must be >= 1");
+    const int64_t rows = tokens * images;
+    if (!workspace || workspace_bytes < idol_b200_block_workspace_bytes(b, rows) ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(IDOL_ERR_INVALID, "block_forward: workspace smaller than idol_b200_block_workspace_bytes or not "
+                                      "256-byte aligned");
+    IDOL_CUDA(cudaSetDevice(b->device));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int D = b->dim;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws);                       // rows x D
+    __nv_bfloat16* big = reinterpret_cast<__nv_bfloat16*>(ws + align256(rows * D * 2));  // rows x max(3D, H)
+
+    IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
+                                     nullptr, s));
+    int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
+    if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, 3 * D, rows, b->heads, b->q_gamma, s));
+    IDOL_CUDA(idol::launch_rms_heads(big + D, IDOL_BF16, 3 * D, rows, b->heads, b->k_gamma, s));
+    idol::AttentionCall ac = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
+    rc = idol::attention(ac);
+    if (rc != IDOL_OK) return rc;
+    rc = gemm(b->out, h, rows, D, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+    if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
+                                     nullptr, s));
+    rc = gemm(b->ff1, h, rows, D, nullptr, 0, IDOL_ACT_GELU_TANH, big, IDOL_BF16, b->hidden, s);
+    if (rc != IDOL_OK) return rc;
+    return gemm(b->ff2, big, rows, b->hidden, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+}
+
+int idol_b200_gaussian_mlp_create(const idol_q8_matrix* l0, const idol_q8_matrix* l1, const idol_q8_matrix* l2,
+                                  idol_gaussian_mlp** mlp) {
+    if (!mlp) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: mlp is NULL");
+    *mlp = nullptr;
+    if (!l0 || !l1 || !l2) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: NULL");
+    if (l1->m.k != l0->m.n || l2->m.k != l1->m.n || l2->m.n != 14)
+        return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: layer shapes must chain and end in 14 outputs");
+    if (l0->m.n % 8 || l1->m.n % 8) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: hidden widths % 8 != 0");
+    *mlp = new idol_gaussian_mlp{l0, l1, l2, l0->m.device};
+    return IDOL_OK;
+}
+
+int idol_b200_gaussian_mlp_free(idol_gaussian_mlp* mlp) {
+    delete mlp;
+    return IDOL_OK;
+}
+
+int64_t idol_b200_gaussian_mlp_workspace_bytes(const idol_gaussian_mlp* mlp, int64_t points) {
+    if (!mlp || points < 0) return -1;
+    return align256(points * mlp->l0->m.n * 2) + align256(points * mlp->l1->m.n * 2) + align256(points * 14 * 4);
+}
+
+int idol_b200_gaussian_mlp_forward(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
+                                   void* workspace, int64_t workspace_bytes, float* raw_out, float* out,
+                                   void* stream) {
+    if (!mlp || !x || !out) return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward: NULL");
+    if (points < 0) return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward: points < 0");
+    if (points == 0) return IDOL_OK;
+    if (!workspace || workspace_bytes < idol_b200_gaussian_mlp_workspace_bytes(mlp, points) ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward: workspace too small or not 256-byte aligned");
+    IDOL_CUDA(cudaSetDevice(mlp->device));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int h0 = mlp->l0->m.n, h1 = mlp->l1->m.n;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    // The two hidden activations stay in fp16 (8x finer than bf16; SiLU outputs of this MLP are far inside its
+    // range), so layers 1 and 2 run the kernel's f16 operand path with fp16(d * q) weights.
+    __half* a = reinterpret_cast<__half*>(ws);
+    __half* b = reinterpret_cast<__half*>(ws + align256(points * h0 * 2));
+    float* raw = raw_out ? raw_out : reinterpret_cast<float*>(ws + align256(points * h0 * 2) + align256(points * h1 * 2));
+    int rc = gemm(mlp->l0, x, points, ldx, nullptr, 0, IDOL_ACT_SILU, a, IDOL_F16, h0, s);
+    if (rc != IDOL_OK) return rc;
+    rc = gemm(mlp->l1, a, points, h0, nullptr, 0, IDOL_ACT_SILU, b, IDOL_F16, h1, s, IDOL_F16);
+    if (rc != IDOL_OK) return rc;
+    rc = gemm(mlp->l2, b, points, h1, nullptr, 0, IDOL_ACT_NONE, raw, IDOL_F32, 14, s, IDOL_F16);
+    if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_gaussian_heads(raw, IDOL_F32, points, 14, out, s));
+    return IDOL_OK;
+}
+
+int idol_b200_gaussian_heads(const void* raw, int raw_dtype, int64_t points, int64_t ld, float* out, void* stream) {
+    if (points < 0 || ld < 14) return fail(IDOL_ERR_INVALID, "gaussian_heads: sizes");
+    if (points == 0) return IDOL_OK;
+    if (!raw || !out) return fail(IDOL_ERR_INVALID, "gaussian_heads: NULL");
+    IDOL_CUDA(idol::launch_gaussian_heads(raw, raw_dtype, points, ld, out, static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+}  // extern "C"

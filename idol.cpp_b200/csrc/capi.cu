@@ -86,10 +86,6 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 using idol::fail;
 
-struct idol_q8_matrix {
-    idol::Q8Matrix m;
-};
-
 namespace {
 
 bool shape_ok(int out, int in) { return out >= 1 && in >= 32 && in % 32 == 0; }

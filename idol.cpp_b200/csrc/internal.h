@@ -94,4 +94,12 @@ int attention(const AttentionCall& c);
 cudaError_t take_device_error_gemm(unsigned int* flags);
 cudaError_t take_device_error_attention(unsigned int* flags);
 
+cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
+                                  cudaStream_t s);
+
 }  // namespace idol
+
+// The opaque C-ABI handle around a device matrix (shared by the translation units that compose kernels).
+struct idol_q8_matrix {
+    idol::Q8Matrix m;
+};

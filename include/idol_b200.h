@@ -137,6 +137,37 @@ int idol_b200_rms_heads(void* x, int dtype, int64_t rows, int64_t ld, int heads,
 int idol_b200_attention(const void* q, int64_t lq, int64_t ldq, const void* k, const void* v, int64_t lk, int64_t ldkv,
                         int heads, int head_dim, void* out, int64_t ldo, int batch, void* stream);
 
+/* ------------------------------------------------------------------------------------------------ compositions */
+
+/* A denoiser-style transformer block over resident matrices (scope row A14: src/decoders.cpp:296-313 without the
+ * cross-attention): LN -> QKV -> rms q,k -> self-attention -> out + residual -> LN -> ff1 (GELU tanh) -> ff2 +
+ * residual. qkv is 3D x D, out D x D, ff1 H x D, ff2 D x H, D = heads * 64; q_gamma/k_gamma are fp32 [D] on the
+ * device. The handle keeps pointers only; the matrices must outlive it. */
+typedef struct idol_block idol_block;
+int idol_b200_block_create(const idol_q8_matrix* qkv, const idol_q8_matrix* out, const idol_q8_matrix* ff1,
+                           const idol_q8_matrix* ff2, const float* q_gamma, const float* k_gamma, int heads,
+                           float eps, idol_block** block);
+int idol_b200_block_free(idol_block* block);
+/* Device workspace the forward needs for `rows` = tokens * images rows. */
+int64_t idol_b200_block_workspace_bytes(const idol_block* block, int64_t rows);
+/* x: [images * tokens, D] residual stream (IDOL_F32 or IDOL_BF16), updated in place; each image attends within its
+ * own `tokens` rows. workspace: device, 256-byte aligned, >= idol_b200_block_workspace_bytes. */
+int idol_b200_block_forward(const idol_block* block, void* x, int x_dtype, int64_t tokens, int images, void* workspace,
+                            int64_t workspace_bytes, void* stream);
+
+/* The Gaussian decoder MLP of config 4 (scope row A15): x [points, in] bf16 -> l0 (SiLU) -> l1 (SiLU) -> l2 (14
+ * outputs) -> heads: pos identity, scale exp, rotation r = f * 0.1 + (1, 0, 0, 0) divided by max(|r|, 1e-12)
+ * (src/decoders.cpp:422-428 with the default lr_rotation), colour and opacity sigmoid (:429). out: fp32 [points, 14]; raw_out: fp32 [points, 14] pre-activation values, or NULL. */
+typedef struct idol_gaussian_mlp idol_gaussian_mlp;
+int idol_b200_gaussian_mlp_create(const idol_q8_matrix* l0, const idol_q8_matrix* l1, const idol_q8_matrix* l2,
+                                  idol_gaussian_mlp** mlp);
+int idol_b200_gaussian_mlp_free(idol_gaussian_mlp* mlp);
+int64_t idol_b200_gaussian_mlp_workspace_bytes(const idol_gaussian_mlp* mlp, int64_t points);
+int idol_b200_gaussian_mlp_forward(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
+                                   void* workspace, int64_t workspace_bytes, float* raw_out, float* out, void* stream);
+/* The output heads alone: raw [points, >= 14] (rows ld apart, raw_dtype) -> out fp32 [points, 14]. */
+int idol_b200_gaussian_heads(const void* raw, int raw_dtype, int64_t points, int64_t ld, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

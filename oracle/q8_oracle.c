@@ -215,7 +215,19 @@ void orc_gemm_q8(const float* a, int m, const uint8_t* q8, const float* bias, in
         const int col = n_offset + j;
         if (col >= N) break;
         orc_q8_dequantize(q8 + (int64_t)col * nb * 34, 1, K, wrow);
-        for (int i = 0; i < m; ++i) {
+        /* Eight rows at a time: independent chains for the CPU, the same per-output order as one row at a time. */
+        int i = 0;
+        for (; i + 8 <= m; i += 8) {
+            float tile[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int k0 = 0; k0 < K; k0 += 32) {
+                float part[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int k = k0; k < k0 + 32; ++k)
+                    for (int r = 0; r < 8; ++r) part[r] = fmaf(a[(int64_t)(i + r) * K + k], wrow[k], part[r]);
+                for (int r = 0; r < 8; ++r) tile[r] = k0 == 0 ? part[r] : tile[r] + part[r];
+            }
+            for (int r = 0; r < 8; ++r) out[i + r] = tile[r];
+        }
+        for (; i < m; ++i) {
             const float* ar = a + (int64_t)i * K;
             float tile = 0.0f;
             for (int k0 = 0; k0 < K; k0 += 32) {
@@ -321,8 +333,9 @@ void orc_attention(const float* q, int lq, int ldq, const float* k, const float*
 
 /* ------------------------------------------------------------------------------------------------------------------
  * Output heads of the synthetic Gaussian MLP (14 raw values per point -> 14 activated values, same order):
- *   pos 0..2 identity; scale 3..5 exp; rot 6..9 divided by max(|r|, 1e-12) (src/decoders.cpp:422-428);
- *   color 10..12 sigmoid; opacity 13 sigmoid (src/decoders.cpp:429).
+ *   pos 0..2 identity; scale 3..5 exp; rot 6..9 as src/decoders.cpp:422-428: r = f * lr_rotation + (1, 0, 0, 0)
+ *   with the default lr_rotation 0.1 (src/weights.hpp:27), divided by max(|r|, 1e-12); color 10..12 sigmoid;
+ *   opacity 13 sigmoid (src/decoders.cpp:429).
  * ---------------------------------------------------------------------------------------------------------------- */
 void orc_gaussian_heads(const float* raw, int64_t points, float* out) {
     for (int64_t p = 0; p < points; ++p) {
@@ -330,11 +343,14 @@ void orc_gaussian_heads(const float* raw, int64_t points, float* out) {
         float* o = out + p * 14;
         for (int c = 0; c < 3; ++c) o[c] = f[c];
         for (int c = 3; c < 6; ++c) o[c] = expf(f[c]);
-        float nrm = 0.0f;
-        for (int c = 6; c < 10; ++c) nrm += f[c] * f[c];
+        float r[4], nrm = 0.0f;
+        for (int c = 0; c < 4; ++c) {
+            r[c] = f[6 + c] * 0.1f + (c == 0 ? 1.0f : 0.0f);
+            nrm += r[c] * r[c];
+        }
         nrm = sqrtf(nrm);
         if (nrm < 1e-12f) nrm = 1e-12f;
-        for (int c = 6; c < 10; ++c) o[c] = f[c] / nrm;
+        for (int c = 0; c < 4; ++c) o[6 + c] = r[c] / nrm;
         for (int c = 10; c < 14; ++c) o[c] = 1.0f / (1.0f + expf(-f[c]));
     }
 }

@@ -1,0 +1,162 @@
+"""GPU parity of the compositions: the denoiser block (scope row A14) and the Gaussian MLP (row A15).
+
+* Small block (2 images x 128 tokens, D 1024, 16 heads, hidden 4096) against the CPU oracle's composition of the
+  pinned reference functions, bar max |y - ref| <= 2e-2 x rms(ref) on the block output; plus the block's update
+  (out - x) at 5e-2 x rms, which each sublayer must get right.
+* Config-3 size (2 x 4096 tokens) against an fp32 torch composition of the same math on the same GPU (dequantised
+  weights, fp32 matmuls with TF32 off, fp32 softmax attention).
+* Gaussian MLP at config-4 size (262,144 points): rows are independent, so sampled rows are checked against the
+  oracle: raw outputs at 2e-2 x rms, activated parameters at 1e-2 relative (north_star), with the group RMS as the
+  floor of the relative error for parameters near zero.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _check(y, ref, tol=TOL, what=""):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.isfinite(y).all(), what
+    rms = np.sqrt((ref ** 2).mean())
+    err = np.abs(y - ref).max()
+    assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
+
+
+def _make_block(pkg, oracle, cuda, D=1024, heads=16, H=4096, seed=0):
+    from idol_b200.block import DenoiserBlock, Q8Weight
+    rng = np.random.default_rng(seed)
+    layers, weights = {}, {}
+    for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "ff1": (H, D), "ff2": (D, H)}.items():
+        w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+        b = rng.normal(0, 0.01, n).astype(np.float32)
+        q8 = oracle.q8_quantize(w)
+        layers[name] = (q8, b, n, k)
+        weights[name] = Q8Weight(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k, torch.from_numpy(b))
+    qg = rng.normal(1, 0.1, D).astype(np.float32)
+    kg = rng.normal(1, 0.1, D).astype(np.float32)
+    layers["q_gamma"], layers["k_gamma"] = qg, kg
+    blk = DenoiserBlock(weights["qkv"], weights["out"], weights["ff1"], weights["ff2"], torch.from_numpy(qg),
+                        torch.from_numpy(kg), heads)
+    return blk, layers
+
+
+@pytest.mark.parametrize("x_dtype", [torch.float32, torch.bfloat16])
+def test_block_small_against_the_oracle(pkg, oracle, cuda, x_dtype):
+    blk, layers = _make_block(pkg, oracle, cuda)
+    rng = np.random.default_rng(1)
+    images, L, D = 2, 128, 1024
+    x = oracle.f32_to_bf16_round(rng.normal(0, 1, (images * L, D)).astype(np.float32))
+    ref = oracle.block_forward(x, layers, 16, images=images)
+    xt = torch.from_numpy(x).to(cuda, x_dtype)
+    blk.forward_(xt, images=images)
+    torch.cuda.synchronize()
+    y = xt.float().cpu().numpy()
+    _check(y, ref, what=f"block output ({x_dtype})")
+    _check(y - x, ref - x, tol=5e-2, what=f"block update ({x_dtype})")
+
+
+def _torch_block(x, ws, heads, eps=1e-6, images=1):
+    """fp32 torch composition of the block on dequantised weights (independent of the kernels under test)."""
+    D = x.shape[1]
+
+    def lin(a, name, act=None):
+        w, b = ws[name]
+        y = a @ w.T + b
+        if act == "gelu_tanh":
+            y = torch.nn.functional.gelu(y, approximate="tanh")
+        return y
+
+    def ln(a):
+        return torch.nn.functional.layer_norm(a, (D,), eps=eps)
+
+    h = ln(x)
+    qkv = lin(h, "qkv")
+    q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+
+    def rms(t, g):
+        t = t.reshape(t.shape[0], heads, 64)
+        t = t * 8.0 / t.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+        return t.reshape(t.shape[0], D) * g
+
+    q, k = rms(q, ws["q_gamma"]), rms(k, ws["k_gamma"])
+    L = x.shape[0] // images
+    outs = []
+    for i in range(images):
+        sl = slice(i * L, (i + 1) * L)
+        qh = q[sl].reshape(L, heads, 64).transpose(0, 1)
+        kh = k[sl].reshape(L, heads, 64).transpose(0, 1)
+        vh = v[sl].reshape(L, heads, 64).transpose(0, 1)
+        att = torch.softmax(qh @ kh.transpose(1, 2) / 8.0, dim=-1) @ vh
+        outs.append(att.transpose(0, 1).reshape(L, D))
+    a = torch.cat(outs)
+    x = lin(a, "out") + x
+    h = ln(x)
+    return lin(lin(h, "ff1", "gelu_tanh"), "ff2") + x
+
+
+def test_block_config3_size_against_torch_fp32(pkg, oracle, cuda):
+    from idol_b200.q8 import dequantize_tiled, repack
+    torch.backends.cuda.matmul.allow_tf32 = False
+    blk, layers = _make_block(pkg, oracle, cuda, seed=5)
+    ws = {}
+    for name in ("qkv", "out", "ff1", "ff2"):
+        q8, b, n, k = layers[name]
+        codes, scales = repack(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k)
+        ws[name] = (dequantize_tiled(codes, scales, n, k, torch.float32), torch.from_numpy(b).to(cuda))
+    ws["q_gamma"] = torch.from_numpy(layers["q_gamma"]).to(cuda)
+    ws["k_gamma"] = torch.from_numpy(layers["k_gamma"]).to(cuda)
+    g = torch.Generator(device=cuda).manual_seed(9)
+    images, L = 2, 4096
+    x = torch.randn((images * L, 1024), device=cuda, generator=g).to(torch.bfloat16).float()
+    ref = _torch_block(x, ws, 16, images=images)
+    y = x.clone()
+    blk.forward_(y, images=images)
+    torch.cuda.synchronize()
+    _check(y.cpu().numpy(), ref.cpu().numpy(), what="config-3 block vs torch fp32")
+    _check((y - x).cpu().numpy(), (ref - x).cpu().numpy(), tol=5e-2, what="config-3 block update vs torch fp32")
+
+
+def test_gaussian_mlp_config4_sampled_rows(pkg, oracle, cuda):
+    from idol_b200.block import GaussianMLP, Q8Weight
+    rng = np.random.default_rng(11)
+    dims = [(512, 128), (512, 512), (14, 512)]
+    layers, ws = [], []
+    for n, k in dims:
+        w = rng.normal(0, 0.02 if n != 14 else 0.2, (n, k)).astype(np.float32)
+        b = rng.normal(0, 0.01, n).astype(np.float32)
+        q8 = oracle.q8_quantize(w)
+        layers.append((q8, b, n, k))
+        ws.append(Q8Weight(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k, torch.from_numpy(b)))
+    mlp = GaussianMLP(ws)
+    P = 262144
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn((P, 128), device=cuda, generator=g).to(torch.bfloat16)
+    raw, out = mlp(x)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.linspace(0, P - 1, 300).astype(int), [0, 1, 255, 256, P - 1]]))
+    xs = x[rows].float().cpu().numpy()
+    ref_raw, ref_out = oracle.gaussian_mlp(xs, layers)
+    _check(raw[rows].cpu().numpy(), ref_raw, what="gaussian mlp raw")
+    got = out[rows].cpu().numpy()
+    for lo, hi, name in [(0, 3, "pos"), (3, 6, "scale"), (6, 10, "rot"), (10, 13, "color"), (13, 14, "opacity")]:
+        r, y = ref_out[:, lo:hi].astype(np.float64), got[:, lo:hi].astype(np.float64)
+        floor = np.sqrt((r ** 2).mean())
+        rel = np.abs(y - r) / np.maximum(np.abs(r), floor)
+        assert rel.max() <= 1e-2, f"{name}: max relative error {rel.max():.3e}"
+
+
+def test_block_workspace_and_errors(pkg, oracle, cuda):
+    blk, _ = _make_block(pkg, oracle, cuda, D=256, heads=4, H=512, seed=2)
+    assert blk.workspace_bytes(1000) >= 1000 * 256 * 2 + 1000 * 768 * 2
+    x = torch.zeros((100, 256), device=cuda)
+    with pytest.raises(ValueError):
+        blk.forward_(x, images=3)   # rows do not split into images
+
+
+def test_compositions_no_timeout(pkg, cuda):
+    torch.cuda.synchronize()
+    assert pkg._capi.device_status(0) == 0

@@ -109,7 +109,7 @@ def test_gaussian_heads(oracle):
     out = oracle.gaussian_heads(raw)
     np.testing.assert_array_equal(out[:, :3], raw[:, :3])
     np.testing.assert_allclose(out[:, 3:6], np.exp(raw[:, 3:6]), rtol=1e-6)
-    norms = np.linalg.norm(out[1:, 6:10], axis=1)
-    np.testing.assert_allclose(norms, 1.0, rtol=1e-6)
-    assert np.all(out[0, 6:10] == 0.0)
+    r = raw[:, 6:10] * np.float32(0.1) + np.array([1, 0, 0, 0], np.float32)
+    np.testing.assert_allclose(out[:, 6:10], r / np.linalg.norm(r, axis=1, keepdims=True), rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(out[0, 6:10], [1, 0, 0, 0])
     np.testing.assert_allclose(out[:, 10:], 1 / (1 + np.exp(-raw[:, 10:])), rtol=1e-6)
