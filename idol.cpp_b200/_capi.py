@@ -49,6 +49,7 @@ SIGNATURES = {
     "idol_b200_gaussian_mlp_free": (_i32, [_vp]),
     "idol_b200_gaussian_mlp_workspace_bytes": (_i64, [_vp, _i64]),
     "idol_b200_gaussian_mlp_forward": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "idol_b200_gaussian_mlp_forward_static": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "idol_b200_gaussian_heads": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp]),
 }
 

@@ -21,6 +21,8 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <mutex>
+#include <string>
 
 #include "internal.h"
 
@@ -220,6 +222,55 @@ int idol_b200_gaussian_mlp_forward(const idol_gaussian_mlp* mlp, const void* x, 
     if (rc != IDOL_OK) return rc;
     IDOL_CUDA(idol::launch_gaussian_heads(raw, IDOL_F32, points, 14, out, s));
     return IDOL_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Scratch of idol_b200_gaussian_mlp_forward_static: a fixed 8 MiB per GPU, reserved when the library's device code
+// is loaded on that GPU and held until the process exits. Host code must not use this name as an address (on the
+// host it is only a stand-in for the device symbol): the device address comes from cudaGetSymbolAddress below.
+constexpr int64_t kStaticMlpScratchBytes = 8ll << 20;
+static __device__ __align__(256) unsigned char g_mlp_static_scratch[kStaticMlpScratchBytes];
+
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_ptr[64] = {};
+
+// Device address of the scratch on the current device (`device`), looked up once per device.
+int static_scratch(int device, void** ptr) {
+    if (device < 0 || device >= 64) return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward_static: device index");
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (!g_static_scratch_ptr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_mlp_static_scratch);
+        if (e != cudaSuccess) return idol::cuda_fail(e, "cudaGetSymbolAddress (static MLP scratch)");
+        g_static_scratch_ptr[device] = p;
+    }
+    *ptr = g_static_scratch_ptr[device];
+    return IDOL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int idol_b200_gaussian_mlp_forward_static(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
+                                          float* raw_out, float* out, void* stream) {
+    if (!mlp) return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward_static: mlp is NULL");
+    const int64_t need = idol_b200_gaussian_mlp_workspace_bytes(mlp, points);
+    if (need < 0) return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward_static: points < 0");
+    if (need > kStaticMlpScratchBytes)
+        return fail(IDOL_ERR_INVALID, "gaussian_mlp_forward_static: " + std::to_string(points) + " points need " +
+                                          std::to_string(need) + " bytes of scratch, more than the fixed " +
+                                          std::to_string(kStaticMlpScratchBytes) +
+                                          " bytes this entry point has; split the batch or pass a workspace to "
+                                          "idol_b200_gaussian_mlp_forward");
+    IDOL_CUDA(cudaSetDevice(mlp->device));
+    void* scratch = nullptr;
+    const int rc = static_scratch(mlp->device, &scratch);
+    if (rc != IDOL_OK) return rc;
+    return idol_b200_gaussian_mlp_forward(mlp, x, points, ldx, scratch, kStaticMlpScratchBytes, raw_out, out, stream);
 }
 
 int idol_b200_gaussian_heads(const void* raw, int raw_dtype, int64_t points, int64_t ld, float* out, void* stream) {

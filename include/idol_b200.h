@@ -165,6 +165,19 @@ int idol_b200_gaussian_mlp_free(idol_gaussian_mlp* mlp);
 int64_t idol_b200_gaussian_mlp_workspace_bytes(const idol_gaussian_mlp* mlp, int64_t points);
 int idol_b200_gaussian_mlp_forward(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
                                    void* workspace, int64_t workspace_bytes, float* raw_out, float* out, void* stream);
+/* The same Gaussian MLP forward for callers that cannot allocate device memory at all, not even once for a
+ * workspace: code running where CUDA allocation calls are not allowed (for example a host function enqueued on a
+ * stream) or in a process whose device memory another allocator has already reserved in full. It allocates nothing:
+ * its scratch is a fixed 8 MiB array in the library's device code, reserved on every GPU that loads the library and
+ * held until exit; the caller still passes x, raw_out (or NULL) and out. A batch whose scratch would not fit
+ * (idol_b200_gaussian_mlp_workspace_bytes(mlp, points) > 8 MiB: about 3,980 points for 128 -> 512 -> 512 -> 14) is
+ * rejected with IDOL_ERR_INVALID. The first call on a device looks the array's address up on that device; make that
+ * first call before any stream capture. Every call on a device shares the one array, which keeps the last call's
+ * contents (nothing in it needs to start at zero): calls that overlap on the GPU, on different streams or different
+ * host threads, race on it and must be ordered by the caller. With matrices made by idol_b200_q8_view over memory
+ * the caller already holds, the whole path runs without a device allocation. No counterpart in the reference. */
+int idol_b200_gaussian_mlp_forward_static(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
+                                          float* raw_out, float* out, void* stream);
 /* The output heads alone: raw [points, >= 14] (rows ld apart, raw_dtype) -> out fp32 [points, 14]. */
 int idol_b200_gaussian_heads(const void* raw, int raw_dtype, int64_t points, int64_t ld, float* out, void* stream);
 
