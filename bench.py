@@ -170,19 +170,19 @@ def run_ours(args, rank, world, local_rank):
     for (m, k, n) in shapes():
         w = torch.randn((n, k), device=dev, generator=g) * 0.02
         packed = pkg.quantize(w)
-        codes, scales = pkg.repack(packed, n, k)
+        tiles = pkg.repack(packed, n, k)
         del w
         x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
         bias = (torch.randn(n, device=dev, generator=g) * 0.01)
         y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
-        ops.append(dict(m=m, k=k, n=n, packed=packed, codes=codes, scales=scales, x=x, bias=bias, y=y,
+        ops.append(dict(m=m, k=k, n=n, packed=packed, tiles=tiles, x=x, bias=bias, y=y,
                         bias_bf16=bias.to(torch.bfloat16)))
     step_flops = sum(flops(o["m"], o["k"], o["n"]) for o in ops)
     stream = torch.cuda.Stream(device=dev)
 
     def launch_step():
         for o in ops:
-            pkg.gemm_into(o["y"], o["x"], o["codes"], o["scales"], o["bias"], o["n"], o["k"])
+            pkg.gemm_into(o["y"], o["x"], o["tiles"], o["bias"], o["n"], o["k"])
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 1)):
@@ -238,18 +238,18 @@ def run_ours(args, rank, world, local_rank):
     mean_ms = []
     reps = []
     for o in ops:
-        per_copy = o["codes"].numel() + o["scales"].numel() * 2 + o["x"].numel() * 2
+        per_copy = o["tiles"].numel() + o["x"].numel() * 2
         R = int(min(32, max(2, -(-256e6 // per_copy))))
         copies = []
         for _ in range(R):
-            copies.append((o["codes"].clone(), o["scales"].clone(), o["x"].clone(), torch.empty_like(o["y"])))
+            copies.append((o["tiles"].clone(), o["x"].clone(), torch.empty_like(o["y"])))
         gs = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
-            for (c_, s_, x_, y_) in copies[:1]:
-                pkg.gemm_into(y_, x_, c_, s_, o["bias"], o["n"], o["k"])
+            for (t_, x_, y_) in copies[:1]:
+                pkg.gemm_into(y_, x_, t_, o["bias"], o["n"], o["k"])
             with torch.cuda.graph(gs, stream=stream):
-                for (c_, s_, x_, y_) in copies:
-                    pkg.gemm_into(y_, x_, c_, s_, o["bias"], o["n"], o["k"])
+                for (t_, x_, y_) in copies:
+                    pkg.gemm_into(y_, x_, t_, o["bias"], o["n"], o["k"])
             gs.replay()
         stream.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -291,10 +291,17 @@ def run_ours(args, rank, world, local_rank):
     h2d = sum(t.numel() * t.element_size() for t in host_x)
     d2h = sum(t.numel() * t.element_size() for t in host_y)
 
+    # Config 3 (denoiser-block steps) and config 4 (Gaussian MLP) on this GPU's own data (shard by request).
+    block_steps = max(3, min(args.steps, 30))
+    block_ms = measure_block(pkg, dev, stream, block_steps, world)
+    mlp_steps = max(3, min(args.steps, 30))
+    mlp_ms = measure_mlp(pkg, dev, stream, mlp_steps, world)
+    status = max(status, pkg._capi.device_status(local_rank))
+
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(status)], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, status = float(t[0]), float(t[1]), int(t[2])
+        ms, e2e_ms, status, block_ms, mlp_ms = float(t[0]), float(t[1]), int(t[2]), float(t[3]), float(t[4])
     clk = clocks.stop(wall0, wall1) if rank == 0 else None
     if rank != 0:
         return
@@ -325,7 +332,7 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
         "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
                    "operands": "resident in HBM", "l2": "each operand used once per step; a step streams "
-                   f"{sum(o['x'].numel() * 2 + o['codes'].numel() + o['y'].numel() * 2 for o in ops) / 1e9:.2f} GB "
+                   f"{sum(o['x'].numel() * 2 + o['tiles'].numel() + o['y'].numel() * 2 for o in ops) / 1e9:.2f} GB "
                    "> 126 MB L2", "timing": f"CUDA graph of {G} steps replayed; CUDA events",
                    "per_launch_timing": "per shape, a CUDA graph of R launches over R operand copies (> 256 MB in "
                    "total) replayed 3 times between CUDA events; R per shape in shapes[].copies",
@@ -342,6 +349,18 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": len(ops) * args.steps,
         "device_status": status,
         "clocks": clk,
+        "block": {"metric": "denoiser-block steps/s (config 3: 2 images x 4096 tokens, D 1024, 16 heads x 64, "
+                            "Q8_0 QKV/out/MLP 1024->4096->1024, GELU tanh, fp32 residual)",
+                  "value": round(block_steps * world / (block_ms / 1e3), 2), "unit": "block-steps/s",
+                  "ms_per_step": round(block_ms / block_steps, 3), "steps": block_steps,
+                  "tflops": round(BLOCK_FLOPS * block_steps * world / (block_ms / 1e3) / 1e12, 1),
+                  "frac_tensor": round(BLOCK_FLOPS / (block_ms / block_steps / 1e3) / 1e12 / tc_peak, 3),
+                  "scaling": "weak (each GPU runs its own images; no collective)",
+                  "work": "343.6 GFLOP per step (206.2 linears + 137.4 attention)"},
+        "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
+                                   "heads)", "value": round(MLP_POINTS * mlp_steps * world / (mlp_ms / 1e3), 0),
+                         "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
+                         "tflops": round(MLP_FLOPS * mlp_steps * world / (mlp_ms / 1e3) / 1e12, 1)},
     }
     if world == 1 and not args.no_cpu_baseline:
         v, cores, kind, sample = cpu_reference_sample()
@@ -350,30 +369,103 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_profile_shape(args):
-    """One GEMM shape, launched warmup + steps times back to back: the small case an ncu capture targets."""
+    """One GEMM shape (or the block / MLP composition), launched warmup + steps times back to back: the small case an
+    ncu capture targets."""
     import torch
     import __graft_entry__
     pkg = __graft_entry__.load_package()
+    if args.profile_shape in ("block", "mlp"):
+        dev = torch.device("cuda", 0)
+        stream = torch.cuda.Stream(device=dev)
+        fn = measure_block if args.profile_shape == "block" else measure_mlp
+        ms = fn(pkg, dev, stream, args.steps, 1)
+        print(json.dumps({"profile": args.profile_shape, "ms_per_step": round(ms / args.steps, 3),
+                          "device_status": pkg._capi.device_status(0)}))
+        return
     m, k, n = (int(v) for v in args.profile_shape.split(","))
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(7)
     packed = pkg.quantize(torch.randn((n, k), device=dev, generator=g) * 0.02)
-    codes, scales = pkg.repack(packed, n, k)
+    tiles = pkg.repack(packed, n, k)
     x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
     bias = torch.randn(n, device=dev, generator=g) * 0.01
     y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
     for _ in range(args.warmup):
-        pkg.gemm_into(y, x, codes, scales, bias, n, k)
+        pkg.gemm_into(y, x, tiles, bias, n, k)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        pkg.gemm_into(y, x, codes, scales, bias, n, k)
+        pkg.gemm_into(y, x, tiles, bias, n, k)
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
     print(json.dumps({"profile_shape": [m, k, n], "us_per_launch": round(us, 2),
                       "tflops": round(flops(m, k, n) / us / 1e6, 1), "device_status": pkg._capi.device_status(0)}))
+
+
+BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
+BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
+               + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
+MLP_POINTS = 262144
+MLP_FLOPS = 2.0 * MLP_POINTS * (128 * 512 + 512 * 512 + 512 * 14)
+
+
+def _graph_ms(torch, stream, fn, steps, world):
+    """Capture `fn` (one step) in a CUDA graph, warm it, then time `steps` replays with CUDA events."""
+    import torch.distributed as dist
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def measure_block(pkg, dev, stream, steps, world):
+    """Config 3: one denoiser block over 2 images x 4096 tokens (fp32 residual stream updated in place)."""
+    import torch
+    from idol_b200.block import DenoiserBlock, Q8Weight
+    g = torch.Generator(device=dev).manual_seed(77)
+    D, H = BLOCK_D, BLOCK_H
+    w = {}
+    for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "ff1": (H, D), "ff2": (D, H)}.items():
+        w[name] = Q8Weight.from_float(torch.randn((n, k), device=dev, generator=g) * 0.02,
+                                      torch.randn(n, device=dev, generator=g) * 0.01)
+    blk = DenoiserBlock(w["qkv"], w["out"], w["ff1"], w["ff2"], 1 + 0.1 * torch.randn(D, device=dev, generator=g),
+                        1 + 0.1 * torch.randn(D, device=dev, generator=g), BLOCK_HEADS)
+    x = torch.randn((BLOCK_IMAGES * BLOCK_TOKENS, D), device=dev, generator=g)
+    blk.forward_(x, images=BLOCK_IMAGES)  # sizes the workspace outside the graph
+    return _graph_ms(torch, stream, lambda: blk.forward_(x, images=BLOCK_IMAGES), steps, world)
+
+
+def measure_mlp(pkg, dev, stream, steps, world):
+    """Config 4: the Gaussian MLP over 262,144 points."""
+    import torch
+    from idol_b200.block import GaussianMLP, Q8Weight
+    g = torch.Generator(device=dev).manual_seed(78)
+    layers = [Q8Weight.from_float(torch.randn((n, k), device=dev, generator=g) * 0.02,
+                                  torch.randn(n, device=dev, generator=g) * 0.01)
+              for n, k in [(512, 128), (512, 512), (14, 512)]]
+    mlp = GaussianMLP(layers)
+    x = torch.randn((MLP_POINTS, 128), device=dev, generator=g).to(torch.bfloat16)
+    mlp(x)
+    return _graph_ms(torch, stream, lambda: mlp(x), steps, world)
 
 
 def run_reference(args, rank):
@@ -406,7 +498,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-shape", default=None,
-                    help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture")
+                    help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture; 'block' or 'mlp' "
+                         "runs the config-3 block or the config-4 MLP instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -6,7 +6,7 @@ Python identifier, so callers load it under the name ``idol_b200`` (see ``__graf
 """
 from . import _capi
 from .q8 import (PackedLinear, dequantize_tiled, enable_fused_packed, fused_linear, gemm_into, q8_bytes, q8_linear,
-                 quantize, repack, unpack)
+                 quantize, repack, tiled_bytes, unpack)
 
 __all__ = ["_capi", "PackedLinear", "dequantize_tiled", "enable_fused_packed", "fused_linear", "gemm_into", "q8_bytes",
-           "q8_linear", "quantize", "repack", "unpack"]
+           "q8_linear", "quantize", "repack", "tiled_bytes", "unpack"]

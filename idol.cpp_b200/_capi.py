@@ -22,15 +22,14 @@ SIGNATURES = {
     "idol_b200_version": (_i32, []),
     "idol_b200_device_status": (_i32, [_i32, _u32p]),
     "idol_b200_q8_bytes": (_i64, [_i32, _i32]),
-    "idol_b200_q8_codes_bytes": (_i64, [_i32, _i32]),
-    "idol_b200_q8_scales_bytes": (_i64, [_i32, _i32]),
+    "idol_b200_q8_tiled_bytes": (_i64, [_i32, _i32]),
     "idol_b200_q8_quantize": (_i32, [_vp, _i64, _i64, _vp, _vp]),
-    "idol_b200_q8_repack": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp]),
-    "idol_b200_q8_unpack": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
-    "idol_b200_q8_dequantize": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _vp]),
+    "idol_b200_q8_repack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "idol_b200_q8_unpack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "idol_b200_q8_dequantize": (_i32, [_vp, _i32, _i32, _vp, _i32, _vp]),
     "idol_b200_q8_upload": (_i32, [_vp, _i64, _i32, _i32, _vp, _i32, ctypes.POINTER(_vp)]),
     "idol_b200_q8_import": (_i32, [_vp, _i64, _i32, _i32, _vp, _i32, _vp, ctypes.POINTER(_vp)]),
-    "idol_b200_q8_view": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
+    "idol_b200_q8_view": (_i32, [_vp, _vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "idol_b200_q8_free": (_i32, [_vp]),
     "idol_b200_q8_info": (_i32, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
                                  ctypes.POINTER(_i64)]),

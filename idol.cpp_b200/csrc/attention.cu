@@ -59,6 +59,14 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128_mn(uint32_t start) {
     return d;
 }
 
+// 2^x by the hardware's approximate base-2 exponential (relative error near 2^-22, far below the bf16 rounding P gets
+// next); -inf gives +0.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
     asm volatile(
@@ -188,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool got = mbar_wait(&o_full[bo], (jo / 2) & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) return false;
             tc_fence_after();
-            const float f = (m_acc == -INFINITY) ? 0.0f : exp2f(m_acc - m_prev_blk);
+            const float f = (m_acc == -INFINITY) ? 0.0f : ex2(m_acc - m_prev_blk);
 #pragma unroll
             for (int c0 = 0; c0 < kHd; c0 += 16) {
                 uint32_t v[16];
@@ -210,19 +218,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int valid = p.lk - j * kKTile;  // keys of this block that exist
             const uint32_t s_col = kColS + b * kKTile;
-            // Pass 1: the row maximum of the scaled scores.
+            // Pass 1: the row maximum of the raw scores (the scale is positive, so it commutes with the max).
             float mx = -INFINITY;
+            if (valid >= kKTile) {
 #pragma unroll
-            for (int c0 = 0; c0 < kKTile; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + lane_base + s_col + c0, v);
-                tmem_ld_wait();
+                for (int c0 = 0; c0 < kKTile; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld16(tmem + lane_base + s_col + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+                    tmem_ld16(tmem + lane_base + s_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+                    tmem_ld_wait();
 #pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    if (c0 + c < valid) mx = fmaxf(mx, __uint_as_float(v[c]) * p.scale_log2);
+                    for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(v[c]));
+                }
+            } else {
+#pragma unroll
+                for (int c0 = 0; c0 < kKTile; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + lane_base + s_col + c0, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                        if (c0 + c < valid) mx = fmaxf(mx, __uint_as_float(v[c]));
+                }
             }
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - m_new);
+            const float m_new = fmaxf(m_run, mx * p.scale_log2);
+            const float alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_new);
+            const float neg_m = -m_new;
             // P_j goes to TMEM buffer b once P V of block j - 2 (which read that buffer) has completed.
             if (j >= 2) {
                 got = mbar_wait(&o_full[b], ((j - 2) / 2) & 1, abort_flag);
@@ -240,10 +261,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    const float t0 = (c0 + c < valid) ? __uint_as_float(v[c]) * p.scale_log2 - m_new : -INFINITY;
-                    const float t1 = (c0 + c + 1 < valid) ? __uint_as_float(v[c + 1]) * p.scale_log2 - m_new
-                                                          : -INFINITY;
-                    const float e0 = exp2f(t0), e1 = exp2f(t1);
+                    float t0 = fmaf(__uint_as_float(v[c]), p.scale_log2, neg_m);
+                    float t1 = fmaf(__uint_as_float(v[c + 1]), p.scale_log2, neg_m);
+                    if (c0 + c >= valid) t0 = -INFINITY;
+                    if (c0 + c + 1 >= valid) t1 = -INFINITY;
+                    const float e0 = ex2(t0), e1 = ex2(t1);
                     sum += e0 + e1;
                     pk[c / 2] = pack_bf16x2(e0, e1);
                 }

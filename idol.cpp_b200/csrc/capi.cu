@@ -95,11 +95,8 @@ int alloc_matrix(int out, int in, int device, idol_q8_matrix** result) {
     h->m.device = device;
     h->m.n = out;
     h->m.k = in;
-    h->m.groups = (out + 31) / 32;
-    cudaError_t e = cudaMalloc(&h->m.codes, idol::codes_bytes(out, in));
-    if (e == cudaSuccess) e = cudaMalloc(&h->m.scales, idol::scales_bytes(out, in));
+    const cudaError_t e = cudaMalloc(&h->m.tiles, idol::tiled_bytes(out, in));
     if (e != cudaSuccess) {
-        cudaFree(h->m.codes);
         delete h;
         return idol::cuda_fail(e, "cudaMalloc (Q8_0 matrix)");
     }
@@ -128,8 +125,7 @@ int idol_b200_device_status(int device, unsigned int* flags) {
 }
 
 int64_t idol_b200_q8_bytes(int out, int in) { return shape_ok(out, in) ? (int64_t)out * (in / 32) * 34 : -1; }
-int64_t idol_b200_q8_codes_bytes(int out, int in) { return shape_ok(out, in) ? idol::codes_bytes(out, in) : -1; }
-int64_t idol_b200_q8_scales_bytes(int out, int in) { return shape_ok(out, in) ? idol::scales_bytes(out, in) : -1; }
+int64_t idol_b200_q8_tiled_bytes(int out, int in) { return shape_ok(out, in) ? idol::tiled_bytes(out, in) : -1; }
 
 int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, void* stream) {
     if (rows < 0 || cols < 0 || cols % 32) return fail(IDOL_ERR_INVALID, "q8_quantize: cols must be a multiple of 32");
@@ -139,35 +135,34 @@ int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, 
     return IDOL_OK;
 }
 
-int idol_b200_q8_repack(const void* q8, int out, int in, void* codes, void* scales, void* stream) {
+int idol_b200_q8_repack(const void* q8, int out, int in, void* tiles, void* stream) {
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_repack: out >= 1 and in a positive multiple of 32");
-    if (!q8 || !codes || !scales) return fail(IDOL_ERR_INVALID, "q8_repack: NULL pointer");
-    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(codes) % 16 ||
-        reinterpret_cast<uintptr_t>(scales) % 2)
-        return fail(IDOL_ERR_INVALID, "q8_repack: q8 must be 2-byte, codes 16-byte aligned");
-    IDOL_CUDA(idol::launch_q8_repack(static_cast<const uint8_t*>(q8), out, in, static_cast<int8_t*>(codes),
-                                     static_cast<uint16_t*>(scales), static_cast<cudaStream_t>(stream)));
+    if (!q8 || !tiles) return fail(IDOL_ERR_INVALID, "q8_repack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q8_repack: q8 must be 2-byte, tiles 16-byte aligned");
+    IDOL_CUDA(idol::launch_q8_repack(static_cast<const uint8_t*>(q8), out, in, static_cast<uint8_t*>(tiles),
+                                     static_cast<cudaStream_t>(stream)));
     return IDOL_OK;
 }
 
-int idol_b200_q8_unpack(const void* codes, const void* scales, int out, int in, void* q8, void* stream) {
+int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stream) {
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_unpack: out >= 1 and in a positive multiple of 32");
-    if (!q8 || !codes || !scales) return fail(IDOL_ERR_INVALID, "q8_unpack: NULL pointer");
-    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(codes) % 16)
-        return fail(IDOL_ERR_INVALID, "q8_unpack: q8 must be 2-byte, codes 16-byte aligned");
-    IDOL_CUDA(idol::launch_q8_unpack(static_cast<const int8_t*>(codes), static_cast<const uint16_t*>(scales), out, in,
-                                     static_cast<uint8_t*>(q8), static_cast<cudaStream_t>(stream)));
+    if (!q8 || !tiles) return fail(IDOL_ERR_INVALID, "q8_unpack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q8) % 2 || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q8_unpack: q8 must be 2-byte, tiles 16-byte aligned");
+    IDOL_CUDA(idol::launch_q8_unpack(static_cast<const uint8_t*>(tiles), out, in, static_cast<uint8_t*>(q8),
+                                     static_cast<cudaStream_t>(stream)));
     return IDOL_OK;
 }
 
-int idol_b200_q8_dequantize(const void* codes, const void* scales, int out, int in, void* w, int w_dtype,
-                            void* stream) {
+int idol_b200_q8_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream) {
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_dequantize: out >= 1 and in a positive multiple of 32");
-    if (!codes || !scales || !w) return fail(IDOL_ERR_INVALID, "q8_dequantize: NULL pointer");
+    if (!tiles || !w) return fail(IDOL_ERR_INVALID, "q8_dequantize: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(tiles) % 16) return fail(IDOL_ERR_INVALID, "q8_dequantize: tiles not 16-byte aligned");
     if (w_dtype != IDOL_F32 && w_dtype != IDOL_BF16 && w_dtype != IDOL_F16)
         return fail(IDOL_ERR_UNSUPPORTED, "q8_dequantize: output must be f32, bf16 or f16");
-    IDOL_CUDA(idol::launch_q8_dequant(static_cast<const int8_t*>(codes), static_cast<const uint16_t*>(scales), out, in,
-                                      w, w_dtype, static_cast<cudaStream_t>(stream)));
+    IDOL_CUDA(idol::launch_q8_dequant(static_cast<const uint8_t*>(tiles), out, in, w, w_dtype,
+                                      static_cast<cudaStream_t>(stream)));
     return IDOL_OK;
 }
 
@@ -190,7 +185,7 @@ int idol_b200_q8_upload(const void* q8_host, int64_t nbytes, int out, int in, co
         if (e == cudaSuccess) e = cudaMemcpy(h->m.bias, bias_host, sizeof(float) * out, cudaMemcpyHostToDevice);
     }
     if (e == cudaSuccess)
-        e = idol::launch_q8_repack(static_cast<const uint8_t*>(staging), out, in, h->m.codes, h->m.scales, nullptr);
+        e = idol::launch_q8_repack(static_cast<const uint8_t*>(staging), out, in, h->m.tiles, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(staging);
     if (e != cudaSuccess) {
@@ -220,7 +215,7 @@ int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, con
         if (e == cudaSuccess) e = cudaMemcpyAsync(h->m.bias, bias_dev, sizeof(float) * out, cudaMemcpyDeviceToDevice, s);
     }
     if (e == cudaSuccess)
-        e = idol::launch_q8_repack(static_cast<const uint8_t*>(q8_dev), out, in, h->m.codes, h->m.scales, s);
+        e = idol::launch_q8_repack(static_cast<const uint8_t*>(q8_dev), out, in, h->m.tiles, s);
     if (e != cudaSuccess) {
         idol_b200_q8_free(h);
         return idol::cuda_fail(e, "q8_import");
@@ -229,20 +224,17 @@ int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, con
     return IDOL_OK;
 }
 
-int idol_b200_q8_view(const void* codes, const void* scales, const float* bias_dev, int out, int in, int device,
-                      idol_q8_matrix** matrix) {
+int idol_b200_q8_view(const void* tiles, const float* bias_dev, int out, int in, int device, idol_q8_matrix** matrix) {
     if (!matrix) return fail(IDOL_ERR_INVALID, "q8_view: matrix is NULL");
     *matrix = nullptr;
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_view: out >= 1 and in a positive multiple of 32");
-    if (!codes || !scales || reinterpret_cast<uintptr_t>(codes) % 16 || reinterpret_cast<uintptr_t>(scales) % 16)
-        return fail(IDOL_ERR_INVALID, "q8_view: codes and scales must be 16-byte aligned device pointers");
+    if (!tiles || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q8_view: tiles must be a 16-byte aligned device pointer");
     auto* h = new idol_q8_matrix();
     h->m.device = device;
     h->m.n = out;
     h->m.k = in;
-    h->m.groups = (out + 31) / 32;
-    h->m.codes = static_cast<int8_t*>(const_cast<void*>(codes));
-    h->m.scales = static_cast<uint16_t*>(const_cast<void*>(scales));
+    h->m.tiles = static_cast<uint8_t*>(const_cast<void*>(tiles));
     h->m.bias = const_cast<float*>(bias_dev);
     h->m.owns = false;
     *matrix = h;
@@ -253,8 +245,7 @@ int idol_b200_q8_free(idol_q8_matrix* matrix) {
     if (!matrix) return IDOL_OK;
     if (matrix->m.owns) {
         cudaSetDevice(matrix->m.device);
-        cudaFree(matrix->m.codes);
-        cudaFree(matrix->m.scales);
+        cudaFree(matrix->m.tiles);
         cudaFree(matrix->m.bias);
     }
     delete matrix;
@@ -267,8 +258,7 @@ int idol_b200_q8_info(const idol_q8_matrix* matrix, int* out, int* in, int* devi
     if (in) *in = matrix->m.k;
     if (device) *device = matrix->m.device;
     if (device_bytes)
-        *device_bytes = idol::codes_bytes(matrix->m.n, matrix->m.k) + idol::scales_bytes(matrix->m.n, matrix->m.k) +
-                        (matrix->m.bias ? 4 * (int64_t)matrix->m.n : 0);
+        *device_bytes = idol::tiled_bytes(matrix->m.n, matrix->m.k) + (matrix->m.bias ? 4 * (int64_t)matrix->m.n : 0);
     return IDOL_OK;
 }
 
@@ -277,7 +267,7 @@ int idol_b200_q8_export(const idol_q8_matrix* matrix, void* q8_dev, int64_t nbyt
     if (nbytes != (int64_t)matrix->m.n * (matrix->m.k / 32) * 34)
         return fail(IDOL_ERR_INVALID, "q8_export: byte count does not match the shape");
     IDOL_CUDA(cudaSetDevice(matrix->m.device));
-    IDOL_CUDA(idol::launch_q8_unpack(matrix->m.codes, matrix->m.scales, matrix->m.n, matrix->m.k,
+    IDOL_CUDA(idol::launch_q8_unpack(matrix->m.tiles, matrix->m.n, matrix->m.k,
                                      static_cast<uint8_t*>(q8_dev), static_cast<cudaStream_t>(stream)));
     return IDOL_OK;
 }

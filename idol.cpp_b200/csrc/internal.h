@@ -11,15 +11,24 @@
 
 namespace idol {
 
-// Device-resident Q8_0 matrix in the tiled layout (see q8_format.cu):
-//   codes : ceil(N/32) row groups x K/32 blocks x [2 halves][32 rows][16 bytes] int8
-//   scales: ceil(N/32) row groups x K/32 blocks x [32 rows] fp16 (the Q8_0 block scale d, bit for bit)
+// Tiled device layout of a Q8_0 matrix (see q8_format.cu): stage chunks of 128 weight rows x 64 k, each
+// kChunkBytes = 8192 bytes of codes ([quarter][block][half][lane][16]) followed by 512 bytes of fp16 scales
+// ([quarter][block][lane]), chunks ordered by (row tile, k stage). Rows past N and blocks past K/32 are zero.
+constexpr int kTileRows = 128;
+constexpr int kTileK = 64;
+constexpr int kChunkCodeBytes = 8192;
+constexpr int kChunkBytes = 8704;
+__host__ __device__ inline int row_tiles(int n) { return (n + kTileRows - 1) / kTileRows; }
+__host__ __device__ inline int k_stages(int k) { return (k + kTileK - 1) / kTileK; }
+__host__ __device__ inline int64_t tiled_bytes(int n, int k) {
+    return (int64_t)row_tiles(n) * k_stages(k) * kChunkBytes;
+}
+
+// Device-resident Q8_0 matrix in the tiled layout.
 struct Q8Matrix {
     int device = 0;
     int n = 0, k = 0;         // out, in features
-    int groups = 0;           // ceil(n / 32)
-    int8_t* codes = nullptr;
-    uint16_t* scales = nullptr;
+    uint8_t* tiles = nullptr;
     float* bias = nullptr;    // n floats on the device, or nullptr
     bool owns = true;         // false for matrices over caller memory
 };
@@ -34,15 +43,11 @@ int cuda_fail(cudaError_t e, const char* what);
         if (e_ != cudaSuccess) return ::idol::cuda_fail(e_, #call); \
     } while (0)
 
-inline int64_t codes_bytes(int n, int k) { return (int64_t)((n + 31) / 32) * 32 * k; }
-inline int64_t scales_bytes(int n, int k) { return (int64_t)((n + 31) / 32) * 32 * (k / 32) * 2; }
-
 // Format kernels (q8_format.cu).
-cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, int8_t* codes, uint16_t* scales, cudaStream_t s);
-cudaError_t launch_q8_unpack(const int8_t* codes, const uint16_t* scales, int n, int k, uint8_t* q8, cudaStream_t s);
+cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, uint8_t* tiles, cudaStream_t s);
+cudaError_t launch_q8_unpack(const uint8_t* tiles, int n, int k, uint8_t* q8, cudaStream_t s);
 cudaError_t launch_q8_quantize(const float* w, int64_t rows, int64_t cols, uint8_t* q8, cudaStream_t s);
-cudaError_t launch_q8_dequant(const int8_t* codes, const uint16_t* scales, int n, int k, void* w, int w_dtype,
-                              cudaStream_t s);
+cudaError_t launch_q8_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s);
 
 // The Q8_0 GEMM (q8_gemm.cu).
 struct GemmCall {

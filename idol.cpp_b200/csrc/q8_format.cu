@@ -3,10 +3,12 @@
 // GGUF Q8_0 (the interchange format): per output row, K/32 blocks of 34 bytes: fp16 scale d, then 32 int8 codes;
 // weight = d * q (tools/idol_packed.py:28-31, tools/idol_triton.py:24-33).
 //
-// Tiled device layout (what the GEMM reads): rows are grouped by 32. For row group g and Q8 block b, 1024 bytes of
-// codes ordered [half h][row r][16 bytes] (k = 32 b + 16 h + j), so a warp whose lane r owns row 32 g + r reads 512
-// contiguous bytes per 16-byte load; and 32 fp16 scales ordered by row. Rows past N are zero codes with a zero scale.
-// The scale bits and the codes are moved, never recomputed, so unpack(repack(x)) == x byte for byte.
+// Tiled device layout (what the GEMM reads): the matrix is cut into chunks of 128 weight rows x 64 k (two Q8 blocks),
+// ordered by (row tile, k stage). A chunk is the 8192 bytes of codes ordered [quarter q][block b][half h][lane r][16]
+// (row = 128 t + 32 q + r, k = 64 s + 32 b + 16 h + j) followed by the 512 bytes of their fp16 scales ordered
+// [quarter q][block b][lane r] - exactly one pipeline stage of one GEMM CTA, moved by a single bulk copy, in which a
+// warp whose lane r owns row 32 q + r reads 512 contiguous bytes per 16-byte load. Rows past N and blocks past K/32
+// are zero. Scale bits and codes are moved, never recomputed, so unpack(repack(x)) == x byte for byte.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -16,47 +18,58 @@ namespace idol {
 
 namespace {
 
-// One warp per (row group, block); lane r handles row 32 g + r.
-__global__ void q8_repack_kernel(const uint8_t* __restrict__ q8, int n, int k, int8_t* __restrict__ codes,
-                                 uint16_t* __restrict__ scales, int64_t units) {
-    const int kb = k / 32;
+// Byte offsets inside a chunk for lane r of quarter q, block b (code half h).
+__device__ __forceinline__ int64_t chunk_of(int t, int s, int ks) { return ((int64_t)t * ks + s) * kChunkBytes; }
+__device__ __forceinline__ int code_off(int q, int b, int h, int r) { return q * 2048 + b * 1024 + h * 512 + r * 16; }
+__device__ __forceinline__ int scale_off(int q, int b, int r) { return kChunkCodeBytes + q * 128 + b * 64 + r * 2; }
+
+// One warp per (row tile, stage, quarter, block); lane r handles row 128 t + 32 q + r.
+__global__ void q8_repack_kernel(const uint8_t* __restrict__ q8, int n, int k, uint8_t* __restrict__ tiles,
+                                 int64_t units) {
+    const int kb = k / 32, ks = k_stages(k);
     const int64_t unit = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (unit >= units) return;
     const int lane = threadIdx.x % 32;
-    const int64_t g = unit / kb;
-    const int b = (int)(unit % kb);
-    const int64_t row = g * 32 + lane;
+    const int b = (int)(unit % 2), q = (int)((unit / 2) % 4);
+    const int64_t ts = unit / 8;
+    const int s = (int)(ts % ks);
+    const int t = (int)(ts / ks);
+    const int64_t row = (int64_t)t * kTileRows + q * 32 + lane;
+    const int blk = 2 * s + b;
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     uint16_t d = 0;
-    if (row < n) {
+    if (row < n && blk < kb) {
         // A 34-byte block starts on a 2-byte boundary: read it as 17 halfwords.
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(q8 + (row * kb + b) * 34);
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(q8 + (row * kb + blk) * 34);
         d = src[0];
 #pragma unroll
         for (int i = 0; i < 8; ++i) w[i] = (uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16);
     }
-    int8_t* dst = codes + (g * kb + b) * 1024 + lane * 16;
-    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    reinterpret_cast<uint4*>(dst + 512)[0] = make_uint4(w[4], w[5], w[6], w[7]);
-    scales[(g * kb + b) * 32 + lane] = d;
+    uint8_t* chunk = tiles + chunk_of(t, s, ks);
+    *reinterpret_cast<uint4*>(chunk + code_off(q, b, 0, lane)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(chunk + code_off(q, b, 1, lane)) = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint16_t*>(chunk + scale_off(q, b, lane)) = d;
 }
 
-__global__ void q8_unpack_kernel(const int8_t* __restrict__ codes, const uint16_t* __restrict__ scales, int n, int k,
-                                 uint8_t* __restrict__ q8, int64_t units) {
-    const int kb = k / 32;
+__global__ void q8_unpack_kernel(const uint8_t* __restrict__ tiles, int n, int k, uint8_t* __restrict__ q8,
+                                 int64_t units) {
+    const int kb = k / 32, ks = k_stages(k);
     const int64_t unit = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (unit >= units) return;
     const int lane = threadIdx.x % 32;
-    const int64_t g = unit / kb;
-    const int b = (int)(unit % kb);
-    const int64_t row = g * 32 + lane;
-    if (row >= n) return;
-    const int8_t* src = codes + (g * kb + b) * 1024 + lane * 16;
-    const uint4 lo = reinterpret_cast<const uint4*>(src)[0];
-    const uint4 hi = reinterpret_cast<const uint4*>(src + 512)[0];
+    const int b = (int)(unit % 2), q = (int)((unit / 2) % 4);
+    const int64_t ts = unit / 8;
+    const int s = (int)(ts % ks);
+    const int t = (int)(ts / ks);
+    const int64_t row = (int64_t)t * kTileRows + q * 32 + lane;
+    const int blk = 2 * s + b;
+    if (row >= n || blk >= kb) return;
+    const uint8_t* chunk = tiles + chunk_of(t, s, ks);
+    const uint4 lo = *reinterpret_cast<const uint4*>(chunk + code_off(q, b, 0, lane));
+    const uint4 hi = *reinterpret_cast<const uint4*>(chunk + code_off(q, b, 1, lane));
     const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    uint16_t* dst = reinterpret_cast<uint16_t*>(q8 + (row * kb + b) * 34);
-    dst[0] = scales[(g * kb + b) * 32 + lane];
+    uint16_t* dst = reinterpret_cast<uint16_t*>(q8 + (row * kb + blk) * 34);
+    dst[0] = *reinterpret_cast<const uint16_t*>(chunk + scale_off(q, b, lane));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         dst[1 + 2 * i] = (uint16_t)(w[i] & 0xffffu);
@@ -96,18 +109,18 @@ __global__ void q8_quantize_kernel(const float* __restrict__ w, int64_t blocks, 
 }
 
 // Tiled layout -> dense [n, k] weights d * q in fp32, bf16 or fp16 (bf16/fp16 rounded from the exact fp32 product).
-__global__ void q8_dequant_kernel(const int8_t* __restrict__ codes, const uint16_t* __restrict__ scales, int n, int k,
-                                  void* __restrict__ out, int dtype) {
+__global__ void q8_dequant_kernel(const uint8_t* __restrict__ tiles, int n, int k, void* __restrict__ out, int dtype) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)n * k) return;
     const int64_t row = idx / k;
     const int col = (int)(idx % k);
-    const int kb = k / 32;
-    const int64_t g = row / 32;
-    const int r = (int)(row % 32), b = col / 32, h = (col % 32) / 16, j = col % 16;
-    const float q = (float)codes[((g * kb + b) * 2 + h) * 512 + r * 16 + j];
-    const float d = __half2float(__ushort_as_half(scales[(g * kb + b) * 32 + r]));
-    const float v = d * q;
+    const int ks = k_stages(k);
+    const int t = (int)(row / kTileRows), rq = (int)(row % kTileRows);
+    const int q = rq / 32, r = rq % 32, blk = col / 32, s = blk / 2, b = blk % 2, h = (col % 32) / 16, j = col % 16;
+    const uint8_t* chunk = tiles + chunk_of(t, s, ks);
+    const float qv = (float)(int8_t)chunk[code_off(q, b, h, r) + j];
+    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(chunk + scale_off(q, b, r))));
+    const float v = d * qv;
     if (dtype == IDOL_F32)
         static_cast<float*>(out)[idx] = v;
     else if (dtype == IDOL_BF16)
@@ -118,17 +131,17 @@ __global__ void q8_dequant_kernel(const int8_t* __restrict__ codes, const uint16
 
 }  // namespace
 
-cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, int8_t* codes, uint16_t* scales, cudaStream_t s) {
-    const int64_t units = (int64_t)((n + 31) / 32) * (k / 32);
+cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, uint8_t* tiles, cudaStream_t s) {
+    const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 8;
     const int warps = 8;
-    q8_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q8, n, k, codes, scales, units);
+    q8_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q8, n, k, tiles, units);
     return cudaGetLastError();
 }
 
-cudaError_t launch_q8_unpack(const int8_t* codes, const uint16_t* scales, int n, int k, uint8_t* q8, cudaStream_t s) {
-    const int64_t units = (int64_t)((n + 31) / 32) * (k / 32);
+cudaError_t launch_q8_unpack(const uint8_t* tiles, int n, int k, uint8_t* q8, cudaStream_t s) {
+    const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 8;
     const int warps = 8;
-    q8_unpack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(codes, scales, n, k, q8, units);
+    q8_unpack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(tiles, n, k, q8, units);
     return cudaGetLastError();
 }
 
@@ -140,11 +153,10 @@ cudaError_t launch_q8_quantize(const float* w, int64_t rows, int64_t cols, uint8
     return cudaGetLastError();
 }
 
-cudaError_t launch_q8_dequant(const int8_t* codes, const uint16_t* scales, int n, int k, void* w, int w_dtype,
-                              cudaStream_t s) {
+cudaError_t launch_q8_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s) {
     const int64_t total = (int64_t)n * k;
     if (total == 0) return cudaSuccess;
-    q8_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(codes, scales, n, k, w, w_dtype);
+    q8_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(tiles, n, k, w, w_dtype);
     return cudaGetLastError();
 }
 

@@ -39,17 +39,17 @@ constexpr int kRowsPerTile = 128;   // weight rows (output features) per CTA = T
 constexpr int kStageK = 64;         // k per pipeline stage: two Q8 blocks, one 128-byte swizzle row of bf16
 constexpr int kDequantWarps = 8;    // two per TMEM lane quarter: one per Q8 block of a stage
 constexpr int kThreads = 64 + 32 * kDequantWarps;  // warp 0 producer, warp 1 MMA / TMEM owner, warps 2-9 dequant
-constexpr int kCodeBytesPerStage = kRowsPerTile * kStageK;          // 8192
-constexpr int kScaleBytesPerStage = kRowsPerTile * 2 * 2;           // 512
+// One stage of weights = one chunk of the tiled layout: 8192 code bytes + 512 scale bytes, one bulk copy.
+static_assert(kTileRows == kRowsPerTile && kTileK == kStageK, "the GEMM stage is the layout's chunk");
 
 struct Params {
-    const int8_t* codes;
-    const uint16_t* scales;
+    const uint8_t* tiles;
     const float* bias;
     const void* residual;
     void* y;
-    int m, n, k, kb, groups;
-    int row_begin;            // first weight row of tile 0 (the window start rounded down to 32)
+    int m, n, k, kb;
+    int row_tiles, layout_stages;  // chunk grid of the tiled layout
+    int row_begin;            // first weight row of tile 0 (the window start rounded down to 128)
     int n_offset, n_count;    // output columns [n_offset, n_offset + n_count)
     long long ldy, ldr;
     int act;
@@ -60,7 +60,7 @@ struct Params {
 template <int BN, int S>
 struct Config {
     static constexpr int kXBytes = BN * 128;                         // BN rows of 64 bf16
-    static constexpr int kStageBytes = kXBytes + kCodeBytesPerStage + kScaleBytesPerStage;
+    static constexpr int kStageBytes = kXBytes + kChunkBytes;
     static constexpr int kACol0 = BN < 32 ? 32 : BN;                 // TMEM column of A stage 0 (D at column 0)
     static constexpr int kColsNeeded = kACol0 + S * 32;
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
@@ -173,9 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
     // The 128-byte swizzle needs 1024-aligned tiles in the shared address space.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;                                        // S x kXBytes, each 1024-aligned
-    uint8_t* cs = xs + S * C::kXBytes;                         // S x 8192
-    uint8_t* ss = cs + S * kCodeBytesPerStage;                 // S x 512
-    uint64_t* full = reinterpret_cast<uint64_t*>(ss + S * kScaleBytesPerStage);
+    uint8_t* ws = xs + S * C::kXBytes;                         // S x 8704: codes then scales of the stage
+    uint64_t* full = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);
     uint64_t* empty = full + S;
     uint64_t* afull = empty + S;
     uint64_t* accfull = afull + S;
@@ -184,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     const int row0 = p.row_begin + blockIdx.x * kRowsPerTile;
-    const int g0 = row0 / 32;
+    const int t128 = row0 / kRowsPerTile;  // row tile of the layout (always < row_tiles)
     const int m0 = blockIdx.y * BN;
     const int split = blockIdx.z;
     const int ks_begin = split * p.stages_per_split;
@@ -195,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 32 * kDequantWarps);
+            mbar_init(&afull[s], kDequantWarps);  // one arrival per dequant warp
         }
         mbar_init(accfull, 1);
         *abort_flag = 0;
@@ -219,18 +218,11 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
                 const int ks = ks_begin + i;
                 const int b0 = ks * 2;
                 const int nb = min(2, p.kb - b0);
-                int valid = 0;
-                for (int q = 0; q < 4; ++q) valid += (g0 + q < p.groups) ? 1 : 0;
-                const uint32_t tx = C::kXBytes + valid * nb * (1024 + 64);
-                mbar_arrive_expect_tx(&full[s], tx);
+                (void)nb;
+                mbar_arrive_expect_tx(&full[s], C::kXBytes + kChunkBytes);
                 tma_load_2d(xs + s * C::kXBytes, &xmap, ks * kStageK, m0, &full[s]);
-                for (int q = 0; q < 4; ++q) {
-                    const int g = g0 + q;
-                    if (g >= p.groups) continue;
-                    const long long blk = (long long)g * p.kb + b0;
-                    bulk_load(cs + s * kCodeBytesPerStage + q * 2048, p.codes + blk * 1024, nb * 1024, &full[s]);
-                    bulk_load(ss + s * kScaleBytesPerStage + q * 128, p.scales + blk * 32, nb * 64, &full[s]);
-                }
+                bulk_load(ws + s * kChunkBytes, p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes,
+                          kChunkBytes, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -257,7 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         // first Q8 block, warps 6-9 its second.
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
-        const bool valid = (g0 + q) < p.groups;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         for (int i = 0; i < nks; ++i) {
             const int s = i % S, u = i / S;
@@ -268,9 +259,9 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             const int ks = ks_begin + i;
             const bool present = half < min(2, p.kb - ks * 2);
             uint32_t regs[16];
-            if (valid && present) {
-                const uint8_t* cbase = cs + s * kCodeBytesPerStage + q * 2048 + half * 1024 + lane * 16;
-                const uint16_t* sbase = reinterpret_cast<const uint16_t*>(ss + s * kScaleBytesPerStage + q * 128);
+            if (present) {
+                const uint8_t* cbase = ws + s * kChunkBytes + q * 2048 + half * 1024 + lane * 16;
+                const uint16_t* sbase = reinterpret_cast<const uint16_t*>(ws + s * kChunkBytes + kChunkCodeBytes + q * 128);
                 const float d = __half2float(__ushort_as_half(sbase[half * 32 + lane]));
                 const float2 dd = make_float2(d, d);
                 const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
@@ -283,7 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             tmem_st16(tmem + lane_base + C::kACol0 + s * 32 + half * 16, *reinterpret_cast<const uint32_t(*)[16]>(regs));
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&afull[s]);
+            __syncwarp();  // every lane's stores are complete and fenced before lane 0 reports the warp
+            if (lane == 0) mbar_arrive(&afull[s]);
         }
 
         // Epilogue: the accumulator is ready once the last commit lands. Warp half h covers tokens
@@ -343,6 +335,260 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         tc_fence_after();
         tmem_dealloc(tmem, C::kTmemCols);
     }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Persistent CTA-pair variant (cta_group::2) for large M.
+//
+// Two CTAs of a cluster share one MMA of M = 256 weight rows x N = BN tokens: each CTA dequantises its own 128 rows
+// into its own TMEM but TMA-loads only its half of the token tile, so a CTA moves BN/2 x 64 x 2 bytes of activations
+// per stage instead of BN x 64 x 2 (L2 -> SM traffic per tensor-pipe cycle ~48 instead of ~81 bytes per SM at
+// BN = 256). The even CTA issues the MMAs; its barriers collect both CTAs' TMA bytes and both CTAs' dequantised
+// stages, and its commits arrive on the stage and accumulator barriers of both CTAs. No TMA multicast: each CTA loads
+// its own half.
+//
+// The grid holds one pair per two SMs and each pair walks the output tiles p, p + P, p + 2P, ... (P pairs). The stage
+// ring runs continuously across tiles, so the producer and dequant warps prepare the next tile while eight separate
+// epilogue warps drain the accumulator of the previous one; the MMA warp starts a tile once the epilogue warps of
+// both CTAs have read the accumulator out of TMEM (accempty).
+constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the token columns each
+constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
+
+template <int BN, int S>
+struct ConfigPair {
+    static constexpr int kHalf = BN / 2;
+    static constexpr int kXBytes = kHalf * 128;
+    static constexpr int kStageBytes = kXBytes + kChunkBytes;
+    static constexpr int kACol0 = BN;
+    static constexpr int kColsNeeded = kACol0 + S * 32;
+    static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
+    static constexpr int kBarBytes = 8 * (4 * S + 2) + 16;
+    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kBarBytes;
+    // At least 120 KB: one CTA per SM, so the pair's TMEM allocations never wait on a neighbour.
+    static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
+    static_assert(kColsNeeded <= 512, "TMEM budget");
+    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair MMA N");
+};
+
+struct PairSchedule {
+    int pairs_n;   // 256-row tiles along the output features
+    int tiles_m;   // BN-token tiles along M
+};
+
+template <int BN, int S, bool kBF16, typename OutT>
+__global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                       const Params p, const PairSchedule sched) {
+    using C = ConfigPair<BN, S>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* xs = smem;
+    uint8_t* ws = xs + S * C::kXBytes;                                              // S x 8704 weight chunks
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);            // even CTA: both halves landed
+    uint64_t* cfull = xfull + S;                                                    // this CTA's codes landed
+    uint64_t* empty = cfull + S;                                                    // both: the pair's MMA is done
+    uint64_t* afull = empty + S;                                                    // even CTA: both A stages in TMEM
+    uint64_t* accfull = afull + S;                                                  // both: accumulator ready
+    uint64_t* accempty = accfull + 1;                                               // even CTA: accumulator drained
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    const uint32_t rank = cluster_ctarank();
+    const int pair_id = blockIdx.x / 2;
+    const int num_pairs = gridDim.x / 2;
+    const int total_tiles = sched.pairs_n * sched.tiles_m;
+    const int nks = p.stages_total;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&cfull[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 2 * kDequantWarps);  // one arrival per dequant warp of either CTA
+        }
+        mbar_init(accfull, 1);
+        mbar_init(accempty, 2 * kEpilogueWarps);      // one arrival per epilogue warp of either CTA
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_holder, C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the peer's barriers exist before anything arrives on them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&xmap);
+            int i = 0;  // stage counter across tiles
+            bool ok = true;
+            for (int t = pair_id; t < total_tiles && ok; t += num_pairs) {
+                const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
+                const int t128 = row0 / kRowsPerTile;
+                const bool valid = t128 < p.row_tiles;  // the pair's second tile can fall past N
+                const int m0 = (t / sched.pairs_n) * BN;
+                for (int ks = 0; ks < nks; ++ks, ++i) {
+                    const int s = i % S, u = i / S;
+                    if (i >= S && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) { ok = false; break; }
+                    const int b0 = ks * 2;
+                    const int nb = min(2, p.kb - b0);
+                    if (rank == 0) mbar_arrive_expect_tx(&xfull[s], 2 * C::kXBytes);
+                    tma_load_2d_pair(xs + s * C::kXBytes, &xmap, ks * kStageK, m0 + (int)rank * C::kHalf,
+                                     map_to_rank(smem_u32(&xfull[s]), 0));
+                    (void)nb;
+                    mbar_arrive_expect_tx(&cfull[s], valid ? kChunkBytes : 0);
+                    if (valid)
+                        bulk_load(ws + s * kChunkBytes,
+                                  p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes, kChunkBytes,
+                                  &cfull[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = make_idesc_f16(2 * kRowsPerTile, BN, kBF16);
+            int i = 0, lt = 0;
+            bool ok = true;
+            for (int t = pair_id; t < total_tiles && ok; t += num_pairs, ++lt) {
+                // The epilogue warps of both CTAs must have read the previous tile's accumulator.
+                if (lt >= 1 && !mbar_wait(accempty, (lt - 1) & 1, abort_flag)) break;
+                tc_fence_after();
+                for (int ks = 0; ks < nks; ++ks, ++i) {
+                    const int s = i % S, u = i / S;
+                    if (!mbar_wait(&xfull[s], u & 1, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(&afull[s], u & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const int nk16 = (p.kb - ks * 2) >= 2 ? 4 : 2;
+                    const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
+                    for (int j = 0; j < nk16; ++j)
+                        mma_ts_pair(tmem, tmem + C::kACol0 + s * 32 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
+                                    (ks > 0 || j > 0) ? 1u : 0u);
+                    mma_commit_pair(&empty[s], 0x3);
+                }
+                mma_commit_pair(accfull, 0x3);
+            }
+        }
+    } else if (warp < 2 + kDequantWarps) {
+        const int q = warp % 4;
+        const int half = (warp - 2) / 4;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        int i = 0;
+        bool ok = true;
+        for (int t = pair_id; t < total_tiles && ok; t += num_pairs) {
+            const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
+            const bool valid = row0 / kRowsPerTile < p.row_tiles;
+            for (int ks = 0; ks < nks; ++ks, ++i) {
+                const int s = i % S, u = i / S;
+                bool got = mbar_wait(&cfull[s], u & 1, abort_flag);
+                if (got && i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+                tc_fence_after();
+                const bool present = half < min(2, p.kb - ks * 2);
+                uint32_t regs[16];
+                if (valid && present) {
+                    const uint8_t* cbase = ws + s * kChunkBytes + q * 2048 + half * 1024 + lane * 16;
+                    const uint16_t* sbase =
+                        reinterpret_cast<const uint16_t*>(ws + s * kChunkBytes + kChunkCodeBytes + q * 128);
+                    const float d = __half2float(__ushort_as_half(sbase[half * 32 + lane]));
+                    const float2 dd = make_float2(d, d);
+                    const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
+                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs);
+                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 8);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) regs[j] = 0u;
+                }
+                tmem_st16(tmem + lane_base + C::kACol0 + s * 32 + half * 16,
+                          *reinterpret_cast<const uint32_t(*)[16]>(regs));
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();  // every lane's stores are complete and fenced before lane 0 reports the warp
+                if (lane == 0) {
+                    if (rank == 0) mbar_arrive(&afull[s]);
+                    else mbar_arrive_remote(map_to_rank(smem_u32(&afull[s]), 0));
+                }
+            }
+        }
+    } else {
+        // Epilogue warps: warp w reads TMEM lanes of quarter w % 4; the two warps of a quarter split the columns.
+        const int ew = warp - 2 - kDequantWarps;
+        const int q = warp % 4;
+        const int half = ew / 4;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        constexpr int kHalfCols = BN / 2;
+        int lt = 0;
+        for (int t = pair_id; t < total_tiles; t += num_pairs, ++lt) {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(accfull, lt & 1, abort_flag));
+            if (!ok) break;
+            tc_fence_after();
+            const int row = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile +
+                            32 * q + lane;
+            const int m0 = (t / sched.pairs_n) * BN;
+            const bool row_ok = row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
+            const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
+            const int c_begin = half * kHalfCols;
+            for (int c0 = c_begin; c0 < c_begin + kHalfCols; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_base + c0, v);
+                tmem_ld_wait();
+                if (m0 + c0 < p.m) finish_cols<OutT, 16>(p, m0 + c0, row, v, bias, row_ok);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0) mbar_arrive(accempty);
+                else mbar_arrive_remote(map_to_rank(smem_u32(accempty), 0));
+            }
+        }
+    }
+
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers or read its TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, C::kTmemCols);
+    }
+}
+
+template <int BN, int S, bool kBF16, typename OutT>
+int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles_m, cudaStream_t stream) {
+    using C = ConfigPair<BN, S>;
+    auto kern = q8_gemm_pair_kernel<BN, S, kBF16, OutT>;
+    static unsigned long long configured = 0;
+    int dev = 0;
+    IDOL_CUDA(cudaGetDevice(&dev));
+    if (!(configured >> (dev & 63) & 1ull)) {
+        IDOL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+        configured |= 1ull << (dev & 63);
+    }
+    const int total = pairs_n * tiles_m;
+    const int max_pairs = num_sms(dev) / 2;
+    const int grid_pairs = total < max_pairs ? total : max_pairs;
+    PairSchedule sched = {pairs_n, tiles_m};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, p, sched));
+    return IDOL_OK;
+}
+
+template <bool kBF16, typename OutT>
+int dispatch_pair(int bn, const CUtensorMap& xmap, const Params& p, int pairs, int tiles_m, cudaStream_t stream) {
+    if (bn == 128) return launch_pair<128, 6, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
+    return launch_pair<256, 6, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT>
@@ -424,8 +670,7 @@ int q8_gemm(const GemmCall& c) {
     if (c.act < IDOL_ACT_NONE || c.act > IDOL_ACT_SILU) return fail(IDOL_ERR_INVALID, "q8_gemm: activation");
 
     Params p = {};
-    p.codes = w.codes;
-    p.scales = w.scales;
+    p.tiles = w.tiles;
     p.bias = w.bias;
     p.residual = c.residual;
     p.y = c.y;
@@ -433,8 +678,9 @@ int q8_gemm(const GemmCall& c) {
     p.n = w.n;
     p.k = w.k;
     p.kb = w.k / 32;
-    p.groups = w.groups;
-    p.row_begin = (c.n_offset / 32) * 32;
+    p.row_tiles = row_tiles(w.n);
+    p.layout_stages = k_stages(w.k);
+    p.row_begin = (c.n_offset / kRowsPerTile) * kRowsPerTile;
     p.n_offset = c.n_offset;
     p.n_count = c.n;
     p.ldy = c.ldy;
@@ -446,6 +692,32 @@ int q8_gemm(const GemmCall& c) {
     const int tiles_n = (c.n_offset + c.n - p.row_begin + kRowsPerTile - 1) / kRowsPerTile;
     int bn = 0, splits = 1;
     choose_tiles(w.device, c.m, tiles_n, p.stages_total, &bn, &splits);
+
+    // The CTA-pair kernel (IDOL_B200_GEMM_PAIR = 1 selects it for M tiles of 128 or 256 tokens).
+    const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
+    const bool pair = forced_pair == 1 && bn >= 128;  // off by default until it outruns the single-CTA kernel
+    if (pair) {
+        const int pbn = bn >= 256 ? 256 : 128;
+        p.stages_per_split = p.stages_total;
+        const int pairs = (c.n_offset + c.n - p.row_begin + 2 * kRowsPerTile - 1) / (2 * kRowsPerTile);
+        const int tiles_m = (int)((c.m + pbn - 1) / pbn);
+        if (tiles_m > 65535) return fail(IDOL_ERR_INVALID, "q8_gemm: m too large for one launch (split the batch)");
+        CUtensorMap xmap;
+        const int rc = encode_tmap_2d(&xmap, c.x_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                      c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK, pbn / 2,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc != IDOL_OK) return rc;
+        const bool bf16 = c.x_dtype == IDOL_BF16;
+        if (c.y_dtype == IDOL_F32)
+            return bf16 ? dispatch_pair<true, float>(pbn, xmap, p, pairs, tiles_m, c.stream)
+                        : dispatch_pair<false, float>(pbn, xmap, p, pairs, tiles_m, c.stream);
+        if (c.y_dtype == IDOL_BF16)
+            return bf16 ? dispatch_pair<true, __nv_bfloat16>(pbn, xmap, p, pairs, tiles_m, c.stream)
+                        : dispatch_pair<false, __nv_bfloat16>(pbn, xmap, p, pairs, tiles_m, c.stream);
+        return bf16 ? dispatch_pair<true, __half>(pbn, xmap, p, pairs, tiles_m, c.stream)
+                    : dispatch_pair<false, __half>(pbn, xmap, p, pairs, tiles_m, c.stream);
+    }
     p.stages_per_split = (p.stages_total + splits - 1) / splits;
     splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // every split gets >= 1 stage
     const int tiles_m = (int)((c.m + bn - 1) / bn);

@@ -46,22 +46,25 @@ def quantize(w: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def repack(packed: torch.Tensor, n: int, k: int):
-    """GGUF Q8_0 bytes (CUDA uint8) -> (codes int8, scales int16 holding fp16 bits) in the tiled device layout."""
+def tiled_bytes(n: int, k: int) -> int:
+    return int(C.lib().idol_b200_q8_tiled_bytes(n, k))
+
+
+def repack(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """GGUF Q8_0 bytes (CUDA uint8) -> the tiled device layout (uint8): chunks of 128 rows x 64 k, each 8192 code
+    bytes followed by their 512 bytes of fp16 scales."""
     if not packed.is_cuda or packed.dtype != torch.uint8 or packed.numel() != q8_bytes(n, k):
         raise ValueError("repack: expected CUDA uint8 Q8_0 bytes of the given shape")
     packed = packed.contiguous()
-    L = C.lib()
-    codes = torch.empty(L.idol_b200_q8_codes_bytes(n, k), dtype=torch.int8, device=packed.device)
-    scales = torch.empty(L.idol_b200_q8_scales_bytes(n, k) // 2, dtype=torch.int16, device=packed.device)
-    C.check(L.idol_b200_q8_repack(_ptr(packed), n, k, _ptr(codes), _ptr(scales), _stream(packed.device)))
-    return codes, scales
+    tiles = torch.empty(tiled_bytes(n, k), dtype=torch.uint8, device=packed.device)
+    C.check(C.lib().idol_b200_q8_repack(_ptr(packed), n, k, _ptr(tiles), _stream(packed.device)))
+    return tiles
 
 
-def unpack(codes: torch.Tensor, scales: torch.Tensor, n: int, k: int) -> torch.Tensor:
+def unpack(tiles: torch.Tensor, n: int, k: int) -> torch.Tensor:
     """Tiled layout -> GGUF Q8_0 bytes, the exact inverse of ``repack``."""
-    out = torch.empty(q8_bytes(n, k), dtype=torch.uint8, device=codes.device)
-    C.check(C.lib().idol_b200_q8_unpack(_ptr(codes), _ptr(scales), n, k, _ptr(out), _stream(codes.device)))
+    out = torch.empty(q8_bytes(n, k), dtype=torch.uint8, device=tiles.device)
+    C.check(C.lib().idol_b200_q8_unpack(_ptr(tiles), n, k, _ptr(out), _stream(tiles.device)))
     return out
 
 
@@ -70,15 +73,15 @@ _views: "collections.OrderedDict[tuple, int]" = collections.OrderedDict()
 _VIEW_CACHE = 4096
 
 
-def _view(codes, scales, bias, n, k, device_index):
+def _view(tiles, bias, n, k, device_index):
     """A C-ABI matrix handle over tensors the caller holds (cached; a handle is a few host bytes)."""
-    key = (codes.data_ptr(), scales.data_ptr(), 0 if bias is None else bias.data_ptr(), n, k, device_index)
+    key = (tiles.data_ptr(), 0 if bias is None else bias.data_ptr(), n, k, device_index)
     h = _views.get(key)
     if h is not None:
         _views.move_to_end(key)
         return h
     out = ctypes.c_void_p()
-    C.check(C.lib().idol_b200_q8_view(_ptr(codes), _ptr(scales), _ptr(bias), n, k, device_index, ctypes.byref(out)))
+    C.check(C.lib().idol_b200_q8_view(_ptr(tiles), _ptr(bias), n, k, device_index, ctypes.byref(out)))
     _views[key] = out.value
     if len(_views) > _VIEW_CACHE:
         _, old = _views.popitem(last=False)
@@ -86,13 +89,13 @@ def _view(codes, scales, bias, n, k, device_index):
     return out.value
 
 
-def gemm_into(y: torch.Tensor, x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
-              bias: Optional[torch.Tensor], n: int, k: int, n_offset: int = 0, n_count: Optional[int] = None,
-              residual: Optional[torch.Tensor] = None, act: int = C.ACT_NONE, flags: int = 0) -> torch.Tensor:
+def gemm_into(y: torch.Tensor, x: torch.Tensor, tiles: torch.Tensor, bias: Optional[torch.Tensor], n: int, k: int,
+              n_offset: int = 0, n_count: Optional[int] = None, residual: Optional[torch.Tensor] = None,
+              act: int = C.ACT_NONE, flags: int = 0) -> torch.Tensor:
     """y[m, :n_count] = x . W[n_offset:n_offset+n_count]^T + bias (+ residual) (-> act), written into y (2-D, rows of
     any stride >= n_count). x: 2-D bf16/f16 CUDA tensor with unit column stride. residual may alias y."""
     n_count = n - n_offset if n_count is None else n_count
-    h = _view(codes, scales, bias, n, k, x.device.index)
+    h = _view(tiles, bias, n, k, x.device.index)
     ldr = 0 if residual is None else residual.stride(0)
     C.check(C.lib().idol_b200_q8_gemm(ctypes.c_void_p(h), _ptr(x), _DTYPES[x.dtype], x.shape[0], x.stride(0),
                                       n_offset, n_count, _ptr(residual), ldr, act, flags, _ptr(y), _DTYPES[y.dtype],
@@ -107,18 +110,18 @@ def _aligned_rows(x2: torch.Tensor) -> torch.Tensor:
 
 
 @torch.library.custom_op("idol_b200::q8_linear", mutates_args=())
-def q8_linear(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, bias: Optional[torch.Tensor], n: int,
-              k: int, act: int = 0, flags: int = 0) -> torch.Tensor:
-    """x [..., k] bf16/f16 -> [..., n] in x's dtype; bias is fp32 [n] or None."""
+def q8_linear(x: torch.Tensor, tiles: torch.Tensor, bias: Optional[torch.Tensor], n: int, k: int, act: int = 0,
+              flags: int = 0) -> torch.Tensor:
+    """x [..., k] bf16/f16 -> [..., n] in x's dtype; tiles from ``repack``; bias is fp32 [n] or None."""
     x2 = _aligned_rows(x.reshape(-1, k))
     y = torch.empty((x2.shape[0], n), dtype=x.dtype, device=x.device)
     if x2.shape[0]:
-        gemm_into(y, x2, codes, scales, bias, n, k, act=act, flags=flags)
+        gemm_into(y, x2, tiles, bias, n, k, act=act, flags=flags)
     return y.reshape(*x.shape[:-1], n)
 
 
 @q8_linear.register_fake
-def _(x, codes, scales, bias, n, k, act=0, flags=0):
+def _(x, tiles, bias, n, k, act=0, flags=0):
     return x.new_empty((*x.shape[:-1], n))
 
 
@@ -155,9 +158,9 @@ def fused_linear(value, packed, shape, kind, bias=None):
         raise ValueError('invalid fused linear bias')
     if kind != Q8_0_KIND:
         raise ValueError('unsupported fused linear input: only Q8_0 is implemented on sm_100a')
-    codes, scales = _tiled_for(packed, n, k)
+    tiles = _tiled_for(packed, n, k)
     b32 = None if bias is None else bias.float()
-    return torch.ops.idol_b200.q8_linear(value, codes, scales, b32, n, k, C.ACT_NONE, C.EPI_BIAS_AFTER_ROUND)
+    return torch.ops.idol_b200.q8_linear(value, tiles, b32, n, k, C.ACT_NONE, C.EPI_BIAS_AFTER_ROUND)
 
 
 # ----------------------------------------------------------------------------------- PackedLinear (drop-in)
@@ -182,15 +185,13 @@ class PackedLinear(torch.nn.Module):
     def _tiles(self):
         dev = self.packed.device
         if self._tiled is None or self._tiled[0] != dev or self._tiled[1] != self.packed._version:
-            codes, scales = repack(self.packed, *self.shape)
-            self._tiled = (dev, self.packed._version, codes, scales)
-        return self._tiled[2], self._tiled[3]
+            self._tiled = (dev, self.packed._version, repack(self.packed, *self.shape))
+        return self._tiled[2]
 
     def dequantize(self, dtype):
         n, k = self.shape
         if self.packed.is_cuda:
-            codes, scales = self._tiles()
-            return dequantize_tiled(codes, scales, n, k, dtype)
+            return dequantize_tiled(self._tiles(), n, k, dtype)
         blocks = self.packed.reshape(-1, 34)
         scale = blocks[:, :2].contiguous().view(torch.float16).float()
         codes = blocks[:, 2:].contiguous().view(torch.int8).float()
@@ -214,13 +215,8 @@ def enable_fused_packed(model):
     return count
 
 
-def dequantize_tiled(codes, scales, n, k, dtype=torch.float32):
+def dequantize_tiled(tiles, n, k, dtype=torch.float32):
     """Dense [n, k] weights d * q from the tiled layout (fp32 exact; bf16/fp16 rounded from the fp32 product)."""
-    out = torch.empty((n, k), dtype=dtype, device=codes.device)
-    _dequant(codes, scales, n, k, out)
+    out = torch.empty((n, k), dtype=dtype, device=tiles.device)
+    C.check(C.lib().idol_b200_q8_dequantize(_ptr(tiles), n, k, _ptr(out), _DTYPES[out.dtype], _stream(tiles.device)))
     return out
-
-
-def _dequant(codes, scales, n, k, out):
-    C.check(C.lib().idol_b200_q8_dequantize(_ptr(codes), _ptr(scales), n, k, _ptr(out), _DTYPES[out.dtype],
-                                            _stream(codes.device)))

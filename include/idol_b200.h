@@ -54,23 +54,23 @@ int idol_b200_device_status(int device, unsigned int* flags);
 
 /* Bytes of GGUF Q8_0 data for an out x in matrix: out * in / 32 * 34 (tools/idol_triton.py:104). */
 int64_t idol_b200_q8_bytes(int out, int in);
-/* Bytes of the tiled device layout: codes (int8) and scales (fp16) planes. */
-int64_t idol_b200_q8_codes_bytes(int out, int in);
-int64_t idol_b200_q8_scales_bytes(int out, int in);
+/* Bytes of the tiled device layout: chunks of 128 rows x 64 k, each 8192 code bytes then their 512 bytes of fp16
+ * scales, ordered by (row tile, k stage); rows past `out` and blocks past in/32 are zero. */
+int64_t idol_b200_q8_tiled_bytes(int out, int in);
 
 /* fp32 weights [rows, cols] (device) -> Q8_0 blocks (device), byte-equal to gguf-py 0.19.0 gguf.quantize(W, Q8_0)
  * (called by tools/export_full_gguf.py:335). cols must be a multiple of 32. */
 int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, void* stream);
 
 /* Q8_0 blocks -> tiled layout (device to device), and the exact inverse. Replaces the GGUF->native conversion
- * tools/gguf_to_decoder.py:16-40 + tools/idolq.py:137-166 (pack_blob) with a layout the kernels stream coalesced. */
-int idol_b200_q8_repack(const void* q8, int out, int in, void* codes, void* scales, void* stream);
-int idol_b200_q8_unpack(const void* codes, const void* scales, int out, int in, void* q8, void* stream);
+ * tools/gguf_to_decoder.py:16-40 + tools/idolq.py:137-166 (pack_blob) with a layout one GEMM pipeline stage moves with
+ * a single bulk copy. tiles: idol_b200_q8_tiled_bytes(out, in) bytes, 16-byte aligned. */
+int idol_b200_q8_repack(const void* q8, int out, int in, void* tiles, void* stream);
+int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stream);
 
 /* Tiled layout -> dense out x in weights d * q (w_dtype IDOL_F32 exact; IDOL_BF16 / IDOL_F16 rounded from the fp32
  * product). Replaces src/kernels.cpp:535-550 dequantize_linear and tools/idol_packed.py:25-31 dequantize. */
-int idol_b200_q8_dequantize(const void* codes, const void* scales, int out, int in, void* w, int w_dtype,
-                            void* stream);
+int idol_b200_q8_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------------- resident matrices */
 
@@ -88,10 +88,9 @@ int idol_b200_q8_upload(const void* q8_host, int64_t nbytes, int out, int in, co
 int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, const float* bias_dev, int device,
                         void* stream, idol_q8_matrix** matrix);
 
-/* A matrix handle over tiled codes/scales (and an optional fp32 bias) that the caller already holds on `device`, e.g.
+/* A matrix handle over a tiled buffer (and an optional fp32 bias) that the caller already holds on `device`, e.g.
  * tensors of a PyTorch module; nothing is allocated on the device and idol_b200_q8_free releases only the handle. */
-int idol_b200_q8_view(const void* codes, const void* scales, const float* bias_dev, int out, int in, int device,
-                      idol_q8_matrix** matrix);
+int idol_b200_q8_view(const void* tiles, const float* bias_dev, int out, int in, int device, idol_q8_matrix** matrix);
 
 int idol_b200_q8_free(idol_q8_matrix* matrix);
 

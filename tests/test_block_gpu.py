@@ -105,8 +105,8 @@ def test_block_config3_size_against_torch_fp32(pkg, oracle, cuda):
     ws = {}
     for name in ("qkv", "out", "ff1", "ff2"):
         q8, b, n, k = layers[name]
-        codes, scales = repack(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k)
-        ws[name] = (dequantize_tiled(codes, scales, n, k, torch.float32), torch.from_numpy(b).to(cuda))
+        tiles = repack(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k)
+        ws[name] = (dequantize_tiled(tiles, n, k, torch.float32), torch.from_numpy(b).to(cuda))
     ws["q_gamma"] = torch.from_numpy(layers["q_gamma"]).to(cuda)
     ws["k_gamma"] = torch.from_numpy(layers["k_gamma"]).to(cuda)
     g = torch.Generator(device=cuda).manual_seed(9)

@@ -28,13 +28,13 @@ def test_library_exports_every_declared_symbol(pkg):
 def test_sizes_and_argument_errors_without_a_device(pkg):
     L = pkg._capi.lib()
     assert L.idol_b200_q8_bytes(4096, 1024) == 4096 * 32 * 34
-    assert L.idol_b200_q8_codes_bytes(14, 128) == 32 * 128
-    assert L.idol_b200_q8_scales_bytes(14, 128) == 32 * 4 * 2
+    assert L.idol_b200_q8_tiled_bytes(14, 128) == 1 * 2 * 8704
+    assert L.idol_b200_q8_tiled_bytes(300, 96) == 3 * 2 * 8704
     assert L.idol_b200_q8_bytes(16, 33) == -1
     h = ctypes.c_void_p()
     assert L.idol_b200_q8_upload(None, 0, 16, 48, None, 0, ctypes.byref(h)) == pkg._capi.ERR_INVALID
     assert b"multiple of 32" in L.idol_b200_last_error()
-    assert L.idol_b200_q8_view(None, None, None, 16, 64, 0, ctypes.byref(h)) == pkg._capi.ERR_INVALID
+    assert L.idol_b200_q8_view(None, None, 16, 64, 0, ctypes.byref(h)) == pkg._capi.ERR_INVALID
     assert L.idol_b200_q8_gemm(None, None, 2, 1, 64, 0, 16, None, 0, 0, 0, None, 2, 16, None) == pkg._capi.ERR_INVALID
     assert L.idol_b200_version() >= 100
 

@@ -34,7 +34,7 @@ def _upload(pkg, dev, q8, n, k):
     return pkg.repack(packed, n, k)
 
 
-def _gemm(pkg, dev, x, codes, scales, bias, n, k, n_offset=0, n_count=None, residual=None, act=0, flags=0,
+def _gemm(pkg, dev, x, tiles, bias, n, k, n_offset=0, n_count=None, residual=None, act=0, flags=0,
           out_dtype=torch.float32, x_dtype=torch.bfloat16):
     n_count = n - n_offset if n_count is None else n_count
     xt = torch.from_numpy(x).to(dev, x_dtype)
@@ -43,7 +43,7 @@ def _gemm(pkg, dev, x, codes, scales, bias, n, k, n_offset=0, n_count=None, resi
     if residual is not None:
         r = torch.from_numpy(residual).to(dev, out_dtype)
     b = None if bias is None else torch.from_numpy(bias).to(dev)
-    pkg.gemm_into(y, xt, codes, scales, b, n, k, n_offset, n_count, r, act, flags)
+    pkg.gemm_into(y, xt, tiles, b, n, k, n_offset, n_count, r, act, flags)
     return y.float().cpu().numpy()
 
 
@@ -63,16 +63,17 @@ def test_repack_round_trip_is_exact(pkg, cuda, n, k):
     rng = np.random.default_rng(n * 7 + k)
     raw = rng.integers(0, 256, size=n * (k // 32) * 34, dtype=np.uint8)  # any bytes, scales included
     packed = torch.from_numpy(raw).to(cuda)
-    codes, scales = pkg.repack(packed, n, k)
-    assert torch.equal(pkg.unpack(codes, scales, n, k).cpu(), torch.from_numpy(raw))
+    tiles = pkg.repack(packed, n, k)
+    assert tiles.numel() == ((n + 127) // 128) * ((k + 63) // 64) * 8704
+    assert torch.equal(pkg.unpack(tiles, n, k).cpu(), torch.from_numpy(raw))
 
 
 def test_dequantize_is_exact(pkg, oracle, cuda):
     rng = np.random.default_rng(11)
     n, k = 71, 256
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
-    codes, scales = _upload(pkg, cuda, q8, n, k)
-    got = pkg.dequantize_tiled(codes, scales, n, k, torch.float32).cpu().numpy()
+    tiles = _upload(pkg, cuda, q8, n, k)
+    got = pkg.dequantize_tiled(tiles, n, k, torch.float32).cpu().numpy()
     assert np.array_equal(got, oracle.q8_dequantize(q8, n, k))
 
 
@@ -86,8 +87,8 @@ def _golden_cases():
 def test_gemm_matches_the_reference_golden_outputs(pkg, cuda, name):
     c = _golden_cases()[name]
     m, n, k, n_off, cnt, gelu, has_res = (int(v) for v in c["meta"])
-    codes, scales = _upload(pkg, cuda, c["q8"], n, k)
-    y = _gemm(pkg, cuda, c["x"], codes, scales, c["bias"], n, k, n_off, cnt, c["res"] if has_res else None,
+    tiles = _upload(pkg, cuda, c["q8"], n, k)
+    y = _gemm(pkg, cuda, c["x"], tiles, c["bias"], n, k, n_off, cnt, c["res"] if has_res else None,
               act=1 if gelu else 0)
     _check(y, c["y"], what=name)
 
@@ -99,8 +100,8 @@ def test_gemm_matches_the_oracle_on_reference_test_shapes(pkg, oracle, cuda, m, 
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
     b = rng.normal(0, 0.5, n).astype(np.float32)
-    codes, scales = _upload(pkg, cuda, q8, n, k)
-    y = _gemm(pkg, cuda, x, codes, scales, b, n, k)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k)
     rows = np.unique(np.linspace(0, m - 1, min(m, 48)).astype(int))
     ref = oracle.gemm_q8(x[rows], q8, b, n, k)
     _check(y[rows], ref, what=f"{m}x{n}x{k}")
@@ -113,10 +114,10 @@ def test_gemm_config_sweep_sampled_rows(pkg, oracle, cuda, m, k, n):
     g = torch.Generator(device=cuda).manual_seed(m * 31 + k + n)
     w = torch.randn((n, k), device=cuda, generator=g) * 0.02
     q8_dev = pkg.quantize(w)
-    codes, scales = pkg.repack(q8_dev, n, k)
+    tiles = pkg.repack(q8_dev, n, k)
     x = torch.randn((m, k), device=cuda, generator=g).to(torch.bfloat16)
     b = (torch.randn(n, device=cuda, generator=g) * 0.01)
-    y = torch.ops.idol_b200.q8_linear(x, codes, scales, b, n, k, 0, 0)
+    y = torch.ops.idol_b200.q8_linear(x, tiles, b, n, k, 0, 0)
     torch.cuda.synchronize()
     rows = np.unique(np.linspace(0, m - 1, min(m, 24)).astype(int))
     q8 = q8_dev.cpu().numpy()
@@ -129,14 +130,40 @@ def test_gemm_config_sweep_sampled_rows(pkg, oracle, cuda, m, k, n):
 def test_every_tile_width_and_split(pkg, oracle, cuda, bn, splits, monkeypatch):
     monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
     monkeypatch.setenv("IDOL_B200_GEMM_SPLITS", str(splits))
+    monkeypatch.setenv("IDOL_B200_GEMM_PAIR", "0")  # the single-CTA kernel; the CTA-pair kernel is tested below
     rng = np.random.default_rng(bn * 10 + splits)
     m, n, k = 300, 200, 1056  # ragged M and N; K ends with a single 32-deep block
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
     b = rng.normal(0, 0.5, n).astype(np.float32)
-    codes, scales = _upload(pkg, cuda, q8, n, k)
-    y = _gemm(pkg, cuda, x, codes, scales, b, n, k)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k)
     _check(y, oracle.gemm_q8(x, q8, b, n, k), what=f"bn={bn} splits={splits}")
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("m,n,k,n_off,cnt", [(300, 200, 1056, 0, 200), (4097, 71, 256, 0, 71),
+                                             (1000, 600, 512, 64, 500), (257, 1024, 4096, 0, 1024),
+                                             (129, 384, 96, 128, 200)])
+def test_cta_pair_kernel(pkg, oracle, cuda, bn, m, n, k, n_off, cnt, monkeypatch):
+    """The cta_group::2 kernel: ragged M and N (odd tile counts leave the last pair's second CTA idle), windows,
+    K ending in a single 32-deep block, and a residual with GELU."""
+    monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
+    monkeypatch.setenv("IDOL_B200_GEMM_PAIR", "1")
+    rng = np.random.default_rng(m + n + k + bn)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    res = rng.normal(0, 1, (m, cnt)).astype(np.float32)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k, n_off, cnt, res, act=1)
+    rows = np.unique(np.linspace(0, m - 1, min(m, 64)).astype(int))
+    ref = oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], 1)
+    _check(y[rows], ref, what=f"pair bn={bn} {m}x{n}x{k} window {n_off}+{cnt}")
+    y16 = _gemm(pkg, cuda, x.astype(np.float16).astype(np.float32), tiles, b, n, k, x_dtype=torch.float16,
+                out_dtype=torch.float16)
+    ref16 = oracle.gemm_q8(x[rows].astype(np.float16).astype(np.float32), q8, b, n, k)
+    _check(y16[rows], ref16, what=f"pair fp16 bn={bn} {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("act", [0, 1, 2, 3])
@@ -151,11 +178,11 @@ def test_epilogue_window_residual_activation(pkg, oracle, cuda, act, out_dtype):
     res = rng.normal(0, 1, (m, cnt)).astype(np.float32)
     if out_dtype != torch.float32:
         res = torch.from_numpy(res).to(out_dtype).float().numpy()
-    codes, scales = _upload(pkg, cuda, q8, n, k)
+    tiles = _upload(pkg, cuda, q8, n, k)
     # residual aliasing the output, as src/decoders.cpp:303 passes X as both
     xt = torch.from_numpy(x).to(cuda, torch.bfloat16)
     y = torch.from_numpy(res).to(cuda, out_dtype)
-    pkg.gemm_into(y, xt, codes, scales, torch.from_numpy(b).to(cuda), n, k, n_off, cnt, y, act)
+    pkg.gemm_into(y, xt, tiles, torch.from_numpy(b).to(cuda), n, k, n_off, cnt, y, act)
     ref = oracle.gemm_q8(x, q8, b, n, k, n_off, cnt, res, act)
     _check(y.float().cpu().numpy(), ref, what=f"act={act} {out_dtype}")
 
@@ -166,8 +193,8 @@ def test_fp16_activations(pkg, oracle, cuda):
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = rng.normal(0, 1, (m, k)).astype(np.float16).astype(np.float32)
     b = rng.normal(0, 0.5, n).astype(np.float32)
-    codes, scales = _upload(pkg, cuda, q8, n, k)
-    y = _gemm(pkg, cuda, x, codes, scales, b, n, k, x_dtype=torch.float16, out_dtype=torch.float16)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k, x_dtype=torch.float16, out_dtype=torch.float16)
     _check(y, oracle.gemm_q8(x, q8, b, n, k), what="fp16")
 
 
