@@ -134,13 +134,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tmap(&vmap);
             mbar_arrive_expect_tx(q_full, kTileBytes);
             tma_load_3d(qs, &qmap, h * kHd, q0, img, q_full);
+            int issued = 0;
             for (int j = 0; j < nb; ++j) {
                 const int s = j % kStages, u = j / kStages;
                 if (j >= kStages && !mbar_wait(&kv_empty[s], (u - 1) & 1, abort_flag)) break;
                 mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
                 tma_load_3d(ks + s * kTileBytes, &kmap, h * kHd, j * kKTile, img, &kv_full[s]);
                 tma_load_3d(vs + s * kTileBytes, &vmap, h * kHd, j * kKTile, img, &kv_full[s]);
+                ++issued;
             }
+            // Every copy this CTA issued has landed before it can leave (see mbar_drain).
+            mbar_drain(q_full, 0);
+            for (int j = issued - kStages > 0 ? issued - kStages : 0; j < issued; ++j)
+                mbar_drain(&kv_full[j % kStages], (j / kStages) & 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {

@@ -121,6 +121,21 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Before a CTA leaves, its producer waits for the copies it issued into its own shared memory: the phase of the last
+// load into a stage completes when that load's bytes have landed. On the normal path these phases completed long
+// ago; after an aborted wait they may not have, and a copy must never land in a CTA that has exited. Bounded by
+// kDrainLimitNs and independent of the abort flag.
+constexpr unsigned long long kDrainLimitNs = 200000000ull;
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const unsigned long long start = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - start > kDrainLimitNs) {
+            atomicOr(&g_device_error, kErrWaitTimeout);
+            return;
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------ TMA and bulk copies
 // TMA load for a CTA pair (cta_group::2): the data lands in this CTA's shared memory and the completed bytes are
 // counted on the barrier at `bar_cluster_addr`, which may be the peer CTA's.

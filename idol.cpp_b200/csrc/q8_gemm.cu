@@ -212,9 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
     if (warp == 0) {
         if (lane == 0) {
             prefetch_tmap(&xmap);
+            int issued = 0;  // stages loaded so far
             for (int i = 0; i < nks; ++i) {
                 const int s = i % S, u = i / S;
                 if (i >= S && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) break;
+                ++issued;
                 const int ks = ks_begin + i;
                 const int b0 = ks * 2;
                 const int nb = min(2, p.kb - b0);
@@ -224,6 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
                 bulk_load(ws + s * kChunkBytes, p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes,
                           kChunkBytes, &full[s]);
             }
+            // The last load into each stage has landed before the CTA can leave (see mbar_drain).
+            for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) mbar_drain(&full[i % S], (i / S) & 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -424,7 +428,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
     if (warp == 0) {
         if (lane == 0) {
             prefetch_tmap(&xmap);
-            int i = 0;  // stage counter across tiles
+            int i = 0;  // stage counter across tiles (= stages loaded so far)
             bool ok = true;
             for (int t = pair_id; t < total_tiles && ok; t += num_pairs) {
                 const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
@@ -446,6 +450,13 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
                                   p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes, kChunkBytes,
                                   &cfull[s]);
                 }
+            }
+            // The last loads into each stage have landed before the CTA can leave (see mbar_drain): this CTA's codes
+            // on cfull; both CTAs' token halves on the even CTA's xfull (the odd CTA's copies count there too, and
+            // the final cluster barrier keeps the odd CTA until the even one has drained).
+            for (int j = i - S > 0 ? i - S : 0; j < i; ++j) {
+                mbar_drain(&cfull[j % S], (j / S) & 1);
+                if (rank == 0) mbar_drain(&xfull[j % S], (j / S) & 1);
             }
         }
     } else if (warp == 1) {
