@@ -141,6 +141,32 @@ __device__ __forceinline__ void dequant16(uint4 c, float2 dd, float2 ncd, uint32
     }
 }
 
+// One warp's share of a stage: rows 32 q .. 32 q + 31 of the weight chunk at `chunk` (both 32-deep Q8 blocks, or the
+// first `blocks` of them), dequantised into TMEM columns col .. col + 31 of those lanes (lane_base folded into col).
+// Blocks past K are written as zeros.
+template <bool kBF16>
+__device__ __forceinline__ void dequant_stage(const uint8_t* chunk, int q, int lane, int blocks, uint32_t col) {
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(chunk + kChunkCodeBytes + q * 128);
+    uint32_t regs[32];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if (b < blocks) {
+            const uint8_t* cbase = chunk + q * 2048 + b * 1024 + lane * 16;
+            const float d = __half2float(__ushort_as_half(sbase[b * 32 + lane]));
+            const float2 dd = make_float2(d, d);
+            const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
+            dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs + 16 * b);
+            dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 16 * b + 8);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) regs[16 * b + j] = 0u;
+        }
+    }
+    tmem_st16(col, *reinterpret_cast<const uint32_t(*)[16]>(regs));
+    tmem_st16(col + 16, *reinterpret_cast<const uint32_t(*)[16]>(regs + 16));
+    tmem_st_wait();
+}
+
 // Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row.
 template <typename OutT, int kCols>
 __device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
@@ -194,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], kDequantWarps);  // one arrival per dequant warp
+            mbar_init(&afull[s], kDequantWarps / 2);  // one arrival per dequant warp of the stage's group
         }
         mbar_init(accfull, 1);
         *abort_flag = 0;
@@ -231,52 +257,41 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            // One wait per stage: every dequant warp waited for the stage's bytes (full) before it reported its A
+            // stage (afull), so afull completing implies the token tile has landed too.
             const uint32_t idesc = make_idesc_f16(kRowsPerTile, BN, kBF16);
             for (int i = 0; i < nks; ++i) {
                 const int s = i % S, u = i / S;
-                if (!mbar_wait(&full[s], u & 1, abort_flag)) break;
                 if (!mbar_wait(&afull[s], u & 1, abort_flag)) break;
                 tc_fence_after();
                 const int ks = ks_begin + i;
-                const int nk16 = (p.kb - ks * 2) >= 2 ? 4 : 2;
+                const bool two_blocks = (p.kb - ks * 2) >= 2;
                 const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
-                for (int j = 0; j < nk16; ++j) {
-                    const uint32_t a = tmem + C::kACol0 + s * 32 + j * 8;
-                    mma_ts(tmem, a, make_sdesc_sw128(xaddr + j * 32), idesc, (i > 0 || j > 0) ? 1u : 0u);
-                }
+                const uint32_t a0 = tmem + C::kACol0 + s * 32;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < 2 || two_blocks)
+                        mma_ts(tmem, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc, (i > 0 || j > 0) ? 1u : 0u);
                 mma_commit(&empty[s]);
             }
             mma_commit(accfull);
         }
     } else {
-        // Dequant warps: warp w may only touch TMEM lanes [32 (w % 4), 32 (w % 4) + 32); warps 2-5 take the stage's
-        // first Q8 block, warps 6-9 its second.
+        // Dequant warps: warp w may only touch TMEM lanes [32 (w % 4), 32 (w % 4) + 32). Warps 2-5 take the even
+        // stages, warps 6-9 the odd ones, each dequantising both Q8 blocks of its stage for its 32 weight rows: the
+        // same work per warp as one block per stage, with half the barrier traffic per stage (waits, arrivals and
+        // tcgen05 fences of other warps slow the MMA issuer down).
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        for (int i = 0; i < nks; ++i) {
+        for (int i = half; i < nks; i += 2) {
             const int s = i % S, u = i / S;
             bool got = mbar_wait(&full[s], u & 1, abort_flag);
             if (got && i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
             tc_fence_after();
-            const int ks = ks_begin + i;
-            const bool present = half < min(2, p.kb - ks * 2);
-            uint32_t regs[16];
-            if (present) {
-                const uint8_t* cbase = ws + s * kChunkBytes + q * 2048 + half * 1024 + lane * 16;
-                const uint16_t* sbase = reinterpret_cast<const uint16_t*>(ws + s * kChunkBytes + kChunkCodeBytes + q * 128);
-                const float d = __half2float(__ushort_as_half(sbase[half * 32 + lane]));
-                const float2 dd = make_float2(d, d);
-                const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
-                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs);
-                dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 8);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) regs[j] = 0u;
-            }
-            tmem_st16(tmem + lane_base + C::kACol0 + s * 32 + half * 16, *reinterpret_cast<const uint32_t(*)[16]>(regs));
-            tmem_st_wait();
+            dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, min(2, p.kb - (ks_begin + i) * 2),
+                                 tmem + lane_base + C::kACol0 + s * 32);
             tc_fence_before();
             __syncwarp();  // every lane's stores are complete and fenced before lane 0 reports the warp
             if (lane == 0) mbar_arrive(&afull[s]);
@@ -351,27 +366,36 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 // stages, and its commits arrive on the stage and accumulator barriers of both CTAs. No TMA multicast: each CTA loads
 // its own half.
 //
-// The grid holds one pair per two SMs and each pair walks the output tiles p, p + P, p + 2P, ... (P pairs). The stage
-// ring runs continuously across tiles, so the producer and dequant warps prepare the next tile while eight separate
-// epilogue warps drain the accumulator of the previous one; the MMA warp starts a tile once the epilogue warps of
-// both CTAs have read the accumulator out of TMEM (accempty).
+// The grid holds one pair per two SMs and each pair walks the output tiles p, p + P, p + 2P, ... (P pairs). Three
+// rings run continuously across tiles:
+//   * S shared-memory stages (token half + weight chunk), filled by the producer, freed by the MMA commit (empty);
+//   * SA TMEM A slots (32 columns: one stage of dequantised weights), filled by the dequant warps (afull) - fewer
+//     than S, since TMEM also holds the accumulators. Slot i % SA is free again once stage i - SA is consumed, which
+//     the same per-stage commit reports (empty[(i - SA) % S]), so the MMA thread commits once per stage;
+//   * two TMEM accumulators of BN columns: the MMA warp fills accumulator lt % 2 for its lt-th tile and commits
+//     accfull; eight separate epilogue warps drain it (bias, residual, activation, stores) and report accempty, so
+//     the epilogue of one tile runs under the main loop of the next.
+// TMEM budget: 2 BN + 32 SA <= 512 columns (BN = 192 with SA = 4, BN = 128 with SA = 8).
 constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the token columns each
 constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 
-template <int BN, int S>
+template <int BN, int S, int SA>
 struct ConfigPair {
     static constexpr int kHalf = BN / 2;
     static constexpr int kXBytes = kHalf * 128;
     static constexpr int kStageBytes = kXBytes + kChunkBytes;
-    static constexpr int kACol0 = BN;
-    static constexpr int kColsNeeded = kACol0 + S * 32;
+    static constexpr int kACol0 = 2 * BN;  // accumulators at columns 0 and BN, then the A slots
+    static constexpr int kColsNeeded = kACol0 + SA * 32;
     static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
-    static constexpr int kBarBytes = 8 * (4 * S + 2) + 16;
+    static constexpr int kBarBytes = 8 * (3 * S + SA + 4) + 16;
+    static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
     static constexpr int kSmemUsed = 1024 + S * kStageBytes + kBarBytes;
     // At least 120 KB: one CTA per SM, so the pair's TMEM allocations never wait on a neighbour.
     static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
     static_assert(kColsNeeded <= 512, "TMEM budget");
+    static_assert(kSmemUsed <= 227 * 1024, "shared memory budget");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair MMA N");
+    static_assert(kXBytes % 1024 == 0, "each token half must stay 1024-aligned for the 128-byte swizzle");
 };
 
 struct PairSchedule {
@@ -379,21 +403,21 @@ struct PairSchedule {
     int tiles_m;   // BN-token tiles along M
 };
 
-template <int BN, int S, bool kBF16, typename OutT>
+template <int BN, int S, int SA, bool kBF16, typename OutT>
 __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                        const Params p, const PairSchedule sched) {
-    using C = ConfigPair<BN, S>;
+    using C = ConfigPair<BN, S, SA>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;
     uint8_t* ws = xs + S * C::kXBytes;                                              // S x 8704 weight chunks
     uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);            // even CTA: both halves landed
     uint64_t* cfull = xfull + S;                                                    // this CTA's codes landed
-    uint64_t* empty = cfull + S;                                                    // both: the pair's MMA is done
-    uint64_t* afull = empty + S;                                                    // even CTA: both A stages in TMEM
-    uint64_t* accfull = afull + S;                                                  // both: accumulator ready
-    uint64_t* accempty = accfull + 1;                                               // even CTA: accumulator drained
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 1);
+    uint64_t* empty = cfull + S;                                                    // both: stage s consumed
+    uint64_t* afull = empty + S;                                                    // even CTA: A slot written (both)
+    uint64_t* accfull = afull + SA;                                                 // both: accumulator b ready
+    uint64_t* accempty = accfull + 2;                                               // even CTA: accumulator b drained
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -408,10 +432,12 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             mbar_init(&xfull[s], 1);
             mbar_init(&cfull[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 2 * kDequantWarps);  // one arrival per dequant warp of either CTA
         }
-        mbar_init(accfull, 1);
-        mbar_init(accempty, 2 * kEpilogueWarps);      // one arrival per epilogue warp of either CTA
+        for (int a = 0; a < SA; ++a) mbar_init(&afull[a], kDequantWarps);  // one per dequant warp of the group, both CTAs
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accfull[b], 1);
+            mbar_init(&accempty[b], 2 * kEpilogueWarps);  // one arrival per epilogue warp of either CTA
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -465,25 +491,33 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             int i = 0, lt = 0;
             bool ok = true;
             for (int t = pair_id; t < total_tiles && ok; t += num_pairs, ++lt) {
-                // The epilogue warps of both CTAs must have read the previous tile's accumulator.
-                if (lt >= 1 && !mbar_wait(accempty, (lt - 1) & 1, abort_flag)) break;
+                // The epilogue warps of both CTAs must have read this accumulator's previous tile (two tiles ago).
+                const int b = lt & 1;
+                if (lt >= 2 && !mbar_wait(&accempty[b], ((lt >> 1) - 1) & 1, abort_flag)) break;
                 tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(b * BN);
                 for (int ks = 0; ks < nks; ++ks, ++i) {
-                    const int s = i % S, u = i / S;
-                    if (!mbar_wait(&xfull[s], u & 1, abort_flag)) { ok = false; break; }
-                    if (!mbar_wait(&afull[s], u & 1, abort_flag)) { ok = false; break; }
+                    // One wait per stage: the even CTA's dequant warps waited for both token halves (xfull) before
+                    // they reported the A slot, so afull completing implies the stage's tokens have landed.
+                    const int s = i % S;
+                    const int a = i % SA, ua = i / SA;
+                    if (!mbar_wait(&afull[a], ua & 1, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    const int nk16 = (p.kb - ks * 2) >= 2 ? 4 : 2;
+                    const bool two_blocks = (p.kb - ks * 2) >= 2;
                     const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
-                    for (int j = 0; j < nk16; ++j)
-                        mma_ts_pair(tmem, tmem + C::kACol0 + s * 32 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
-                                    (ks > 0 || j > 0) ? 1u : 0u);
+                    const uint32_t a0 = tmem + C::kACol0 + a * 32;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (j < 2 || two_blocks)
+                            mma_ts_pair(acc, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
+                                        (ks > 0 || j > 0) ? 1u : 0u);
                     mma_commit_pair(&empty[s], 0x3);
                 }
-                mma_commit_pair(accfull, 0x3);
+                mma_commit_pair(&accfull[b], 0x3);
             }
         }
     } else if (warp < 2 + kDequantWarps) {
+        // As in the single-CTA kernel: warps 2-5 take the even stages, warps 6-9 the odd ones, both Q8 blocks each.
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
@@ -493,34 +527,24 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
             const bool valid = row0 / kRowsPerTile < p.row_tiles;
             for (int ks = 0; ks < nks; ++ks, ++i) {
+                if ((i & 1) != half) continue;
                 const int s = i % S, u = i / S;
+                const int a = i % SA;
                 bool got = mbar_wait(&cfull[s], u & 1, abort_flag);
-                if (got && i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
+                if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);  // see the MMA loop
+                if (got && i >= SA) {  // A slot a was last read by stage i - SA
+                    const int r = i - SA;
+                    got = mbar_wait(&empty[r % S], (r / S) & 1, abort_flag);
+                }
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
-                const bool present = half < min(2, p.kb - ks * 2);
-                uint32_t regs[16];
-                if (valid && present) {
-                    const uint8_t* cbase = ws + s * kChunkBytes + q * 2048 + half * 1024 + lane * 16;
-                    const uint16_t* sbase =
-                        reinterpret_cast<const uint16_t*>(ws + s * kChunkBytes + kChunkCodeBytes + q * 128);
-                    const float d = __half2float(__ushort_as_half(sbase[half * 32 + lane]));
-                    const float2 dd = make_float2(d, d);
-                    const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
-                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs);
-                    dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 8);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) regs[j] = 0u;
-                }
-                tmem_st16(tmem + lane_base + C::kACol0 + s * 32 + half * 16,
-                          *reinterpret_cast<const uint32_t(*)[16]>(regs));
-                tmem_st_wait();
+                dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, valid ? min(2, p.kb - ks * 2) : 0,
+                                     tmem + lane_base + C::kACol0 + a * 32);
                 tc_fence_before();
                 __syncwarp();  // every lane's stores are complete and fenced before lane 0 reports the warp
                 if (lane == 0) {
-                    if (rank == 0) mbar_arrive(&afull[s]);
-                    else mbar_arrive_remote(map_to_rank(smem_u32(&afull[s]), 0));
+                    if (rank == 0) mbar_arrive(&afull[a]);
+                    else mbar_arrive_remote(map_to_rank(smem_u32(&afull[a]), 0));
                 }
             }
         }
@@ -533,7 +557,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
         constexpr int kHalfCols = BN / 2;
         int lt = 0;
         for (int t = pair_id; t < total_tiles; t += num_pairs, ++lt) {
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(accfull, lt & 1, abort_flag));
+            const int b = lt & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&accfull[b], (lt >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
             const int row = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile +
@@ -542,17 +567,18 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             const bool row_ok = row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
             const int c_begin = half * kHalfCols;
+            const uint32_t acc = tmem + lane_base + (uint32_t)(b * BN);
             for (int c0 = c_begin; c0 < c_begin + kHalfCols; c0 += 16) {
                 uint32_t v[16];
-                tmem_ld16(tmem + lane_base + c0, v);
+                tmem_ld16(acc + c0, v);
                 tmem_ld_wait();
                 if (m0 + c0 < p.m) finish_cols<OutT, 16>(p, m0 + c0, row, v, bias, row_ok);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                if (rank == 0) mbar_arrive(accempty);
-                else mbar_arrive_remote(map_to_rank(smem_u32(accempty), 0));
+                if (rank == 0) mbar_arrive(&accempty[b]);
+                else mbar_arrive_remote(map_to_rank(smem_u32(&accempty[b]), 0));
             }
         }
     }
@@ -565,10 +591,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
     }
 }
 
-template <int BN, int S, bool kBF16, typename OutT>
+template <int BN, int S, int SA, bool kBF16, typename OutT>
 int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles_m, cudaStream_t stream) {
-    using C = ConfigPair<BN, S>;
-    auto kern = q8_gemm_pair_kernel<BN, S, kBF16, OutT>;
+    using C = ConfigPair<BN, S, SA>;
+    auto kern = q8_gemm_pair_kernel<BN, S, SA, kBF16, OutT>;
     static unsigned long long configured = 0;
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -598,8 +624,8 @@ int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles
 
 template <bool kBF16, typename OutT>
 int dispatch_pair(int bn, const CUtensorMap& xmap, const Params& p, int pairs, int tiles_m, cudaStream_t stream) {
-    if (bn == 128) return launch_pair<128, 6, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
-    return launch_pair<256, 6, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
+    if (bn == 128) return launch_pair<128, 8, 8, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
+    return launch_pair<192, 8, 4, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT>
@@ -708,7 +734,7 @@ int q8_gemm(const GemmCall& c) {
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
     const bool pair = forced_pair == 1 && bn >= 128;  // off by default until it outruns the single-CTA kernel
     if (pair) {
-        const int pbn = bn >= 256 ? 256 : 128;
+        const int pbn = bn >= 256 ? 192 : 128;  // two accumulators of pbn columns fit TMEM beside the A slots
         p.stages_per_split = p.stages_total;
         const int pairs = (c.n_offset + c.n - p.row_begin + 2 * kRowsPerTile - 1) / (2 * kRowsPerTile);
         const int tiles_m = (int)((c.m + pbn - 1) / pbn);

@@ -166,6 +166,28 @@ def test_cta_pair_kernel(pkg, oracle, cuda, bn, m, n, k, n_off, cnt, monkeypatch
     _check(y16[rows], ref16, what=f"pair fp16 bn={bn} {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("m,n,k", [(70001, 200, 96), (20000, 1000, 1056)])
+def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, bn, m, n, k, monkeypatch):
+    """Persistent pairs walking several tiles: both TMEM accumulators and the A-slot ring wrap many times (70001
+    tokens of 96-deep K give up to 7 tiles per pair, two stages each, the second a single 32-deep block)."""
+    monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
+    monkeypatch.setenv("IDOL_B200_GEMM_PAIR", "1")
+    rng = np.random.default_rng(m + n + k)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    g = torch.Generator(device=cuda).manual_seed(m + k)
+    xt = torch.randn((m, k), device=cuda, generator=g).to(torch.bfloat16)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = torch.empty((m, n), device=cuda, dtype=torch.float32)
+    pkg.gemm_into(y, xt, tiles, torch.from_numpy(b).to(cuda), n, k)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.linspace(0, m - 1, 200).astype(int), np.arange(m - 70, m)]))
+    x = xt[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    _check(y[torch.from_numpy(rows).to(cuda)].cpu().numpy(), oracle.gemm_q8(x, q8, b, n, k),
+           what=f"pair bn={bn} {m}x{n}x{k}")
+
+
 @pytest.mark.parametrize("act", [0, 1, 2, 3])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_epilogue_window_residual_activation(pkg, oracle, cuda, act, out_dtype):
