@@ -284,10 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        // The A buffer of slot s was last read by stage i - S. Its MMA has completed once full[s] completes for stage
+        // i: the producer issues stage i's copies only after that MMA's commit (empty[s]), so one wait covers both.
         for (int i = half; i < nks; i += 2) {
             const int s = i % S, u = i / S;
-            bool got = mbar_wait(&full[s], u & 1, abort_flag);
-            if (got && i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
+            const bool got = mbar_wait(&full[s], u & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
             tc_fence_after();
             dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, min(2, p.kb - (ks_begin + i) * 2),
@@ -375,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 //   * two TMEM accumulators of BN columns: the MMA warp fills accumulator lt % 2 for its lt-th tile and commits
 //     accfull; eight separate epilogue warps drain it (bias, residual, activation, stores) and report accempty, so
 //     the epilogue of one tile runs under the main loop of the next.
-// TMEM budget: 2 BN + 32 SA <= 512 columns (BN = 192 with SA = 4, BN = 128 with SA = 8).
+// TMEM budget: 2 BN + 32 SA <= 512 columns (BN = 192 with SA = 4, BN = 128 with SA = 8). With SA == S the
+// dequant warps need no wait for their A slot: the codes of stage i land only after the commit of stage i - S.
 constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the token columns each
 constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 
@@ -532,10 +534,12 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
                 const int a = i % SA;
                 bool got = mbar_wait(&cfull[s], u & 1, abort_flag);
                 if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);  // see the MMA loop
-                if (got && i >= SA) {  // A slot a was last read by stage i - SA
-                    const int r = i - SA;
-                    got = mbar_wait(&empty[r % S], (r / S) & 1, abort_flag);
-                }
+                if constexpr (SA < S) {
+                    if (got && i >= SA) {  // A slot a was last read by stage i - SA
+                        const int r = i - SA;
+                        got = mbar_wait(&empty[r % S], (r / S) & 1, abort_flag);
+                    }
+                }  // with SA == S, cfull[s] of stage i implies the commit of stage i - S (the producer waited for it)
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
                 dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, valid ? min(2, p.kb - ks * 2) : 0,
@@ -625,7 +629,7 @@ int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles
 template <bool kBF16, typename OutT>
 int dispatch_pair(int bn, const CUtensorMap& xmap, const Params& p, int pairs, int tiles_m, cudaStream_t stream) {
     if (bn == 128) return launch_pair<128, 8, 8, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
-    return launch_pair<192, 8, 4, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
+    return launch_pair<192, 4, 4, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT>
