@@ -680,15 +680,22 @@ int env_int(const char* name, int fallback) {
 
 // Token-tile width and split-K factor by M (the strategy choice). IDOL_B200_GEMM_BN and IDOL_B200_GEMM_SPLITS force
 // them for tests and sweeps.
+// Measured on B200 over the config-2 shapes: up to 64 tokens the launch is bound by streaming W, so K is split until
+// the CTAs cover the SMs; above that a split pays only when K is long (>= 32 stages) and the tiles are few, since the
+// cluster reduction costs about as much as a short main loop.
 static void choose_tiles(int device, int64_t m, int tiles_n, int stages_total, int* bn, int* splits) {
-    int b = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+    int b = m <= 16 ? 16 : m <= 32 ? 32 : m <= 128 ? 64 : 256;
     const int forced_bn = env_int("IDOL_B200_GEMM_BN", 0);
     if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) b = forced_bn;
     const int tiles = tiles_n * (int)((m + b - 1) / b);
     const int per_sm = b == 256 ? 1 : 2;
     const int slots = num_sms(device) * per_sm;
     int s = 1;
-    while (s < 8 && tiles * s * 2 <= slots && stages_total >= s * 2 * 2) s *= 2;
+    if (m <= 64) {
+        while (s < 8 && tiles * s * 2 <= slots && stages_total >= s * 2 * 2) s *= 2;
+    } else if (stages_total >= 32) {
+        while (s < 8 && tiles * s * 2 <= slots && stages_total >= s * 2 * 8) s *= 2;
+    }
     const int forced_s = env_int("IDOL_B200_GEMM_SPLITS", 0);
     if (forced_s == 1 || forced_s == 2 || forced_s == 4 || forced_s == 8) s = forced_s;
     if (s > stages_total) s = 1;
