@@ -89,8 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* kv_full = bars + 1;                 // [kStages]
     uint64_t* kv_empty = kv_full + kStages;       // [kStages]
     uint64_t* s_full = kv_empty + kStages;        // [2]
-    uint64_t* s_free = s_full + 2;                // [2]
-    uint64_t* p_full = s_free + 2;                // [2]
+    uint64_t* p_full = s_full + 2;                // [2]
     uint64_t* o_full = p_full + 2;                // [2]
     uint64_t* o_free = o_full + 2;                // [2]
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_free + 2);
@@ -110,10 +109,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&s_free[b], 128);
-            mbar_init(&p_full[b], 128);
+            mbar_init(&p_full[b], 4);  // one elected arrival per softmax warp
             mbar_init(&o_full[b], 1);
-            mbar_init(&o_free[b], 128);
+            mbar_init(&o_free[b], 4);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -157,8 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; ok && j <= nb; ++j) {
                 if (j < nb) {
                     const int s = j % kStages, b = j % 2;
+                    // S buffer b was last read by the softmax of block j - 2, which had finished (p_full) before
+                    // P V of block j - 2 was issued in the previous iteration.
                     if (!mbar_wait(&kv_full[s], (j / kStages) & 1, abort_flag)) break;
-                    if (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) / 2) & 1, abort_flag)) break;
                     tc_fence_after();
                     const uint32_t kaddr = smem_u32(ks + s * kTileBytes);
 #pragma unroll
@@ -204,16 +203,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float f = (m_acc == -INFINITY) ? 0.0f : ex2(m_acc - m_prev_blk);
 #pragma unroll
-            for (int c0 = 0; c0 < kHd; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + lane_base + kColO + bo * kHd + c0, v);
+            for (int c0 = 0; c0 < kHd; c0 += 32) {  // two halves of 32 columns, one wait each
+                uint32_t v[32];
+                tmem_ld16(tmem + lane_base + kColO + bo * kHd + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+                tmem_ld16(tmem + lane_base + kColO + bo * kHd + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                 tmem_ld_wait();
 #pragma unroll
-                for (int c = 0; c < 16; ++c) o_acc[c0 + c] = fmaf(o_acc[c0 + c], f, __uint_as_float(v[c]));
+                for (int c = 0; c < 32; ++c) o_acc[c0 + c] = fmaf(o_acc[c0 + c], f, __uint_as_float(v[c]));
             }
             m_acc = m_prev_blk;
             tc_fence_before();
-            mbar_arrive(&o_free[bo]);
+            __syncwarp();  // the warp's TMEM reads are done and fenced before lane 0 reports it
+            if (lane == 0) mbar_arrive(&o_free[bo]);
             return true;
         };
 
@@ -224,29 +225,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int valid = p.lk - j * kKTile;  // keys of this block that exist
             const uint32_t s_col = kColS + b * kKTile;
-            // Pass 1: the row maximum of the raw scores (the scale is positive, so it commutes with the max).
-            float mx = -INFINITY;
-            if (valid >= kKTile) {
+            // The whole score row in registers: eight asynchronous 16-column loads, one wait.
+            uint32_t sv[kKTile];
 #pragma unroll
-                for (int c0 = 0; c0 < kKTile; c0 += 32) {
-                    uint32_t v[32];
-                    tmem_ld16(tmem + lane_base + s_col + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
-                    tmem_ld16(tmem + lane_base + s_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-                    tmem_ld_wait();
+            for (int c0 = 0; c0 < kKTile; c0 += 16)
+                tmem_ld16(tmem + lane_base + s_col + c0, *reinterpret_cast<uint32_t(*)[16]>(sv + c0));
+            tmem_ld_wait();
+            // Row maximum of the raw scores (the scale is positive, so it commutes with the max), as four independent
+            // chains. Keys past the end exist only in the last block.
+            const bool full = valid >= kKTile;
+            if (!full) {
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(v[c]));
-                }
-            } else {
-#pragma unroll
-                for (int c0 = 0; c0 < kKTile; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + lane_base + s_col + c0, v);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int c = 0; c < 16; ++c)
-                        if (c0 + c < valid) mx = fmaxf(mx, __uint_as_float(v[c]));
-                }
+                for (int c = 0; c < kKTile; ++c)
+                    if (c >= valid) sv[c] = __float_as_uint(-INFINITY);
             }
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < kKTile; ++c) m4[c % 4] = fmaxf(m4[c % 4], __uint_as_float(sv[c]));
+            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             const float m_new = fmaxf(m_run, mx * p.scale_log2);
             const float alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_new);
             const float neg_m = -m_new;
@@ -256,31 +252,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
             }
-            // Pass 2: p = exp2(s - m), summed, packed to bf16 and stored 32 keys at a time.
-            float sum = 0.0f;
+            // p = exp2(s scale - m) on key pairs (packed FMA), summed in four independent pairs of partial sums,
+            // packed to bf16 and stored 32 keys at a time (masked keys give exp2(-inf) = 0).
+            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+            const float2 nm2 = make_float2(neg_m, neg_m);
+            float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
 #pragma unroll
             for (int c0 = 0; c0 < kKTile; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld16(tmem + lane_base + s_col + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
-                tmem_ld16(tmem + lane_base + s_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-                tmem_ld_wait();
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    float t0 = fmaf(__uint_as_float(v[c]), p.scale_log2, neg_m);
-                    float t1 = fmaf(__uint_as_float(v[c + 1]), p.scale_log2, neg_m);
-                    if (c0 + c >= valid) t0 = -INFINITY;
-                    if (c0 + c + 1 >= valid) t1 = -INFINITY;
-                    const float e0 = ex2(t0), e1 = ex2(t1);
-                    sum += e0 + e1;
-                    pk[c / 2] = pack_bf16x2(e0, e1);
+                    const float2 t = __ffma2_rn(make_float2(__uint_as_float(sv[c0 + c]), __uint_as_float(sv[c0 + c + 1])),
+                                                sc2, nm2);
+                    const float2 e = make_float2(ex2(t.x), ex2(t.y));
+                    sum2[(c / 2) % 4] = __fadd2_rn(sum2[(c / 2) % 4], e);
+                    pk[c / 2] = pack_bf16x2(e.x, e.y);
                 }
                 tmem_st16(tmem + lane_base + kColP + b * (kKTile / 2) + c0 / 2, pk);
             }
+            const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+            const float2 s4 = __fadd2_rn(s01, s23);
+            const float sum = s4.x + s4.y;
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&s_free[b]);
-            mbar_arrive(&p_full[b]);
+            __syncwarp();  // the warp's P stores (and S reads) are complete and fenced before lane 0 reports it
+            if (lane == 0) mbar_arrive(&p_full[b]);
             l_run = l_run * alpha + sum;
             m_run = m_new;
             // Fold the partial output of the previous block (its max is m_prev_blk).
