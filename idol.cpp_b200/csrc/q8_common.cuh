@@ -1,0 +1,105 @@
+// q8_common.cuh - pieces shared by the Q8_0 GEMM kernels (q8_gemm.cu: tcgen05 path for M > 16; q8_gemv.cu: the
+// streaming path for M <= 16): the launch parameters, the output epilogue (bias, residual, activation, rounding) and
+// the exact in-register dequantisation of sixteen codes.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace idol {
+namespace q8 {
+
+struct Params {
+    const uint8_t* tiles;
+    const float* bias;
+    const void* residual;
+    void* y;
+    int m, n, k, kb;
+    int row_tiles, layout_stages;  // chunk grid of the tiled layout
+    int row_begin;            // first weight row of tile 0 (the window start rounded down to 128)
+    int n_offset, n_count;    // output columns [n_offset, n_offset + n_count)
+    long long ldy, ldr;
+    int act;
+    int bias_after_round;
+    int stages_per_split, stages_total;
+};
+
+template <typename OutT>
+__device__ __forceinline__ float out_round(float v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
+    else return __half2float(__float2half_rn(v));
+}
+template <typename OutT>
+__device__ __forceinline__ OutT to_out(float v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __float2bfloat16_rn(v);
+    else return __float2half_rn(v);
+}
+template <typename OutT>
+__device__ __forceinline__ float from_out(OutT v) {
+    if constexpr (sizeof(OutT) == 4) return v;
+    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(v);
+    else return __half2float(v);
+}
+
+__device__ __forceinline__ float activate(float v, int act) {
+    switch (act) {
+        case IDOL_ACT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+        case IDOL_ACT_GELU_TANH: return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+        case IDOL_ACT_SILU: return v / (1.0f + expf(-v));
+        default: return v;
+    }
+}
+
+// Epilogue for one accumulator value: output (token m, weight row `row`).
+template <typename OutT>
+__device__ __forceinline__ void finish(const Params& p, int m, int row, float acc) {
+    if (m >= p.m || row >= p.n || row < p.n_offset || row >= p.n_offset + p.n_count) return;
+    const float b = p.bias ? p.bias[row] : 0.0f;
+    float v = p.bias_after_round ? out_round<OutT>(acc) + b : acc + b;
+    const int col = row - p.n_offset;
+    if (p.residual) v += from_out<OutT>(static_cast<const OutT*>(p.residual)[(long long)m * p.ldr + col]);
+    v = activate(v, p.act);
+    static_cast<OutT*>(p.y)[(long long)m * p.ldy + col] = to_out<OutT>(v);
+}
+
+// 16 signed codes (one uint4) times d, as 8 packed 2-element registers of the operand type.
+// Exact dequantisation in three steps: PRMT places the byte u = q + 128 into the mantissa of 32768, giving
+// f = 32896 + q exactly; one packed FMA forms f d - 32896 d = q d with a single rounding, which is exact because q d
+// has at most 19 significant bits and 32896 d = 2^7 (2^8 + 1) d at most 20; the pair is then rounded to the operand
+// type (round to nearest even), which is what tools/idol_triton.py:62,83 does to the fp32 product d * q.
+template <bool kBF16>
+__device__ __forceinline__ void dequant16(uint4 c, float2 dd, float2 ncd, uint32_t* out) {
+    const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float f0 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7504));
+        const float f1 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7514));
+        const float f2 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7524));
+        const float f3 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7534));
+        const float2 p01 = __ffma2_rn(make_float2(f0, f1), dd, ncd);
+        const float2 p23 = __ffma2_rn(make_float2(f2, f3), dd, ncd);
+        if constexpr (kBF16) {
+            out[2 * i] = pack_bf16x2(p01.x, p01.y);
+            out[2 * i + 1] = pack_bf16x2(p23.x, p23.y);
+        } else {
+            out[2 * i] = pack_f16x2(p01.x, p01.y);
+            out[2 * i + 1] = pack_f16x2(p23.x, p23.y);
+        }
+    }
+}
+
+}  // namespace q8
+
+// The streaming kernel for M <= 16 (q8_gemv.cu): the number of K splits it would use for `groups` 32-row groups and
+// `stages_total` k stages (0 when K is too long for it), and the launch.
+int q8_gemv_splits(int device, int groups, int stages_total);
+int q8_gemv(const GemmCall& c, const q8::Params& p, int splits);
+
+}  // namespace idol

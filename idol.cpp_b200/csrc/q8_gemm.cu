@@ -28,6 +28,7 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "q8_common.cuh"
 
 namespace idol {
 
@@ -35,27 +36,14 @@ IDOL_DEVICE_ERROR_READER(take_device_error_gemm)
 
 namespace {
 
+using namespace q8;
+
 constexpr int kRowsPerTile = 128;   // weight rows (output features) per CTA = TMEM lanes
 constexpr int kStageK = 64;         // k per pipeline stage: two Q8 blocks, one 128-byte swizzle row of bf16
 constexpr int kDequantWarps = 8;    // two per TMEM lane quarter: one per Q8 block of a stage
 constexpr int kThreads = 64 + 32 * kDequantWarps;  // warp 0 producer, warp 1 MMA / TMEM owner, warps 2-9 dequant
 // One stage of weights = one chunk of the tiled layout: 8192 code bytes + 512 scale bytes, one bulk copy.
 static_assert(kTileRows == kRowsPerTile && kTileK == kStageK, "the GEMM stage is the layout's chunk");
-
-struct Params {
-    const uint8_t* tiles;
-    const float* bias;
-    const void* residual;
-    void* y;
-    int m, n, k, kb;
-    int row_tiles, layout_stages;  // chunk grid of the tiled layout
-    int row_begin;            // first weight row of tile 0 (the window start rounded down to 128)
-    int n_offset, n_count;    // output columns [n_offset, n_offset + n_count)
-    long long ldy, ldr;
-    int act;
-    int bias_after_round;
-    int stages_per_split, stages_total;
-};
 
 template <int BN, int S>
 struct Config {
@@ -74,72 +62,6 @@ struct Config {
     static_assert(S * kXBytes >= BN * kRowsPerTile * 4, "split-K partial tile must fit in the X ring");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
 };
-
-template <typename OutT>
-__device__ __forceinline__ float out_round(float v) {
-    if constexpr (sizeof(OutT) == 4) return v;
-    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
-    else return __half2float(__float2half_rn(v));
-}
-template <typename OutT>
-__device__ __forceinline__ OutT to_out(float v) {
-    if constexpr (sizeof(OutT) == 4) return v;
-    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __float2bfloat16_rn(v);
-    else return __float2half_rn(v);
-}
-template <typename OutT>
-__device__ __forceinline__ float from_out(OutT v) {
-    if constexpr (sizeof(OutT) == 4) return v;
-    else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) return __bfloat162float(v);
-    else return __half2float(v);
-}
-
-__device__ __forceinline__ float activate(float v, int act) {
-    switch (act) {
-        case IDOL_ACT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-        case IDOL_ACT_GELU_TANH: return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
-        case IDOL_ACT_SILU: return v / (1.0f + expf(-v));
-        default: return v;
-    }
-}
-
-// Epilogue for one accumulator value: output (token m, weight row `row`).
-template <typename OutT>
-__device__ __forceinline__ void finish(const Params& p, int m, int row, float acc) {
-    if (m >= p.m || row >= p.n || row < p.n_offset || row >= p.n_offset + p.n_count) return;
-    const float b = p.bias ? p.bias[row] : 0.0f;
-    float v = p.bias_after_round ? out_round<OutT>(acc) + b : acc + b;
-    const int col = row - p.n_offset;
-    if (p.residual) v += from_out<OutT>(static_cast<const OutT*>(p.residual)[(long long)m * p.ldr + col]);
-    v = activate(v, p.act);
-    static_cast<OutT*>(p.y)[(long long)m * p.ldy + col] = to_out<OutT>(v);
-}
-
-// 16 signed codes (one uint4) times d, as 8 packed 2-element registers of the operand type.
-// Exact dequantisation in three steps: PRMT places the byte u = q + 128 into the mantissa of 32768, giving
-// f = 32896 + q exactly; one packed FMA forms f d - 32896 d = q d with a single rounding, which is exact because q d
-// has at most 19 significant bits and 32896 d = 2^7 (2^8 + 1) d at most 20; the pair is then rounded to the operand
-// type (round to nearest even), which is what tools/idol_triton.py:62,83 does to the fp32 product d * q.
-template <bool kBF16>
-__device__ __forceinline__ void dequant16(uint4 c, float2 dd, float2 ncd, uint32_t* out) {
-    const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float f0 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7504));
-        const float f1 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7514));
-        const float f2 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7524));
-        const float f3 = __uint_as_float(__byte_perm(w[i], 0x47000000u, 0x7534));
-        const float2 p01 = __ffma2_rn(make_float2(f0, f1), dd, ncd);
-        const float2 p23 = __ffma2_rn(make_float2(f2, f3), dd, ncd);
-        if constexpr (kBF16) {
-            out[2 * i] = pack_bf16x2(p01.x, p01.y);
-            out[2 * i + 1] = pack_bf16x2(p23.x, p23.y);
-        } else {
-            out[2 * i] = pack_f16x2(p01.x, p01.y);
-            out[2 * i + 1] = pack_f16x2(p23.x, p23.y);
-        }
-    }
-}
 
 // One warp's share of a stage: rows 32 q .. 32 q + 31 of the weight chunk at `chunk` (both 32-deep Q8 blocks, or the
 // first `blocks` of them), dequantised into TMEM columns col .. col + 31 of those lanes (lane_base folded into col).
@@ -736,6 +658,17 @@ int q8_gemm(const GemmCall& c) {
     p.act = c.act;
     p.bias_after_round = (c.flags & IDOL_EPI_BIAS_AFTER_ROUND) ? 1 : 0;
     p.stages_total = (w.k + kStageK - 1) / kStageK;
+
+    // Decode-sized batches stream W through the register-dequant kernel (IDOL_B200_GEMV=0 forces the tcgen05 path).
+    if (c.m <= 16 && env_int("IDOL_B200_GEMV", 1) != 0) {
+        const int groups = (c.n_offset + c.n - p.row_begin + 31) / 32;
+        int gemv_splits = q8_gemv_splits(w.device, groups, p.stages_total);
+        const int forced = env_int("IDOL_B200_GEMV_SPLITS", 0);  // sweeps and tests: 1, 2, 4 or 8
+        if (gemv_splits > 0 && (forced == 1 || forced == 2 || forced == 4 || forced == 8) &&
+            (p.stages_total + forced - 1) / forced <= 16)
+            gemv_splits = forced;
+        if (gemv_splits > 0) return q8_gemv(c, p, gemv_splits);
+    }
 
     const int tiles_n = (c.n_offset + c.n - p.row_begin + kRowsPerTile - 1) / kRowsPerTile;
     int bn = 0, splits = 1;

@@ -188,6 +188,42 @@ def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, bn, m, n, k, mon
            what=f"pair bn={bn} {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k", [(1, 3072, 1024), (16, 1024, 4096), (3, 14, 512), (7, 200, 1056), (16, 1000, 96),
+                                   (1, 4096, 8192), (5, 300, 16384), (16, 129, 32)])
+def test_small_m_streaming_kernel(pkg, oracle, cuda, m, n, k, monkeypatch):
+    """M <= 16 runs the register-dequant streaming kernel: ragged N (14, 129, 300 rows), K ending in one 32-deep
+    block, K splits 1-8 (8192 = 128 stages is the longest K it takes; 16384 falls back to the tcgen05 path)."""
+    rng = np.random.default_rng(m * 7 + n + k)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    ref = oracle.gemm_q8(x, q8, b, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k)
+    _check(y, ref, what=f"gemv M={m} N={n} K={k}")
+    # Deterministic (fixed reduction order) and within the same bar as the tcgen05 path.
+    assert np.array_equal(y, _gemm(pkg, cuda, x, tiles, b, n, k))
+    monkeypatch.setenv("IDOL_B200_GEMV", "0")
+    _check(_gemm(pkg, cuda, x, tiles, b, n, k), ref, what=f"tcgen05 M={m} N={n} K={k}")
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_small_m_window_residual_activation_fp16(pkg, oracle, cuda, act):
+    rng = np.random.default_rng(90 + act)
+    m, n, k = 9, 700, 640
+    n_off, cnt = 160, 400
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    res = rng.normal(0, 1, (m, cnt)).astype(np.float32)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    y = _gemm(pkg, cuda, x, tiles, b, n, k, n_off, cnt, res, act)
+    _check(y, oracle.gemm_q8(x, q8, b, n, k, n_off, cnt, res, act), what=f"gemv window act={act}")
+    x16 = x.astype(np.float16).astype(np.float32)
+    y16 = _gemm(pkg, cuda, x16, tiles, b, n, k, x_dtype=torch.float16, out_dtype=torch.float16)
+    _check(y16, oracle.gemm_q8(x16, q8, b, n, k), what=f"gemv fp16 act={act}")
+
+
 @pytest.mark.parametrize("act", [0, 1, 2, 3])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_epilogue_window_residual_activation(pkg, oracle, cuda, act, out_dtype):
