@@ -48,11 +48,29 @@ __device__ __forceinline__ float from_out(OutT v) {
     else return __half2float(v);
 }
 
+// Activations of the epilogue. SiLU is v sigmoid(v) = v / (1 + e^-v); GELU-tanh uses the identity
+// 0.5 v (1 + tanh u) = v sigmoid(2u) = v / (1 + e^-2u) with u = sqrt(2/pi) (v + 0.044715 v^3). Both run on the fast
+// base-2 exponential and approximate division intrinsics (relative error near 2^-21, far below the bf16/fp16 output
+// rounding); e^-v overflowing to +inf gives -0, the correct limit. GELU-erf keeps erff.
+template <int kAct>
+__device__ __forceinline__ float activate_t(float v) {
+    if constexpr (kAct == IDOL_ACT_GELU_ERF) {
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    } else if constexpr (kAct == IDOL_ACT_GELU_TANH) {
+        const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+        return __fdividef(v, 1.0f + __expf(-2.0f * u));
+    } else if constexpr (kAct == IDOL_ACT_SILU) {
+        return __fdividef(v, 1.0f + __expf(-v));
+    } else {
+        return v;
+    }
+}
+
 __device__ __forceinline__ float activate(float v, int act) {
     switch (act) {
-        case IDOL_ACT_GELU_ERF: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-        case IDOL_ACT_GELU_TANH: return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
-        case IDOL_ACT_SILU: return v / (1.0f + expf(-v));
+        case IDOL_ACT_GELU_ERF: return activate_t<IDOL_ACT_GELU_ERF>(v);
+        case IDOL_ACT_GELU_TANH: return activate_t<IDOL_ACT_GELU_TANH>(v);
+        case IDOL_ACT_SILU: return activate_t<IDOL_ACT_SILU>(v);
         default: return v;
     }
 }

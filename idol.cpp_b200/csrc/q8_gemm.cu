@@ -89,18 +89,17 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* chunk, int q, int l
     tmem_st_wait();
 }
 
-// Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row.
-template <typename OutT, int kCols>
-__device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
-                                            bool row_ok) {
-    if (!row_ok) return;
+// Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row, with the
+// activation fixed at compile time so the per-element loop carries no dispatch.
+template <typename OutT, int kCols, int kAct>
+__device__ __forceinline__ void finish_cols_act(const Params& p, int m, int row, const uint32_t* v, float bias) {
     const int col = row - p.n_offset;
     OutT* y = static_cast<OutT*>(p.y) + col;
     const OutT* res = static_cast<const OutT*>(p.residual);
-    const bool fast = !p.residual && p.act == IDOL_ACT_NONE && !p.bias_after_round && m + kCols <= p.m;
-    if (fast) {
+    if (!res && !p.bias_after_round && m + kCols <= p.m) {
 #pragma unroll
-        for (int j = 0; j < kCols; ++j) y[(long long)(m + j) * p.ldy] = to_out<OutT>(__uint_as_float(v[j]) + bias);
+        for (int j = 0; j < kCols; ++j)
+            y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(__uint_as_float(v[j]) + bias));
         return;
     }
 #pragma unroll
@@ -109,8 +108,19 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int row, con
         const float acc = __uint_as_float(v[j]);
         float x = p.bias_after_round ? out_round<OutT>(acc) + bias : acc + bias;
         if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
-        x = activate(x, p.act);
-        y[(long long)(m + j) * p.ldy] = to_out<OutT>(x);
+        y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
+    }
+}
+
+template <typename OutT, int kCols>
+__device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
+                                            bool row_ok) {
+    if (!row_ok) return;
+    switch (p.act) {
+        case IDOL_ACT_GELU_ERF: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_ERF>(p, m, row, v, bias); break;
+        case IDOL_ACT_GELU_TANH: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_TANH>(p, m, row, v, bias); break;
+        case IDOL_ACT_SILU: finish_cols_act<OutT, kCols, IDOL_ACT_SILU>(p, m, row, v, bias); break;
+        default: finish_cols_act<OutT, kCols, IDOL_ACT_NONE>(p, m, row, v, bias); break;
     }
 }
 
@@ -674,9 +684,13 @@ int q8_gemm(const GemmCall& c) {
     int bn = 0, splits = 1;
     choose_tiles(w.device, c.m, tiles_n, p.stages_total, &bn, &splits);
 
-    // The CTA-pair kernel (IDOL_B200_GEMM_PAIR = 1 selects it for M tiles of 128 or 256 tokens).
+    // The persistent CTA-pair kernel overlaps each tile's epilogue with the next tile's main loop, which pays when the
+    // main loop is short: measured on B200, K <= 512 with N >= 256 and M >= 4096 (the Gaussian MLP's 128->512 and
+    // 512->512 layers: 0.50 against 0.57 ms per MLP step); with longer K the single-CTA kernel is 5-15% faster.
+    // IDOL_B200_GEMM_PAIR = 1 / 0 forces it on (for 128- or 256-token tiles) / off.
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
-    const bool pair = forced_pair == 1 && bn >= 128;  // off by default until it outruns the single-CTA kernel
+    const bool pair = bn >= 128 && (forced_pair == 1 ||
+                                    (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
     if (pair) {
         const int pbn = bn >= 256 ? 192 : 128;  // two accumulators of pbn columns fit TMEM beside the A slots
         p.stages_per_split = p.stages_total;
