@@ -313,9 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the token columns each
 constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 
-template <int BN, int S, int SA>
-struct ConfigPair {
-    static constexpr int kHalf = BN / 2;
+template <int BN, int S, int SA, bool kPair>
+struct ConfigPersistent {
+    static constexpr int kHalf = kPair ? BN / 2 : BN;  // token rows this CTA loads per stage
     static constexpr int kXBytes = kHalf * 128;
     static constexpr int kStageBytes = kXBytes + kChunkBytes;
     static constexpr int kACol0 = 2 * BN;  // accumulators at columns 0 and BN, then the A slots
@@ -324,23 +324,26 @@ struct ConfigPair {
     static constexpr int kBarBytes = 8 * (3 * S + SA + 4) + 16;
     static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
     static constexpr int kSmemUsed = 1024 + S * kStageBytes + kBarBytes;
-    // At least 120 KB: one CTA per SM, so the pair's TMEM allocations never wait on a neighbour.
+    // At least 120 KB: one CTA per SM, so a TMEM allocation of 512 columns never waits on a neighbour.
     static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
     static_assert(kColsNeeded <= 512, "TMEM budget");
     static_assert(kSmemUsed <= 227 * 1024, "shared memory budget");
-    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair MMA N");
+    static_assert(BN % (kPair ? 32 : 16) == 0 && BN >= 64 && BN <= 256, "MMA N");
     static_assert(kXBytes % 1024 == 0, "each token half must stay 1024-aligned for the 128-byte swizzle");
 };
 
-struct PairSchedule {
-    int pairs_n;   // 256-row tiles along the output features
+struct PersistentSchedule {
+    int units_n;   // row units along the output features (256 rows for a pair, 128 for one CTA)
     int tiles_m;   // BN-token tiles along M
 };
 
-template <int BN, int S, int SA, bool kBF16, typename OutT>
-__global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                                       const Params p, const PairSchedule sched) {
-    using C = ConfigPair<BN, S, SA>;
+// kPair = false is the same pipeline on one CTA (cta_group::1, M = 128 rows, the whole token tile loaded locally, no
+// cluster): X and the codes of a stage land on one barrier, so the dequant warps wait once per stage.
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT>
+__global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
+    const __grid_constant__ CUtensorMap xmap, const Params p, const PersistentSchedule sched) {
+    using C = ConfigPersistent<BN, S, SA, kPair>;
+    constexpr int kRowsPerUnit = kPair ? 2 * kRowsPerTile : kRowsPerTile;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;
@@ -355,10 +358,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const uint32_t rank = cluster_ctarank();
-    const int pair_id = blockIdx.x / 2;
-    const int num_pairs = gridDim.x / 2;
-    const int total_tiles = sched.pairs_n * sched.tiles_m;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const int pair_id = kPair ? blockIdx.x / 2 : blockIdx.x;   // the unit (pair or single CTA) this CTA belongs to
+    const int num_pairs = kPair ? gridDim.x / 2 : gridDim.x;
+    const int total_tiles = sched.units_n * sched.tiles_m;
     const int nks = p.stages_total;
 
     if (tid == 0) {
@@ -367,21 +370,27 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             mbar_init(&cfull[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < SA; ++a) mbar_init(&afull[a], kDequantWarps);  // one per dequant warp of the group, both CTAs
+        // One arrival per dequant warp of the stage's group (four per CTA), and per epilogue warp, of every CTA.
+        for (int a = 0; a < SA; ++a) mbar_init(&afull[a], (kPair ? 2 : 1) * (kDequantWarps / 2));
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accfull[b], 1);
-            mbar_init(&accempty[b], 2 * kEpilogueWarps);  // one arrival per epilogue warp of either CTA
+            mbar_init(&accempty[b], (kPair ? 2 : 1) * kEpilogueWarps);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc_pair(tmem_holder, C::kTmemCols);
-        tmem_relinquish_pair();
+        if constexpr (kPair) {
+            tmem_alloc_pair(tmem_holder, C::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_holder, C::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();  // the peer's barriers exist before anything arrives on them
+    if constexpr (kPair) cluster_sync();  // the peer's barriers exist before anything arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
@@ -391,37 +400,38 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             int i = 0;  // stage counter across tiles (= stages loaded so far)
             bool ok = true;
             for (int t = pair_id; t < total_tiles && ok; t += num_pairs) {
-                const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
+                const int row0 = p.row_begin + (t % sched.units_n) * kRowsPerUnit + (int)rank * kRowsPerTile;
                 const int t128 = row0 / kRowsPerTile;
                 const bool valid = t128 < p.row_tiles;  // the pair's second tile can fall past N
-                const int m0 = (t / sched.pairs_n) * BN;
+                const int m0 = (t / sched.units_n) * BN;
                 for (int ks = 0; ks < nks; ++ks, ++i) {
                     const int s = i % S, u = i / S;
                     if (i >= S && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) { ok = false; break; }
-                    const int b0 = ks * 2;
-                    const int nb = min(2, p.kb - b0);
-                    if (rank == 0) mbar_arrive_expect_tx(&xfull[s], 2 * C::kXBytes);
-                    tma_load_2d_pair(xs + s * C::kXBytes, &xmap, ks * kStageK, m0 + (int)rank * C::kHalf,
-                                     map_to_rank(smem_u32(&xfull[s]), 0));
-                    (void)nb;
-                    mbar_arrive_expect_tx(&cfull[s], valid ? kChunkBytes : 0);
-                    if (valid)
-                        bulk_load(ws + s * kChunkBytes,
-                                  p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes, kChunkBytes,
-                                  &cfull[s]);
+                    const uint8_t* chunk = p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes;
+                    if constexpr (kPair) {
+                        if (rank == 0) mbar_arrive_expect_tx(&xfull[s], 2 * C::kXBytes);
+                        tma_load_2d_pair(xs + s * C::kXBytes, &xmap, ks * kStageK, m0 + (int)rank * C::kHalf,
+                                         map_to_rank(smem_u32(&xfull[s]), 0));
+                        mbar_arrive_expect_tx(&cfull[s], valid ? kChunkBytes : 0);
+                        if (valid) bulk_load(ws + s * kChunkBytes, chunk, kChunkBytes, &cfull[s]);
+                    } else {
+                        mbar_arrive_expect_tx(&xfull[s], C::kXBytes + kChunkBytes);
+                        tma_load_2d(xs + s * C::kXBytes, &xmap, ks * kStageK, m0, &xfull[s]);
+                        bulk_load(ws + s * kChunkBytes, chunk, kChunkBytes, &xfull[s]);
+                    }
                 }
             }
             // The last loads into each stage have landed before the CTA can leave (see mbar_drain): this CTA's codes
             // on cfull; both CTAs' token halves on the even CTA's xfull (the odd CTA's copies count there too, and
             // the final cluster barrier keeps the odd CTA until the even one has drained).
             for (int j = i - S > 0 ? i - S : 0; j < i; ++j) {
-                mbar_drain(&cfull[j % S], (j / S) & 1);
+                if constexpr (kPair) mbar_drain(&cfull[j % S], (j / S) & 1);
                 if (rank == 0) mbar_drain(&xfull[j % S], (j / S) & 1);
             }
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = make_idesc_f16(2 * kRowsPerTile, BN, kBF16);
+            const uint32_t idesc = make_idesc_f16(kPair ? 2 * kRowsPerTile : kRowsPerTile, BN, kBF16);
             int i = 0, lt = 0;
             bool ok = true;
             for (int t = pair_id; t < total_tiles && ok; t += num_pairs, ++lt) {
@@ -441,13 +451,21 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
                     const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
                     const uint32_t a0 = tmem + C::kACol0 + a * 32;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        if (j < 2 || two_blocks)
-                            mma_ts_pair(acc, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
-                                        (ks > 0 || j > 0) ? 1u : 0u);
-                    mma_commit_pair(&empty[s], 0x3);
+                    for (int j = 0; j < 4; ++j) {
+                        if (j < 2 || two_blocks) {
+                            if constexpr (kPair)
+                                mma_ts_pair(acc, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
+                                            (ks > 0 || j > 0) ? 1u : 0u);
+                            else
+                                mma_ts(acc, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
+                                       (ks > 0 || j > 0) ? 1u : 0u);
+                        }
+                    }
+                    if constexpr (kPair) mma_commit_pair(&empty[s], 0x3);
+                    else mma_commit(&empty[s]);
                 }
-                mma_commit_pair(&accfull[b], 0x3);
+                if constexpr (kPair) mma_commit_pair(&accfull[b], 0x3);
+                else mma_commit(&accfull[b]);
             }
         }
     } else if (warp < 2 + kDequantWarps) {
@@ -458,14 +476,16 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
         int i = 0;
         bool ok = true;
         for (int t = pair_id; t < total_tiles && ok; t += num_pairs) {
-            const int row0 = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile;
+            const int row0 = p.row_begin + (t % sched.units_n) * kRowsPerUnit + (int)rank * kRowsPerTile;
             const bool valid = row0 / kRowsPerTile < p.row_tiles;
             for (int ks = 0; ks < nks; ++ks, ++i) {
                 if ((i & 1) != half) continue;
                 const int s = i % S, u = i / S;
                 const int a = i % SA;
-                bool got = mbar_wait(&cfull[s], u & 1, abort_flag);
-                if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);  // see the MMA loop
+                // A pair: this CTA's codes (cfull), and on the even CTA both token halves (xfull, see the MMA loop).
+                // One CTA: codes and tokens land together on xfull.
+                bool got = kPair ? mbar_wait(&cfull[s], u & 1, abort_flag) : true;
+                if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);
                 if constexpr (SA < S) {
                     if (got && i >= SA) {  // A slot a was last read by stage i - SA
                         const int r = i - SA;
@@ -497,9 +517,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&accfull[b], (lt >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            const int row = p.row_begin + (t % sched.pairs_n) * (2 * kRowsPerTile) + (int)rank * kRowsPerTile +
-                            32 * q + lane;
-            const int m0 = (t / sched.pairs_n) * BN;
+            const int row = p.row_begin + (t % sched.units_n) * kRowsPerUnit + (int)rank * kRowsPerTile + 32 * q + lane;
+            const int m0 = (t / sched.units_n) * BN;
             const bool row_ok = row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
             const int c_begin = half * kHalfCols;
@@ -520,17 +539,18 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_pair_kernel(const __g
     }
 
     __syncthreads();
-    cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers or read its TMEM
+    if constexpr (kPair) cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc_pair(tmem, C::kTmemCols);
+        if constexpr (kPair) tmem_dealloc_pair(tmem, C::kTmemCols);
+        else tmem_dealloc(tmem, C::kTmemCols);
     }
 }
 
-template <int BN, int S, int SA, bool kBF16, typename OutT>
-int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles_m, cudaStream_t stream) {
-    using C = ConfigPair<BN, S, SA>;
-    auto kern = q8_gemm_pair_kernel<BN, S, SA, kBF16, OutT>;
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT>
+int launch_persistent(const CUtensorMap& xmap, const Params& p, int units_n, int tiles_m, cudaStream_t stream) {
+    using C = ConfigPersistent<BN, S, SA, kPair>;
+    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT>;
     static unsigned long long configured = 0;
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -538,12 +558,12 @@ int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles
         IDOL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
         configured |= 1ull << (dev & 63);
     }
-    const int total = pairs_n * tiles_m;
-    const int max_pairs = num_sms(dev) / 2;
-    const int grid_pairs = total < max_pairs ? total : max_pairs;
-    PairSchedule sched = {pairs_n, tiles_m};
+    const int total = units_n * tiles_m;
+    const int max_units = kPair ? num_sms(dev) / 2 : num_sms(dev);
+    const int grid_units = total < max_units ? total : max_units;
+    PersistentSchedule sched = {units_n, tiles_m};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * grid_pairs, 1, 1);
+    cfg.gridDim = dim3((kPair ? 2 : 1) * grid_units, 1, 1);
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = stream;
@@ -553,15 +573,18 @@ int launch_pair(const CUtensorMap& xmap, const Params& p, int pairs_n, int tiles
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = kPair ? 1 : 0;
     IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, p, sched));
     return IDOL_OK;
 }
 
+// kind 0: CTA pair, 128- or 192-token tiles; kind 1: one CTA, 192-token tiles.
 template <bool kBF16, typename OutT>
-int dispatch_pair(int bn, const CUtensorMap& xmap, const Params& p, int pairs, int tiles_m, cudaStream_t stream) {
-    if (bn == 128) return launch_pair<128, 8, 8, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
-    return launch_pair<192, 4, 4, kBF16, OutT>(xmap, p, pairs, tiles_m, stream);
+int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const Params& p, int units, int tiles_m,
+                        cudaStream_t stream) {
+    if (kind == 1) return launch_persistent<192, 6, 4, false, kBF16, OutT>(xmap, p, units, tiles_m, stream);
+    if (bn == 128) return launch_persistent<128, 8, 8, true, kBF16, OutT>(xmap, p, units, tiles_m, stream);
+    return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, p, units, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT>
@@ -691,27 +714,32 @@ int q8_gemm(const GemmCall& c) {
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
     const bool pair = bn >= 128 && (forced_pair == 1 ||
                                     (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
-    if (pair) {
-        const int pbn = bn >= 256 ? 192 : 128;  // two accumulators of pbn columns fit TMEM beside the A slots
+    // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator): IDOL_B200_GEMM_PERSIST = 1.
+    const bool persist1 = !pair && bn >= 256 && env_int("IDOL_B200_GEMM_PERSIST", 0) == 1;
+    if (pair || persist1) {
+        const int kind = pair ? 0 : 1;
+        const int pbn = kind == 1 ? 192 : bn >= 256 ? 192 : 128;  // two accumulators fit TMEM beside the A slots
+        const int unit_rows = kind == 0 ? 2 * kRowsPerTile : kRowsPerTile;
         p.stages_per_split = p.stages_total;
-        const int pairs = (c.n_offset + c.n - p.row_begin + 2 * kRowsPerTile - 1) / (2 * kRowsPerTile);
+        const int units = (c.n_offset + c.n - p.row_begin + unit_rows - 1) / unit_rows;
         const int tiles_m = (int)((c.m + pbn - 1) / pbn);
-        if (tiles_m > 65535) return fail(IDOL_ERR_INVALID, "q8_gemm: m too large for one launch (split the batch)");
+        if ((long long)units * tiles_m > 0x7fffffffLL)
+            return fail(IDOL_ERR_INVALID, "q8_gemm: m too large for one launch (split the batch)");
         CUtensorMap xmap;
         const int rc = encode_tmap_2d(&xmap, c.x_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                      c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK, pbn / 2,
-                                      CU_TENSOR_MAP_SWIZZLE_128B);
+                                      c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK,
+                                      kind == 0 ? pbn / 2 : pbn, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc != IDOL_OK) return rc;
         const bool bf16 = c.x_dtype == IDOL_BF16;
         if (c.y_dtype == IDOL_F32)
-            return bf16 ? dispatch_pair<true, float>(pbn, xmap, p, pairs, tiles_m, c.stream)
-                        : dispatch_pair<false, float>(pbn, xmap, p, pairs, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, p, units, tiles_m, c.stream)
+                        : dispatch_persistent<false, float>(kind, pbn, xmap, p, units, tiles_m, c.stream);
         if (c.y_dtype == IDOL_BF16)
-            return bf16 ? dispatch_pair<true, __nv_bfloat16>(pbn, xmap, p, pairs, tiles_m, c.stream)
-                        : dispatch_pair<false, __nv_bfloat16>(pbn, xmap, p, pairs, tiles_m, c.stream);
-        return bf16 ? dispatch_pair<true, __half>(pbn, xmap, p, pairs, tiles_m, c.stream)
-                    : dispatch_pair<false, __half>(pbn, xmap, p, pairs, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, __nv_bfloat16>(kind, pbn, xmap, p, units, tiles_m, c.stream)
+                        : dispatch_persistent<false, __nv_bfloat16>(kind, pbn, xmap, p, units, tiles_m, c.stream);
+        return bf16 ? dispatch_persistent<true, __half>(kind, pbn, xmap, p, units, tiles_m, c.stream)
+                    : dispatch_persistent<false, __half>(kind, pbn, xmap, p, units, tiles_m, c.stream);
     }
     p.stages_per_split = (p.stages_total + splits - 1) / splits;
     splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // every split gets >= 1 stage

@@ -141,15 +141,20 @@ def test_every_tile_width_and_split(pkg, oracle, cuda, bn, splits, monkeypatch):
     _check(y, oracle.gemm_q8(x, q8, b, n, k), what=f"bn={bn} splits={splits}")
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+PERSISTENT = [("pair", 128, "IDOL_B200_GEMM_PAIR"), ("pair", 256, "IDOL_B200_GEMM_PAIR"),
+              ("single", 256, "IDOL_B200_GEMM_PERSIST")]
+
+
+@pytest.mark.parametrize("kind,bn,env", PERSISTENT)
 @pytest.mark.parametrize("m,n,k,n_off,cnt", [(300, 200, 1056, 0, 200), (4097, 71, 256, 0, 71),
                                              (1000, 600, 512, 64, 500), (257, 1024, 4096, 0, 1024),
                                              (129, 384, 96, 128, 200)])
-def test_cta_pair_kernel(pkg, oracle, cuda, bn, m, n, k, n_off, cnt, monkeypatch):
-    """The cta_group::2 kernel: ragged M and N (odd tile counts leave the last pair's second CTA idle), windows,
-    K ending in a single 32-deep block, and a residual with GELU."""
+def test_cta_pair_kernel(pkg, oracle, cuda, kind, bn, env, m, n, k, n_off, cnt, monkeypatch):
+    """The persistent kernels (cta_group::2 pair; one CTA with a double-buffered accumulator): ragged M and N (odd
+    tile counts leave the last pair's second CTA idle), windows, K ending in a single 32-deep block, and a residual
+    with GELU."""
     monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
-    monkeypatch.setenv("IDOL_B200_GEMM_PAIR", "1")
+    monkeypatch.setenv(env, "1")
     rng = np.random.default_rng(m + n + k + bn)
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
@@ -159,20 +164,20 @@ def test_cta_pair_kernel(pkg, oracle, cuda, bn, m, n, k, n_off, cnt, monkeypatch
     y = _gemm(pkg, cuda, x, tiles, b, n, k, n_off, cnt, res, act=1)
     rows = np.unique(np.linspace(0, m - 1, min(m, 64)).astype(int))
     ref = oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], 1)
-    _check(y[rows], ref, what=f"pair bn={bn} {m}x{n}x{k} window {n_off}+{cnt}")
+    _check(y[rows], ref, what=f"{kind} bn={bn} {m}x{n}x{k} window {n_off}+{cnt}")
     y16 = _gemm(pkg, cuda, x.astype(np.float16).astype(np.float32), tiles, b, n, k, x_dtype=torch.float16,
                 out_dtype=torch.float16)
     ref16 = oracle.gemm_q8(x[rows].astype(np.float16).astype(np.float32), q8, b, n, k)
-    _check(y16[rows], ref16, what=f"pair fp16 bn={bn} {m}x{n}x{k}")
+    _check(y16[rows], ref16, what=f"{kind} fp16 bn={bn} {m}x{n}x{k}")
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("kind,bn,env", PERSISTENT)
 @pytest.mark.parametrize("m,n,k", [(70001, 200, 96), (20000, 1000, 1056)])
-def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, bn, m, n, k, monkeypatch):
-    """Persistent pairs walking several tiles: both TMEM accumulators and the A-slot ring wrap many times (70001
+def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, kind, bn, env, m, n, k, monkeypatch):
+    """Persistent CTAs walking several tiles: both TMEM accumulators and the A-slot ring wrap many times (70001
     tokens of 96-deep K give up to 7 tiles per pair, two stages each, the second a single 32-deep block)."""
     monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
-    monkeypatch.setenv("IDOL_B200_GEMM_PAIR", "1")
+    monkeypatch.setenv(env, "1")
     rng = np.random.default_rng(m + n + k)
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     b = rng.normal(0, 0.5, n).astype(np.float32)
@@ -185,7 +190,7 @@ def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, bn, m, n, k, mon
     rows = np.unique(np.concatenate([np.linspace(0, m - 1, 200).astype(int), np.arange(m - 70, m)]))
     x = xt[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
     _check(y[torch.from_numpy(rows).to(cuda)].cpu().numpy(), oracle.gemm_q8(x, q8, b, n, k),
-           what=f"pair bn={bn} {m}x{n}x{k}")
+           what=f"{kind} bn={bn} {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 3072, 1024), (16, 1024, 4096), (3, 14, 512), (7, 200, 1056), (16, 1000, 96),
