@@ -5,14 +5,18 @@
 // pass qkv, kv and kv + D). The reference materialises a full score row per query; this kernel streams keys in blocks
 // of 128 with an online softmax, so nothing of size L x L exists anywhere.
 //
-// One CTA per (128 queries, head, image). Warp roles:
-//   warp 0      : TMA producer - the Q tile once, then K and V tiles of 128 keys into a 3-stage ring;
-//   warp 1      : TMEM owner and MMA issuer - S_j = Q K_j^T (tcgen05 SS, fp32 in TMEM, double-buffered), then
-//                 O_j = P_j V_j (tcgen05 TS: P_j bf16 read from TMEM as the A operand, V_j from shared memory as an
-//                 MN-major B operand) into a double-buffered partial-output region of TMEM;
-//   warps 2-5   : softmax - thread r owns query row r (= TMEM lane r): reads its S row, updates the running max and
-//                 sum, writes P_j (bf16) to TMEM, and folds each partial O_j into a register accumulator with the
-//                 exp2(m_old - m_new) correction; at the end divides by the sum and stores bf16.
+// One CTA per (256 queries = two query tiles t of 128, head, image). Warp roles:
+//   warp 0      : TMA producer - both Q tiles once, then K and V tiles of 128 keys into a 3-stage ring (each K/V
+//                 tile serves both query tiles);
+//   warp 1      : TMEM owner and MMA issuer - S_t,j = Q_t K_j^T (tcgen05 SS, fp32 in TMEM), then
+//                 O_t += P_t,j V_j (tcgen05 TS: P_t,j bf16 read from TMEM as the A operand, V_j from shared memory as
+//                 an MN-major B operand, fp32 O_t accumulated in TMEM); it interleaves the two tiles so that one
+//                 tile's softmax runs while the tensor pipe works for the other;
+//   warps 2-5 / 6-9 : the softmax warpgroups of tiles 0 / 1 - thread r owns query row r of its tile (= TMEM lane r):
+//                 loads its S row (then frees the S buffer), updates the running max and sum, writes P (bf16) to TMEM;
+//                 O and the sum are rescaled only when the row maximum grows by more than 2^8 over the one in use
+//                 (P stays <= 256, exact in bf16 range, and the final O / sum cancels the stale maximum), so O stays
+//                 in TMEM with no per-block fold; at the end the row is divided by its sum and stored as bf16.
 // The same 128-byte-swizzled K/V tile layout serves as the K-major B operand of Q K^T and the MN-major B operand of
 // P V. Every wait is bounded (ptx.cuh); a timeout raises the sticky device error and the CTA winds down.
 #include <cuda_bf16.h>
@@ -26,18 +30,20 @@ IDOL_DEVICE_ERROR_READER(take_device_error_attention)
 
 namespace {
 
-constexpr int kQTile = 128;    // queries per CTA (TMEM lanes)
+constexpr int kQTile = 128;    // queries per query tile (TMEM lanes)
+constexpr int kQTiles = 2;     // query tiles per CTA, one softmax warpgroup each
 constexpr int kKTile = 128;    // keys per block
 constexpr int kHd = 64;        // head dim (128 bytes of bf16: one swizzle row)
 constexpr int kStages = 3;     // K/V ring
-constexpr int kThreads = 192;
-constexpr int kTileBytes = kKTile * kHd * 2;  // 16 KB (Q tile has the same size)
-// TMEM columns: S[0] 0-127, S[1] 128-255, P[0] 256-319, P[1] 320-383, O[0] 384-447, O[1] 448-511.
-constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
+constexpr int kThreads = 64 + 128 * kQTiles;  // producer warp, MMA warp, four softmax warps per query tile
+constexpr int kTileBytes = kKTile * kHd * 2;  // 16 KB (a Q tile has the same size)
+// TMEM columns of query tile t: S at 256 t + 0..127, P (bf16 pairs) at 256 t + 128..191, O at 256 t + 192..255.
+constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kColTile = 256;
 constexpr int kTmemCols = 512;
-constexpr int kSmemBytes = 1024 + kTileBytes * (1 + 2 * kStages) + 256;
+constexpr int kSmemBytes = 1024 + kTileBytes * (kQTiles + 2 * kStages) + 256;
 // Pad to keep one CTA per SM: the TMEM allocation takes all 512 columns.
 constexpr int kSmemLaunch = kSmemBytes < 120 * 1024 ? 120 * 1024 : kSmemBytes;
+constexpr float kRescaleLog2 = 8.0f;  // rescale O and the sum once the row max exceeds the one in use by 2^8
 
 struct AttnParams {
     void* out;
@@ -76,27 +82,29 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// Ten warps leave three on two of the four schedulers, whose register files hold 16K registers each: at most 168 per
+// thread (ptxas keeps the score row in registers with a small spill).
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap, const AttnParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint8_t* qs = smem;
-    uint8_t* ks = qs + kTileBytes;
+    uint8_t* qs = smem;                                   // [kQTiles] Q tiles
+    uint8_t* ks = qs + kQTiles * kTileBytes;
     uint8_t* vs = ks + kStages * kTileBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kStages * kTileBytes);
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;                 // [kStages]
     uint64_t* kv_empty = kv_full + kStages;       // [kStages]
-    uint64_t* s_full = kv_empty + kStages;        // [2]
-    uint64_t* p_full = s_full + 2;                // [2]
-    uint64_t* o_full = p_full + 2;                // [2]
-    uint64_t* o_free = o_full + 2;                // [2]
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_free + 2);
+    uint64_t* s_full = kv_empty + kStages;        // [kQTiles] S_t,j is in TMEM
+    uint64_t* s_free = s_full + kQTiles;          // [kQTiles] the softmax of tile t has read S_t,j
+    uint64_t* p_full = s_free + kQTiles;          // [kQTiles] P_t,j is in TMEM (O_t rescaled if it had to be)
+    uint64_t* o_full = p_full + kQTiles;          // [kQTiles] O_t += P_t,j V_j has completed
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_full + kQTiles);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int q0 = blockIdx.x * kQTile;
+    const int q0 = blockIdx.x * (kQTile * kQTiles);
     const int h = blockIdx.y;
     const int img = blockIdx.z;
     const int nb = (p.lk + kKTile - 1) / kKTile;
@@ -107,11 +115,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&s_full[b], 1);
-            mbar_init(&p_full[b], 4);  // one elected arrival per softmax warp
-            mbar_init(&o_full[b], 1);
-            mbar_init(&o_free[b], 4);
+        for (int t = 0; t < kQTiles; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&s_free[t], 4);  // one elected arrival per softmax warp of the tile
+            mbar_init(&p_full[t], 4);
+            mbar_init(&o_full[t], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -130,8 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tmap(&qmap);
             prefetch_tmap(&kmap);
             prefetch_tmap(&vmap);
-            mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_3d(qs, &qmap, h * kHd, q0, img, q_full);
+            mbar_arrive_expect_tx(q_full, kQTiles * kTileBytes);
+            for (int t = 0; t < kQTiles; ++t)
+                tma_load_3d(qs + t * kTileBytes, &qmap, h * kHd, q0 + t * kQTile, img, q_full);
             int issued = 0;
             for (int j = 0; j < nb; ++j) {
                 const int s = j % kStages, u = j / kStages;
@@ -150,91 +159,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_qk = make_idesc_f16(kQTile, kKTile, true);
             const uint32_t idesc_pv = make_idesc_f16(kQTile, kHd, true) | (1u << 16);  // B (V) is MN-major
-            bool ok = mbar_wait(q_full, 0, abort_flag);
-            const uint32_t qaddr = smem_u32(qs);
-            for (int j = 0; ok && j <= nb; ++j) {
-                if (j < nb) {
-                    const int s = j % kStages, b = j % 2;
-                    // S buffer b was last read by the softmax of block j - 2, which had finished (p_full) before
-                    // P V of block j - 2 was issued in the previous iteration.
-                    if (!mbar_wait(&kv_full[s], (j / kStages) & 1, abort_flag)) break;
-                    tc_fence_after();
-                    const uint32_t kaddr = smem_u32(ks + s * kTileBytes);
+            // S_t,j = Q_t K_j^T into tile t's S columns.
+            auto issue_s = [&](int t, int j) {
+                const uint32_t qaddr = smem_u32(qs + t * kTileBytes);
+                const uint32_t kaddr = smem_u32(ks + (j % kStages) * kTileBytes);
 #pragma unroll
-                    for (int kk = 0; kk < kHd / 16; ++kk)
-                        mma_ss(tmem + kColS + b * kKTile, make_sdesc_sw128(qaddr + kk * 32),
-                               make_sdesc_sw128(kaddr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
-                    mma_commit(&s_full[b]);
-                }
-                if (j >= 1) {
-                    const int jp = j - 1, bp = jp % 2, sp = jp % kStages;
-                    if (!mbar_wait(&p_full[bp], (jp / 2) & 1, abort_flag)) break;
-                    if (jp >= 2 && !mbar_wait(&o_free[bp], ((jp - 2) / 2) & 1, abort_flag)) break;
-                    tc_fence_after();
-                    const uint32_t vaddr = smem_u32(vs + sp * kTileBytes);
+                for (int kk = 0; kk < kHd / 16; ++kk)
+                    mma_ss(tmem + t * kColTile + kColS, make_sdesc_sw128(qaddr + kk * 32),
+                           make_sdesc_sw128(kaddr + kk * 32), idesc_qk, kk > 0 ? 1u : 0u);
+                mma_commit(&s_full[t]);
+            };
+            // O_t (+)= P_t,j V_j (the first block overwrites O_t).
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t vaddr = smem_u32(vs + (j % kStages) * kTileBytes);
 #pragma unroll
-                    for (int kk = 0; kk < kKTile / 16; ++kk)
-                        mma_ts(tmem + kColO + bp * kHd, tmem + kColP + bp * (kKTile / 2) + kk * 8,
-                               make_sdesc_sw128_mn(vaddr + kk * 2048), idesc_pv, kk > 0 ? 1u : 0u);
-                    mma_commit(&o_full[bp]);
-                    mma_commit(&kv_empty[sp]);
+                for (int kk = 0; kk < kKTile / 16; ++kk)
+                    mma_ts(tmem + t * kColTile + kColO, tmem + t * kColTile + kColP + kk * 8,
+                           make_sdesc_sw128_mn(vaddr + kk * 2048), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&o_full[t]);
+            };
+            bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&kv_full[0], 0, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                for (int t = 0; t < kQTiles; ++t) issue_s(t, 0);
+            }
+            // Block j: per tile, S of block j + 1 (once the softmax has read S of block j) then P V of block j (once P
+            // is written); the K/V stage of block j is released after both tiles' P V.
+            for (int j = 0; ok && j < nb; ++j) {
+                for (int t = 0; t < kQTiles && ok; ++t) {
+                    if (j + 1 < nb) {
+                        if (t == 0 && !mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        if (!mbar_wait(&s_free[t], j & 1, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        issue_s(t, j + 1);
+                    }
+                    if (!mbar_wait(&p_full[t], j & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv(t, j);
                 }
+                if (ok) mma_commit(&kv_empty[j % kStages]);
             }
         }
     } else {
-        // Softmax warpgroup: warp w reads TMEM lanes [32 (w % 4), +32); thread = query row.
+        // Softmax warpgroup t: warp w reads TMEM lanes [32 (w % 4), +32) of tile t; thread = query row.
+        const int t = (warp - 2) / 4;
         const int q = warp % 4;
         const int r = 32 * q + lane;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        float o_acc[kHd];
-#pragma unroll
-        for (int c = 0; c < kHd; ++c) o_acc[c] = 0.0f;
-        float m_run = -INFINITY;   // running max (log2 domain) after the latest block
-        float m_acc = -INFINITY;   // the max o_acc is scaled to
-        float m_prev_blk = -INFINITY;
+        const uint32_t tt = tmem + lane_base + (uint32_t)(t * kColTile);
+        float m_used = -INFINITY;  // the maximum (log2 domain) P and O are scaled to
         float l_run = 0.0f;
         bool ok = true;
-
-        auto fold = [&](int jo) {
-            // O_jo = P_jo V_jo is in TMEM buffer jo % 2, scaled to m of block jo (passed in m_prev_blk).
-            const int bo = jo % 2;
-            bool got = mbar_wait(&o_full[bo], (jo / 2) & 1, abort_flag);
-            if (!__all_sync(0xffffffffu, got)) return false;
-            tc_fence_after();
-            const float f = (m_acc == -INFINITY) ? 0.0f : ex2(m_acc - m_prev_blk);
-#pragma unroll
-            for (int c0 = 0; c0 < kHd; c0 += 32) {  // two halves of 32 columns, one wait each
-                uint32_t v[32];
-                tmem_ld16(tmem + lane_base + kColO + bo * kHd + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
-                tmem_ld16(tmem + lane_base + kColO + bo * kHd + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-                tmem_ld_wait();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) o_acc[c0 + c] = fmaf(o_acc[c0 + c], f, __uint_as_float(v[c]));
-            }
-            m_acc = m_prev_blk;
-            tc_fence_before();
-            __syncwarp();  // the warp's TMEM reads are done and fenced before lane 0 reports it
-            if (lane == 0) mbar_arrive(&o_free[bo]);
-            return true;
-        };
-
         for (int j = 0; j < nb && ok; ++j) {
-            const int b = j % 2;
-            bool got = mbar_wait(&s_full[b], (j / 2) & 1, abort_flag);
+            bool got = mbar_wait(&s_full[t], j & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
             tc_fence_after();
-            const int valid = p.lk - j * kKTile;  // keys of this block that exist
-            const uint32_t s_col = kColS + b * kKTile;
-            // The whole score row in registers: eight asynchronous 16-column loads, one wait.
+            // The whole score row in registers (eight asynchronous 16-column loads, one wait), then the S buffer is
+            // free for the next block's Q K^T while this block's exponentials are computed.
             uint32_t sv[kKTile];
 #pragma unroll
             for (int c0 = 0; c0 < kKTile; c0 += 16)
-                tmem_ld16(tmem + lane_base + s_col + c0, *reinterpret_cast<uint32_t(*)[16]>(sv + c0));
+                tmem_ld16(tt + kColS + c0, *reinterpret_cast<uint32_t(*)[16]>(sv + c0));
             tmem_ld_wait();
-            // Row maximum of the raw scores (the scale is positive, so it commutes with the max), as four independent
-            // chains. Keys past the end exist only in the last block.
-            const bool full = valid >= kKTile;
-            if (!full) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[t]);
+            // Keys past the end exist only in the last block.
+            const int valid = p.lk - j * kKTile;
+            if (valid < kKTile) {
 #pragma unroll
                 for (int c = 0; c < kKTile; ++c)
                     if (c >= valid) sv[c] = __float_as_uint(-INFINITY);
@@ -242,20 +237,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int c = 0; c < kKTile; ++c) m4[c % 4] = fmaxf(m4[c % 4], __uint_as_float(sv[c]));
-            const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-            const float m_new = fmaxf(m_run, mx * p.scale_log2);
-            const float alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_new);
-            const float neg_m = -m_new;
-            // P_j goes to TMEM buffer b once P V of block j - 2 (which read that buffer) has completed.
-            if (j >= 2) {
-                got = mbar_wait(&o_full[b], ((j - 2) / 2) & 1, abort_flag);
+            const float m_blk = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
+            // Lazy rescaling: keep the maximum in use unless this block's exceeds it by more than 2^8.
+            float alpha = 1.0f;
+            bool rescale = false;
+            if (m_used == -INFINITY) {
+                m_used = m_blk;  // first block: O is written, not accumulated
+            } else if (m_blk > m_used + kRescaleLog2) {
+                alpha = ex2(m_used - m_blk);
+                m_used = m_blk;
+                rescale = true;
+            }
+            // P_t,j and a rescaled O_t go to TMEM only after P V of block j - 1 has completed.
+            if (j >= 1) {
+                got = mbar_wait(&o_full[t], (j - 1) & 1, abort_flag);
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
+                if (__any_sync(0xffffffffu, rescale)) {  // tcgen05.ld/st are warp-collective: alpha = 1 elsewhere
+#pragma unroll
+                    for (int c0 = 0; c0 < kHd; c0 += 32) {
+                        uint32_t o[32];
+                        tmem_ld16(tt + kColO + c0, *reinterpret_cast<uint32_t(*)[16]>(o));
+                        tmem_ld16(tt + kColO + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16));
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tmem_st16(tt + kColO + c0, *reinterpret_cast<uint32_t(*)[16]>(o));
+                        tmem_st16(tt + kColO + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(o + 16));
+                    }
+                }
             }
             // p = exp2(s scale - m) on key pairs (packed FMA), summed in four independent pairs of partial sums,
             // packed to bf16 and stored 32 keys at a time (masked keys give exp2(-inf) = 0).
             const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-            const float2 nm2 = make_float2(neg_m, neg_m);
+            const float2 nm2 = make_float2(-m_used, -m_used);
             float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
 #pragma unroll
@@ -263,43 +278,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    const float2 t = __ffma2_rn(make_float2(__uint_as_float(sv[c0 + c]), __uint_as_float(sv[c0 + c + 1])),
-                                                sc2, nm2);
-                    const float2 e = make_float2(ex2(t.x), ex2(t.y));
+                    const float2 x2 = __ffma2_rn(make_float2(__uint_as_float(sv[c0 + c]), __uint_as_float(sv[c0 + c + 1])),
+                                                 sc2, nm2);
+                    const float2 e = make_float2(ex2(x2.x), ex2(x2.y));
                     sum2[(c / 2) % 4] = __fadd2_rn(sum2[(c / 2) % 4], e);
                     pk[c / 2] = pack_bf16x2(e.x, e.y);
                 }
-                tmem_st16(tmem + lane_base + kColP + b * (kKTile / 2) + c0 / 2, pk);
+                tmem_st16(tt + kColP + c0 / 2, pk);
             }
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
             const float2 s4 = __fadd2_rn(s01, s23);
-            const float sum = s4.x + s4.y;
+            l_run = l_run * alpha + (s4.x + s4.y);
             tmem_st_wait();
             tc_fence_before();
-            __syncwarp();  // the warp's P stores (and S reads) are complete and fenced before lane 0 reports it
-            if (lane == 0) mbar_arrive(&p_full[b]);
-            l_run = l_run * alpha + sum;
-            m_run = m_new;
-            // Fold the partial output of the previous block (its max is m_prev_blk).
-            if (j >= 1 && !fold(j - 1)) { ok = false; break; }
-            m_prev_blk = m_new;
+            __syncwarp();  // the warp's P (and O) stores are complete and fenced before lane 0 reports it
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        if (ok && nb >= 1) ok = fold(nb - 1);
-
-        // Store: row r of this tile, head h, 64 bf16 = 128 contiguous bytes.
-        const int qrow = q0 + r;
-        if (ok && qrow < p.lq) {
-            const float inv = 1.0f / l_run;
-            __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) +
-                               ((long long)img * p.out_img_stride + qrow) * p.ldo + (long long)h * kHd;
+        // O_t after the last block, divided by the row sum; row r of tile t, head h: 128 contiguous bytes.
+        if (ok && nb >= 1) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], (nb - 1) & 1, abort_flag));
+            if (ok) {
+                tc_fence_after();
+                uint32_t o[kHd];
 #pragma unroll
-            for (int c0 = 0; c0 < kHd; c0 += 8) {
-                uint4 pkt;
-                pkt.x = pack_bf16x2(o_acc[c0 + 0] * inv, o_acc[c0 + 1] * inv);
-                pkt.y = pack_bf16x2(o_acc[c0 + 2] * inv, o_acc[c0 + 3] * inv);
-                pkt.z = pack_bf16x2(o_acc[c0 + 4] * inv, o_acc[c0 + 5] * inv);
-                pkt.w = pack_bf16x2(o_acc[c0 + 6] * inv, o_acc[c0 + 7] * inv);
-                *reinterpret_cast<uint4*>(o + c0) = pkt;
+                for (int c0 = 0; c0 < kHd; c0 += 16)
+                    tmem_ld16(tt + kColO + c0, *reinterpret_cast<uint32_t(*)[16]>(o + c0));
+                tmem_ld_wait();
+                const int qrow = q0 + t * kQTile + r;
+                if (qrow < p.lq) {
+                    const float inv = 1.0f / l_run;
+                    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
+                                         ((long long)img * p.out_img_stride + qrow) * p.ldo + (long long)h * kHd;
+#pragma unroll
+                    for (int c0 = 0; c0 < kHd; c0 += 8) {
+                        uint4 pkt;
+                        pkt.x = pack_bf16x2(__uint_as_float(o[c0 + 0]) * inv, __uint_as_float(o[c0 + 1]) * inv);
+                        pkt.y = pack_bf16x2(__uint_as_float(o[c0 + 2]) * inv, __uint_as_float(o[c0 + 3]) * inv);
+                        pkt.z = pack_bf16x2(__uint_as_float(o[c0 + 4]) * inv, __uint_as_float(o[c0 + 5]) * inv);
+                        pkt.w = pack_bf16x2(__uint_as_float(o[c0 + 6]) * inv, __uint_as_float(o[c0 + 7]) * inv);
+                        *reinterpret_cast<uint4*>(out + c0) = pkt;
+                    }
+                }
             }
         }
         tc_fence_before();
@@ -336,7 +355,7 @@ int attention(const AttentionCall& c) {
     for (const void* ptr : {c.q, c.k, c.v, static_cast<const void*>(c.out)})
         if (!ptr || reinterpret_cast<uintptr_t>(ptr) % 16)
             return fail(IDOL_ERR_INVALID, "attention: q, k, v and out must be 16-byte aligned device pointers");
-    if ((c.lq + kQTile - 1) / kQTile > 0x7fffffff || c.heads > 65535 || c.batch > 65535)
+    if ((c.lq + kQTile * kQTiles - 1) / (kQTile * kQTiles) > 0x7fffffff || c.heads > 65535 || c.batch > 65535)
         return fail(IDOL_ERR_INVALID, "attention: grid too large");
 
     CUtensorMap qm, km, vm;
@@ -366,7 +385,8 @@ int attention(const AttentionCall& c) {
         IDOL_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLaunch));
         configured |= 1ull << (dev & 63);
     }
-    const dim3 grid((unsigned)((c.lq + kQTile - 1) / kQTile), (unsigned)c.heads, (unsigned)c.batch);
+    const dim3 grid((unsigned)((c.lq + kQTile * kQTiles - 1) / (kQTile * kQTiles)), (unsigned)c.heads,
+                    (unsigned)c.batch);
     attention_kernel<<<grid, kThreads, kSmemLaunch, c.stream>>>(qm, km, vm, p);
     IDOL_CUDA(cudaGetLastError());
     return IDOL_OK;
