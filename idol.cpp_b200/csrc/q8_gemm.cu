@@ -91,8 +91,10 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* chunk, int q, int l
 
 // Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row, with the
 // activation fixed at compile time so the per-element loop carries no dispatch.
+// `rv`, when given, holds the residual values of these columns, loaded ahead by the caller.
 template <typename OutT, int kCols, int kAct>
-__device__ __forceinline__ void finish_cols_act(const Params& p, int m, int row, const uint32_t* v, float bias) {
+__device__ __forceinline__ void finish_cols_act(const Params& p, int m, int row, const uint32_t* v, float bias,
+                                                const float* rv) {
     const int col = row - p.n_offset;
     OutT* y = static_cast<OutT*>(p.y) + col;
     const OutT* res = static_cast<const OutT*>(p.residual);
@@ -107,20 +109,60 @@ __device__ __forceinline__ void finish_cols_act(const Params& p, int m, int row,
         if (m + j >= p.m) break;
         const float acc = __uint_as_float(v[j]);
         float x = p.bias_after_round ? out_round<OutT>(acc) + bias : acc + bias;
-        if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
+        if (rv) x += rv[j];
+        else if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
         y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
     }
 }
 
 template <typename OutT, int kCols>
 __device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
-                                            bool row_ok) {
+                                            bool row_ok, const float* rv = nullptr) {
     if (!row_ok) return;
     switch (p.act) {
-        case IDOL_ACT_GELU_ERF: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_ERF>(p, m, row, v, bias); break;
-        case IDOL_ACT_GELU_TANH: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_TANH>(p, m, row, v, bias); break;
-        case IDOL_ACT_SILU: finish_cols_act<OutT, kCols, IDOL_ACT_SILU>(p, m, row, v, bias); break;
-        default: finish_cols_act<OutT, kCols, IDOL_ACT_NONE>(p, m, row, v, bias); break;
+        case IDOL_ACT_GELU_ERF: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_ERF>(p, m, row, v, bias, rv); break;
+        case IDOL_ACT_GELU_TANH: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_TANH>(p, m, row, v, bias, rv); break;
+        case IDOL_ACT_SILU: finish_cols_act<OutT, kCols, IDOL_ACT_SILU>(p, m, row, v, bias, rv); break;
+        default: finish_cols_act<OutT, kCols, IDOL_ACT_NONE>(p, m, row, v, bias, rv); break;
+    }
+}
+
+// Epilogue of one weight row (TMEM lane) over kSpan accumulator columns from TMEM address `acc` (tokens m0 ...),
+// 16 (or 8) columns per tcgen05.ld. With a residual, its values are loaded 32 tokens at a time before the columns
+// they meet, so a row waits one memory latency per 32 tokens instead of one per 16. Control flow around the
+// warp-collective tcgen05.ld depends only on warp-uniform values; row_ok gates the per-lane memory accesses.
+template <typename OutT, int kSpan>
+__device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, uint32_t acc, float bias,
+                                              bool row_ok) {
+    constexpr int kChunk = kSpan >= 16 ? 16 : 8;
+    constexpr int kGroup = kSpan >= 32 ? 32 : kSpan;
+    if constexpr (kGroup % 16 == 0) {
+        if (p.residual != nullptr) {
+            const OutT* res = static_cast<const OutT*>(p.residual) + (row - p.n_offset);
+            for (int g0 = 0; g0 < kSpan && m0 + g0 < p.m; g0 += kGroup) {
+                float rv[kGroup];
+#pragma unroll
+                for (int j = 0; j < kGroup; ++j)
+                    rv[j] = (row_ok && m0 + g0 + j < p.m) ? from_out<OutT>(res[(long long)(m0 + g0 + j) * p.ldr])
+                                                          : 0.0f;
+#pragma unroll
+                for (int c0 = 0; c0 < kGroup; c0 += 16) {
+                    if (m0 + g0 + c0 >= p.m) break;
+                    uint32_t v[16];
+                    tmem_ld16(acc + g0 + c0, v);
+                    tmem_ld_wait();
+                    finish_cols<OutT, 16>(p, m0 + g0 + c0, row, v, bias, row_ok, rv + c0);
+                }
+            }
+            return;
+        }
+    }
+    for (int c0 = 0; c0 < kSpan && m0 + c0 < p.m; c0 += kChunk) {
+        uint32_t v[kChunk];
+        if constexpr (kChunk == 16) tmem_ld16(acc + c0, v);
+        else tmem_ld8(acc + c0, v);
+        tmem_ld_wait();
+        finish_cols<OutT, kChunk>(p, m0 + c0, row, v, bias, row_ok);
     }
 }
 
@@ -241,13 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         if (gridDim.z == 1) {
             const bool row_ok = ok && row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
-            for (int c0 = c_begin; c0 < c_begin + kHalf && m0 + c0 < p.m; c0 += kChunk) {
-                uint32_t v[kChunk];
-                if constexpr (kChunk == 16) tmem_ld16(tmem + lane_base + c0, v);
-                else tmem_ld8(tmem + lane_base + c0, v);
-                tmem_ld_wait();
-                finish_cols<OutT, kChunk>(p, m0 + c0, row, v, bias, row_ok);
-            }
+            epilogue_span<OutT, kHalf>(p, m0 + c_begin, row, tmem + lane_base + c_begin, bias, row_ok);
         } else {
             // Park the partial tile [token][row] in this CTA's X ring (all loads into it have landed).
             float* red = reinterpret_cast<float*>(xs);
@@ -523,12 +559,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
             const int c_begin = half * kHalfCols;
             const uint32_t acc = tmem + lane_base + (uint32_t)(b * BN);
-            for (int c0 = c_begin; c0 < c_begin + kHalfCols; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(acc + c0, v);
-                tmem_ld_wait();
-                if (m0 + c0 < p.m) finish_cols<OutT, 16>(p, m0 + c0, row, v, bias, row_ok);
-            }
+            epilogue_span<OutT, kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
