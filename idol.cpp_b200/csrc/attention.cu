@@ -73,6 +73,13 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100): halves the row-maximum pass.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {
     asm volatile(
@@ -236,7 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < kKTile; ++c) m4[c % 4] = fmaxf(m4[c % 4], __uint_as_float(sv[c]));
+            for (int c = 0; c < kKTile; c += 2)
+                m4[(c / 2) % 4] = fmax3(m4[(c / 2) % 4], __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
             const float m_blk = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
             // Lazy rescaling: keep the maximum in use unless this block's exceeds it by more than 2^8.
             float alpha = 1.0f;
