@@ -307,14 +307,46 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             const int q = warp % 4;
             const int half = (warp - 2) / 4;
             const int row = row0 + 32 * q + lane;
-            const uint32_t z = cluster_ctarank();
-            const uint32_t nz = gridDim.z;
+            const int z = (int)cluster_ctarank();
+            const int nz = (int)gridDim.z;  // <= 8 (a portable cluster)
             const uint32_t red_local = smem_u32(xs);
-            for (int t = (int)z + half * (int)nz; t < BN; t += 2 * (int)nz) {
-                const uint32_t off = (uint32_t)((t * kRowsPerTile + 32 * q + lane) * 4);
-                float acc = 0.0f;
-                for (uint32_t rk = 0; rk < nz; ++rk) acc += ld_cluster_f32(map_to_rank(red_local + off, rk));
-                finish<OutT>(p, m0 + t, row, acc);
+            const bool row_ok = row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
+            const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
+            const OutT* res = static_cast<const OutT*>(p.residual);
+            OutT* y = static_cast<OutT*>(p.y);
+            const int col = row - p.n_offset;
+            // This thread finishes tokens t0, t0 + step, ... of its row. Eight tokens at a time, every rank's partial
+            // and the residual are loaded before any is used (one latency per eight tokens); the partials are summed
+            // in rank order (absent ranks add exact zeros), so the result does not depend on timing.
+            const int t0 = z + half * nz, step = 2 * nz;
+            const int count = t0 < BN ? (BN - t0 + step - 1) / step : 0;
+            for (int i0 = 0; i0 < count; i0 += 8) {
+                float acc[8], rv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int t = t0 + (i0 + u) * step;
+                    acc[u] = 0.0f;
+                    rv[u] = 0.0f;
+                    if (i0 + u < count) {
+                        const uint32_t off = (uint32_t)((t * kRowsPerTile + 32 * q + lane) * 4);
+                        float v[8];
+#pragma unroll
+                        for (int rk = 0; rk < 8; ++rk)
+                            v[rk] = rk < nz ? ld_cluster_f32(map_to_rank(red_local + off, (uint32_t)rk)) : 0.0f;
+#pragma unroll
+                        for (int rk = 0; rk < 8; ++rk) acc[u] += v[rk];
+                        if (res && row_ok && m0 + t < p.m) rv[u] = from_out<OutT>(res[(long long)(m0 + t) * p.ldr + col]);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int t = t0 + (i0 + u) * step;
+                    if (i0 + u < count && row_ok && m0 + t < p.m) {
+                        float x = p.bias_after_round ? out_round<OutT>(acc[u]) + bias : acc[u] + bias;
+                        if (res) x += rv[u];
+                        y[(long long)(m0 + t) * p.ldy + col] = to_out<OutT>(activate(x, p.act));
+                    }
+                }
             }
         }
         cluster_sync();
