@@ -145,6 +145,18 @@ int idol_b200_q8_repack(const void* q8, int out, int in, void* tiles, void* stre
     return IDOL_OK;
 }
 
+int64_t idol_b200_q4_0_bytes(int out, int in) { return shape_ok(out, in) ? (int64_t)out * (in / 32) * 18 : -1; }
+
+int idol_b200_q4_0_repack(const void* q4_0, int out, int in, void* tiles, void* stream) {
+    if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q4_0_repack: out >= 1 and in a positive multiple of 32");
+    if (!q4_0 || !tiles) return fail(IDOL_ERR_INVALID, "q4_0_repack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q4_0) % 2 || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q4_0_repack: q4_0 must be 2-byte, tiles 16-byte aligned");
+    IDOL_CUDA(idol::launch_q4_0_repack(static_cast<const uint8_t*>(q4_0), out, in, static_cast<uint8_t*>(tiles),
+                                       static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
 int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stream) {
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_unpack: out >= 1 and in a positive multiple of 32");
     if (!q8 || !tiles) return fail(IDOL_ERR_INVALID, "q8_unpack: NULL pointer");

@@ -46,6 +46,7 @@ int cuda_fail(cudaError_t e, const char* what);
 // Format kernels (q8_format.cu).
 cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, uint8_t* tiles, cudaStream_t s);
 cudaError_t launch_q8_unpack(const uint8_t* tiles, int n, int k, uint8_t* q8, cudaStream_t s);
+cudaError_t launch_q4_0_repack(const uint8_t* q4, int n, int k, uint8_t* tiles, cudaStream_t s);
 cudaError_t launch_q8_quantize(const float* w, int64_t rows, int64_t cols, uint8_t* q8, cudaStream_t s);
 cudaError_t launch_q8_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s);
 

@@ -51,6 +51,42 @@ __global__ void q8_repack_kernel(const uint8_t* __restrict__ q8, int n, int k, u
     *reinterpret_cast<uint16_t*>(chunk + scale_off(q, b, lane)) = d;
 }
 
+// GGUF Q4_0 -> the same tiled layout. An 18-byte Q4_0 block holds fp16 d and 16 bytes whose low nibbles are
+// elements 0-15 and high nibbles elements 16-31, each worth d * (nibble - 8) (tools/idol_triton.py:48-61). That is
+// exactly a Q8_0 block with codes nibble - 8 in [-8, 7] and the same d, so every kernel reading the tiled layout
+// computes the reference's bf16(fp32(d) * code) for Q4_0 matrices unchanged. One warp per (row tile, stage, quarter,
+// block) as in the Q8_0 repack; __vsub4 subtracts 8 from every byte without borrows between bytes.
+__global__ void q4_0_repack_kernel(const uint8_t* __restrict__ q4, int n, int k, uint8_t* __restrict__ tiles,
+                                   int64_t units) {
+    const int kb = k / 32, ks = k_stages(k);
+    const int64_t unit = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (unit >= units) return;
+    const int lane = threadIdx.x % 32;
+    const int b = (int)(unit % 2), q = (int)((unit / 2) % 4);
+    const int64_t ts = unit / 8;
+    const int s = (int)(ts % ks);
+    const int t = (int)(ts / ks);
+    const int64_t row = (int64_t)t * kTileRows + q * 32 + lane;
+    const int blk = 2 * s + b;
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+    uint16_t d = 0;
+    if (row < n && blk < kb) {
+        // An 18-byte block starts on a 2-byte boundary: read it as 9 halfwords.
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(q4 + (row * kb + blk) * 18);
+        d = src[0];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = (uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16);
+            lo[i] = __vsub4(v & 0x0F0F0F0Fu, 0x08080808u);
+            hi[i] = __vsub4((v >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+        }
+    }
+    uint8_t* chunk = tiles + chunk_of(t, s, ks);
+    *reinterpret_cast<uint4*>(chunk + code_off(q, b, 0, lane)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(chunk + code_off(q, b, 1, lane)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint16_t*>(chunk + scale_off(q, b, lane)) = d;
+}
+
 __global__ void q8_unpack_kernel(const uint8_t* __restrict__ tiles, int n, int k, uint8_t* __restrict__ q8,
                                  int64_t units) {
     const int kb = k / 32, ks = k_stages(k);
@@ -135,6 +171,13 @@ cudaError_t launch_q8_repack(const uint8_t* q8, int n, int k, uint8_t* tiles, cu
     const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 8;
     const int warps = 8;
     q8_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q8, n, k, tiles, units);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_0_repack(const uint8_t* q4, int n, int k, uint8_t* tiles, cudaStream_t s) {
+    const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 8;
+    const int warps = 8;
+    q4_0_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q4, n, k, tiles, units);
     return cudaGetLastError();
 }
 

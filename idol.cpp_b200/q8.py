@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import collections
 import ctypes
+import weakref
 from typing import Optional
 
 import torch
@@ -18,7 +19,9 @@ import torch.nn.functional as F
 from . import _capi as C
 
 Q8_0_KIND = 8  # tools/idol_triton.py kind code for GGML Q8_0
+Q4_0_KIND = 4  # ... and for GGML Q4_0
 _GGML_Q8_0 = 8  # gguf.GGMLQuantizationType.Q8_0 enum value
+_GGML_Q4_0 = 2  # gguf.GGMLQuantizationType.Q4_0 enum value
 
 _DTYPES = {torch.float32: C.F32, torch.float16: C.F16, torch.bfloat16: C.BF16}
 
@@ -58,6 +61,24 @@ def repack(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
     packed = packed.contiguous()
     tiles = torch.empty(tiled_bytes(n, k), dtype=torch.uint8, device=packed.device)
     C.check(C.lib().idol_b200_q8_repack(_ptr(packed), n, k, _ptr(tiles), _stream(packed.device)))
+    return tiles
+
+
+def q4_0_bytes(n: int, k: int) -> int:
+    v = C.lib().idol_b200_q4_0_bytes(n, k)
+    if v < 0:
+        raise ValueError(f"invalid Q4_0 shape ({n}, {k})")
+    return v
+
+
+def repack_q4_0(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """GGUF Q4_0 bytes (CUDA uint8) -> the tiled device layout. A Q4_0 block is exactly a Q8_0 block with codes
+    nibble - 8 (tools/idol_triton.py:48-61), so the result feeds every tiled-layout kernel unchanged."""
+    if not packed.is_cuda or packed.dtype != torch.uint8 or packed.numel() != q4_0_bytes(n, k):
+        raise ValueError("repack_q4_0: expected CUDA uint8 Q4_0 bytes of the given shape")
+    packed = packed.contiguous()
+    tiles = torch.empty(tiled_bytes(n, k), dtype=torch.uint8, device=packed.device)
+    C.check(C.lib().idol_b200_q4_0_repack(_ptr(packed), n, k, _ptr(tiles), _stream(packed.device)))
     return tiles
 
 
@@ -129,21 +150,26 @@ def _(x, tiles, bias, n, k, act=0, flags=0):
 _tiled_cache: "collections.OrderedDict[tuple, tuple]" = collections.OrderedDict()
 
 
-def _tiled_for(packed: torch.Tensor, n: int, k: int):
-    key = (packed.data_ptr(), packed.numel(), packed._version, n, k, packed.device.index)
+def _tiled_for(packed: torch.Tensor, n: int, k: int, kind: int = Q8_0_KIND):
+    """The tiled copy of `packed`, made once. An entry is used only while it still belongs to this very tensor (a weak
+    reference checked by identity): a freed buffer's address and version are reused by later tensors."""
+    key = (packed.data_ptr(), packed.numel(), packed._version, n, k, packed.device.index, kind)
     hit = _tiled_cache.get(key)
-    if hit is None:
-        hit = repack(packed, n, k)
-        _tiled_cache[key] = hit
-        if len(_tiled_cache) > 256:
-            _tiled_cache.popitem(last=False)
-    return hit
+    if hit is not None and hit[0]() is packed:
+        _tiled_cache.move_to_end(key)
+        return hit[1]
+    tiles = repack_q4_0(packed, n, k) if kind == Q4_0_KIND else repack(packed, n, k)
+    _tiled_cache[key] = (weakref.ref(packed), tiles)
+    if len(_tiled_cache) > 256:
+        _tiled_cache.popitem(last=False)
+    return tiles
 
 
 def fused_linear(value, packed, shape, kind, bias=None):
-    """Multiply FP16/BF16 activations by Q8_0 weights on CUDA, with the contract of tools/idol_triton.py:94-126:
-    same argument checks and ValueError messages, output in value's dtype, bias added after the product is rounded to
-    that dtype. GGUF kinds other than Q8_0 (4 = Q4_0, 44 = Q4_K) are not part of this build and raise ValueError."""
+    """Multiply FP16/BF16 activations by Q8_0 (kind 8) or Q4_0 (kind 4) weights on CUDA, with the contract of
+    tools/idol_triton.py:94-126: same argument checks and ValueError messages, output in value's dtype, bias added
+    after the product is rounded to that dtype. Q4_0 runs the same kernels (an exact conversion to the tiled Q8_0
+    layout); Q4_K (kind 44) is not part of this build and raises ValueError."""
     if (not value.is_cuda or not packed.is_cuda or packed.dtype != torch.uint8
             or value.device != packed.device or value.dtype not in (torch.float16, torch.bfloat16)
             or len(shape) != 2 or value.shape[-1] != shape[1] or kind not in (4, 8, 44)):
@@ -156,25 +182,26 @@ def fused_linear(value, packed, shape, kind, bias=None):
         raise ValueError('invalid packed linear dimensions')
     if bias is not None and (bias.shape != (n,) or bias.device != value.device or bias.dtype != value.dtype):
         raise ValueError('invalid fused linear bias')
-    if kind != Q8_0_KIND:
-        raise ValueError('unsupported fused linear input: only Q8_0 is implemented on sm_100a')
-    tiles = _tiled_for(packed, n, k)
+    if kind not in (Q8_0_KIND, Q4_0_KIND):
+        raise ValueError('unsupported fused linear input: only Q8_0 and Q4_0 are implemented on sm_100a')
+    tiles = _tiled_for(packed, n, k, kind)
     b32 = None if bias is None else bias.float()
     return torch.ops.idol_b200.q8_linear(value, tiles, b32, n, k, C.ACT_NONE, C.EPI_BIAS_AFTER_ROUND)
 
 
 # ----------------------------------------------------------------------------------- PackedLinear (drop-in)
 class PackedLinear(torch.nn.Module):
-    """Mirror of tools/idol_packed.py:12-82 for Q8_0 matrices: keeps the GGUF bytes as the ``packed`` buffer, and when
-    ``fused`` is set and the input is CUDA fp16/bf16 without grad, runs the sm_100a kernel on a tiled copy made once
-    per device. Unfused calls expand the weights (our dequant kernel on CUDA) and use F.linear, as the reference's
-    expansion path does."""
+    """Mirror of tools/idol_packed.py:12-82 for Q8_0 and Q4_0 matrices: keeps the GGUF bytes as the ``packed`` buffer,
+    and when ``fused`` is set and the input is CUDA fp16/bf16 without grad, runs the sm_100a kernels on a tiled copy
+    made once per device. Unfused calls expand the weights (our dequant kernel on CUDA) and use F.linear, as the
+    reference's expansion path does. The reference's other expansion-only kinds (F16, Q2_K, Q4_K, Q6_K) are outside
+    this build and raise ValueError here."""
 
     def __init__(self, source, bias):
         super().__init__()
         self.shape = tuple(reversed([int(s) for s in source.shape]))
         self.kind = int(source.tensor_type)
-        if len(self.shape) != 2 or self.kind != _GGML_Q8_0:
+        if len(self.shape) != 2 or self.kind not in (_GGML_Q8_0, _GGML_Q4_0):
             raise ValueError("unsupported packed matrix")
         import numpy as np
         self.register_buffer("packed", torch.from_numpy(np.array(source.data, copy=True)).reshape(-1))
@@ -183,25 +210,33 @@ class PackedLinear(torch.nn.Module):
         self._tiled = None
 
     def _tiles(self):
-        dev = self.packed.device
-        if self._tiled is None or self._tiled[0] != dev or self._tiled[1] != self.packed._version:
-            self._tiled = (dev, self.packed._version, repack(self.packed, *self.shape))
+        # Valid while it was made from this very buffer at this version (moving the module replaces the buffer).
+        if (self._tiled is None or self._tiled[0]() is not self.packed
+                or self._tiled[1] != self.packed._version):
+            pack = repack_q4_0 if self.kind == _GGML_Q4_0 else repack
+            self._tiled = (weakref.ref(self.packed), self.packed._version, pack(self.packed, *self.shape))
         return self._tiled[2]
 
     def dequantize(self, dtype):
         n, k = self.shape
         if self.packed.is_cuda:
             return dequantize_tiled(self._tiles(), n, k, dtype)
-        blocks = self.packed.reshape(-1, 34)
+        if self.kind == _GGML_Q4_0:  # 18-byte blocks: fp16 d, then low nibbles = elements 0-15, high = 16-31
+            blocks = self.packed.reshape(-1, 18)
+            nib = blocks[:, 2:]
+            codes = (torch.cat((nib & 15, nib >> 4), dim=1).to(torch.int16) - 8).float()
+        else:
+            blocks = self.packed.reshape(-1, 34)
+            codes = blocks[:, 2:].contiguous().view(torch.int8).float()
         scale = blocks[:, :2].contiguous().view(torch.float16).float()
-        codes = blocks[:, 2:].contiguous().view(torch.int8).float()
         return (codes * scale).reshape(self.shape).to(dtype)
 
     def forward(self, value):
         needs_grad = torch.is_grad_enabled() and (value.requires_grad or
                                                   (self.bias is not None and self.bias.requires_grad))
         if self.fused and value.is_cuda and value.dtype in (torch.float16, torch.bfloat16) and not needs_grad:
-            return fused_linear(value, self.packed, self.shape, Q8_0_KIND, self.bias)
+            kind = Q4_0_KIND if self.kind == _GGML_Q4_0 else Q8_0_KIND
+            return fused_linear(value, self.packed, self.shape, kind, self.bias)
         return F.linear(value, self.dequantize(value.dtype), self.bias)
 
 

@@ -68,6 +68,14 @@ int idol_b200_q8_quantize(const float* w, int64_t rows, int64_t cols, void* q8, 
 int idol_b200_q8_repack(const void* q8, int out, int in, void* tiles, void* stream);
 int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stream);
 
+/* GGUF Q4_0 (kind 4): bytes for an out x in matrix, out * in / 32 * 18 (tools/idol_triton.py:103-104), and the device
+ * conversion into the same tiled layout. A Q4_0 block (fp16 d, 16 bytes of nibbles: low nibbles elements 0-15, high
+ * nibbles 16-31) is worth d * (nibble - 8) (tools/idol_triton.py:48-61), i.e. exactly a Q8_0 block with codes in
+ * [-8, 7], so every entry point taking a tiled matrix (q8_view, q8_gemm, q8_dequantize) serves Q4_0 unchanged.
+ * tiles: idol_b200_q8_tiled_bytes(out, in) bytes, 16-byte aligned; q4_0 2-byte aligned. */
+int64_t idol_b200_q4_0_bytes(int out, int in);
+int idol_b200_q4_0_repack(const void* q4_0, int out, int in, void* tiles, void* stream);
+
 /* Tiled layout -> dense out x in weights d * q (w_dtype IDOL_F32 exact; IDOL_BF16 / IDOL_F16 rounded from the fp32
  * product). Replaces src/kernels.cpp:535-550 dequantize_linear and tools/idol_packed.py:25-31 dequantize. */
 int idol_b200_q8_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream);

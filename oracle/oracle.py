@@ -38,6 +38,8 @@ def lib():
         L = ctypes.CDLL(str(path))
         L.orc_q8_quantize.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _u8p]
         L.orc_q8_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+        L.orc_q4_0_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+        L.orc_q4_0_to_q8.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _u8p]
         L.orc_panel_blob_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
         L.orc_panel_blob_bytes.restype = ctypes.c_int64
         L.orc_q8_to_panels.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p]
@@ -117,6 +119,21 @@ def q8_dequantize(q8: np.ndarray, rows: int, cols: int) -> np.ndarray:
     q8 = np.ascontiguousarray(q8, dtype=np.uint8)
     out = np.empty((rows, cols), np.float32)
     lib().orc_q8_dequantize(_ptr(q8, _u8p), rows, cols, _ptr(out))
+    return out
+
+
+def q4_0_dequantize(q4: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    q4 = np.ascontiguousarray(q4, dtype=np.uint8)
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_q4_0_dequantize(_ptr(q4, _u8p), rows, cols, _ptr(out))
+    return out
+
+
+def q4_0_to_q8(q4: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Q4_0 bytes -> the Q8_0 bytes of the same weights (exact)."""
+    q4 = np.ascontiguousarray(q4, dtype=np.uint8)
+    out = np.empty(rows * (cols // 32) * 34, np.uint8)
+    lib().orc_q4_0_to_q8(_ptr(q4, _u8p), rows, cols, _ptr(out, _u8p))
     return out
 
 

@@ -129,6 +129,38 @@ void orc_q8_dequantize(const uint8_t* blocks, int64_t rows, int64_t cols, float*
 }
 
 /* ------------------------------------------------------------------------------------------------------------------
+ * GGUF Q4_0 (kind 4): 18-byte blocks of fp16 d and 16 bytes; element i of a block is nibble (i % 16) of byte i % 16,
+ * the low nibble for i < 16 and the high nibble after, worth d * (nibble - 8): restates tools/idol_triton.py:48-61
+ * (the fused kernel's decoder) and tools/idol_packed.py:32-36 (the expansion path). orc_q4_0_to_q8 writes the same
+ * weights as Q8_0 blocks (codes nibble - 8, same d), which is exact, so orc_gemm_q8 computes a Q4_0 linear too.
+ * ---------------------------------------------------------------------------------------------------------------- */
+static int orc_q4_0_code(const uint8_t* blk, int i) {
+    const uint8_t byte = blk[2 + (i % 16)];
+    return (int)(i < 16 ? (byte & 15) : (byte >> 4)) - 8;
+}
+
+void orc_q4_0_dequantize(const uint8_t* blocks, int64_t rows, int64_t cols, float* w) {
+    const int64_t nb = cols / 32;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t* blk = blocks + (r * nb + b) * 18;
+            const float d = orc_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int i = 0; i < 32; ++i) w[r * cols + b * 32 + i] = d * (float)orc_q4_0_code(blk, i);
+        }
+}
+
+void orc_q4_0_to_q8(const uint8_t* q4, int64_t rows, int64_t cols, uint8_t* q8) {
+    const int64_t nb = cols / 32;
+    for (int64_t blk = 0; blk < rows * nb; ++blk) {
+        const uint8_t* src = q4 + blk * 18;
+        uint8_t* dst = q8 + blk * 34;
+        dst[0] = src[0];
+        dst[1] = src[1];
+        for (int i = 0; i < 32; ++i) dst[2 + i] = (uint8_t)(int8_t)orc_q4_0_code(src, i);
+    }
+}
+
+/* ------------------------------------------------------------------------------------------------------------------
  * Q8_0 -> idol panel blob, bits 8, group 32: restates tools/gguf_to_decoder.py:16-40 (code = q + 128, scale = fp16 d,
  * min = fp16(-128 d), rejected unless exact) and tools/idolq.py:137-166 (16 output columns per panel; per group a 64-byte
  * header of 16 fp16 scales then 16 fp16 minimums, then 32 rows of k x 16 columns of codes). Returns 0, or -1 when a

@@ -307,3 +307,18 @@ def test_empty_batch_and_errors(pkg, cuda):
 def test_no_kernel_reported_a_timeout(pkg, cuda):
     torch.cuda.synchronize()
     assert pkg._capi.device_status(0) == 0
+
+
+def test_fused_linear_cache_never_serves_a_freed_buffer(pkg, oracle, cuda):
+    """The tiled copy fused_linear caches belongs to one packed tensor: a new matrix of the same shape, allocated where
+    a freed one lived (same address, same version counter), gets its own weights."""
+    n, k, m = 256, 512, 8
+    rng = np.random.default_rng(77)
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    xt = torch.from_numpy(x).to(cuda, torch.bfloat16)
+    for trial in range(3):
+        q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+        packed = torch.from_numpy(q8.reshape(-1)).to(cuda)
+        y = pkg.fused_linear(xt, packed, (n, k), 8).float().cpu().numpy()
+        _check(y, oracle.gemm_q8(x, q8, np.zeros(n, np.float32), n, k), what=f"trial {trial}")
+        del packed
