@@ -27,6 +27,7 @@ struct Params {
     int act;
     int bias_after_round;
     int stages_per_split, stages_total;
+    int y_tma;                // the output tensor map may be used for TMA stores (2-byte output, aligned rows)
 };
 
 template <typename OutT>

@@ -166,6 +166,40 @@ __device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, 
     }
 }
 
+// The staged form of epilogue_span for the TMA-store path: the finished value of token m0 + j goes to shared address
+// st + 256 j of the staging tile (token-major, 128 features of 2 bytes per token; this lane's feature folded into st),
+// and a single TMA store later writes the tile. Features outside the output window and tokens past M are written
+// too: the store clips them. The 32 lanes of a warp store 64 contiguous bytes per token (no bank conflict).
+// GELU-erf takes 8 columns per tcgen05.ld: erff on 16 values at once needs more than the 96 registers a thread has.
+template <typename OutT, int kSpan, int kAct>
+__device__ __forceinline__ void epilogue_span_staged(const Params& p, int m0, int row, uint32_t acc, float bias,
+                                                     bool row_ok, uint32_t st) {
+    constexpr int kC = kAct == IDOL_ACT_GELU_ERF ? 8 : 16;
+    static_assert(kSpan % kC == 0 && sizeof(OutT) == 2, "whole chunks of a 2-byte output");
+    const OutT* res = p.residual ? static_cast<const OutT*>(p.residual) + (row - p.n_offset) : nullptr;
+    for (int c0 = 0; c0 < kSpan && m0 + c0 < p.m; c0 += kC) {
+        float rv[kC];
+        if (res) {
+#pragma unroll
+            for (int j = 0; j < kC; ++j)
+                rv[j] = (row_ok && m0 + c0 + j < p.m) ? from_out<OutT>(res[(long long)(m0 + c0 + j) * p.ldr]) : 0.0f;
+        }
+        uint32_t v[kC];
+        if constexpr (kC == 16) tmem_ld16(acc + c0, v);
+        else tmem_ld8(acc + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < kC; ++j) {
+            const float a = __uint_as_float(v[j]);
+            float x = p.bias_after_round ? out_round<OutT>(a) + bias : a + bias;
+            if (res) x += rv[j];
+            const OutT o = to_out<OutT>(activate_t<kAct>(x));
+            st_shared_u16(st + (uint32_t)(c0 + j) * (kRowsPerTile * 2),
+                          *reinterpret_cast<const uint16_t*>(&o));
+        }
+    }
+}
+
 template <int BN, int S, bool kBF16, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Params p) {
     using C = Config<BN, S>;
@@ -335,7 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
                             v[rk] = rk < nz ? ld_cluster_f32(map_to_rank(red_local + off, (uint32_t)rk)) : 0.0f;
 #pragma unroll
                         for (int rk = 0; rk < 8; ++rk) acc[u] += v[rk];
-                        if (res && row_ok && m0 + t < p.m) rv[u] = from_out<OutT>(res[(long long)(m0 + t) * p.ldr + col]);
+                        if (res && row_ok && m0 + t < p.m)
+                            rv[u] = from_out<OutT>(res[(long long)(m0 + t) * p.ldr + col]);
                     }
                 }
 #pragma unroll
@@ -381,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the token columns each
 constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 
-template <int BN, int S, int SA, bool kPair>
+// kYStage: bytes of the shared staging tile the epilogue hands to TMA stores (0: the epilogue stores directly).
+template <int BN, int S, int SA, bool kPair, int kYStage = 0>
 struct ConfigPersistent {
     static constexpr int kHalf = kPair ? BN / 2 : BN;  // token rows this CTA loads per stage
     static constexpr int kXBytes = kHalf * 128;
@@ -389,15 +425,17 @@ struct ConfigPersistent {
     static constexpr int kACol0 = 2 * BN;  // accumulators at columns 0 and BN, then the A slots
     static constexpr int kColsNeeded = kACol0 + SA * 32;
     static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
-    static constexpr int kBarBytes = 8 * (3 * S + SA + 4) + 16;
+    static constexpr int kBarBytes = 8 * (3 * S + SA + 6) + 16;
     static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
-    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kBarBytes;
+    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kYStage + kBarBytes;
     // At least 120 KB: one CTA per SM, so a TMEM allocation of 512 columns never waits on a neighbour.
     static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
     static_assert(kColsNeeded <= 512, "TMEM budget");
     static_assert(kSmemUsed <= 227 * 1024, "shared memory budget");
     static_assert(BN % (kPair ? 32 : 16) == 0 && BN >= 64 && BN <= 256, "MMA N");
     static_assert(kXBytes % 1024 == 0, "each token half must stay 1024-aligned for the 128-byte swizzle");
+    static constexpr int kYStageBytes = kYStage;
+    static_assert(kYStage % 1024 == 0, "the staging tile keeps the weight chunks after it 16-byte aligned");
 };
 
 struct PersistentSchedule {
@@ -407,22 +445,33 @@ struct PersistentSchedule {
 
 // kPair = false is the same pipeline on one CTA (cta_group::1, M = 128 rows, the whole token tile loaded locally, no
 // cluster): X and the codes of a stage land on one barrier, so the dequant warps wait once per stage.
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT>
+//
+// kYStage > 0 (one CTA, 2-byte output, a window starting on a 128-row tile): every tile leaves through a shared
+// staging tile and one TMA store (`ymap`: the output window [n_count features x M tokens]) instead of 96 global
+// stores per lane; the store issuer (epilogue warp 0, lane 0) reports the staging tile free again on sfree once the
+// store has read it.
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage>
 __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
-    const __grid_constant__ CUtensorMap xmap, const Params p, const PersistentSchedule sched) {
-    using C = ConfigPersistent<BN, S, SA, kPair>;
+    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap, const Params p,
+    const PersistentSchedule sched) {
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage>;
+    static_assert(kYStage == 0 || (!kPair && sizeof(OutT) == 2 && kYStage >= BN * kRowsPerTile * 2),
+                  "staging: one CTA, a 2-byte output and room for the whole tile");
     constexpr int kRowsPerUnit = kPair ? 2 * kRowsPerTile : kRowsPerTile;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;
-    uint8_t* ws = xs + S * C::kXBytes;                                              // S x 8704 weight chunks
+    uint8_t* ys = xs + S * C::kXBytes;                                              // output staging (1024-aligned)
+    uint8_t* ws = ys + C::kYStageBytes;                                             // S x 8704 weight chunks
     uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);            // even CTA: both halves landed
     uint64_t* cfull = xfull + S;                                                    // this CTA's codes landed
     uint64_t* empty = cfull + S;                                                    // both: stage s consumed
     uint64_t* afull = empty + S;                                                    // even CTA: A slot written (both)
     uint64_t* accfull = afull + SA;                                                 // both: accumulator b ready
     uint64_t* accempty = accfull + 2;                                               // even CTA: accumulator b drained
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 2);
+    uint64_t* sfull = accempty + 2;                                                 // staging tile written
+    uint64_t* sfree = sfull + 1;                                                    // staging tile read by TMA
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sfree + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -444,6 +493,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
             mbar_init(&accfull[b], 1);
             mbar_init(&accempty[b], (kPair ? 2 : 1) * kEpilogueWarps);
         }
+        mbar_init(sfull, kEpilogueWarps);  // one arrival per epilogue warp once its share of the staging tile is in
+        mbar_init(sfree, 1);               // the store issuer, once the TMA store has read the staging tile
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -580,24 +631,76 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         constexpr int kHalfCols = BN / 2;
         int lt = 0;
+        int ns = 0;  // TMA stores issued so far (staged tiles)
         for (int t = pair_id; t < total_tiles; t += num_pairs, ++lt) {
             const int b = lt & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&accfull[b], (lt >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            const int row = p.row_begin + (t % sched.units_n) * kRowsPerUnit + (int)rank * kRowsPerTile + 32 * q + lane;
+            const int tile_row0 = p.row_begin + (t % sched.units_n) * kRowsPerUnit + (int)rank * kRowsPerTile;
+            const int row = tile_row0 + 32 * q + lane;
             const int m0 = (t / sched.units_n) * BN;
             const bool row_ok = row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
             const int c_begin = half * kHalfCols;
             const uint32_t acc = tmem + lane_base + (uint32_t)(b * BN);
-            epilogue_span<OutT, kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (rank == 0) mbar_arrive(&accempty[b]);
-                else mbar_arrive_remote(map_to_rank(smem_u32(&accempty[b]), 0));
+            if constexpr (C::kYStageBytes > 0) {
+                // Staged: every tile leaves through the staging tile and one TMA store at column tile_row0 - n_offset
+                // (>= 0 and a multiple of 8: the host stages only windows with n_offset % 128 == 0).
+                if (ns > 0 && !__all_sync(0xffffffffu, mbar_wait(sfree, (ns - 1) & 1, abort_flag))) break;
+                const uint32_t st = smem_u32(ys) + 2u * (uint32_t)(c_begin * kRowsPerTile + 32 * q + lane);
+                switch (p.act) {
+                    case IDOL_ACT_GELU_ERF:
+                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_GELU_ERF>(p, m0 + c_begin, row, acc + c_begin,
+                                                                                bias, row_ok, st);
+                        break;
+                    case IDOL_ACT_GELU_TANH:
+                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_GELU_TANH>(p, m0 + c_begin, row, acc + c_begin,
+                                                                                 bias, row_ok, st);
+                        break;
+                    case IDOL_ACT_SILU:
+                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_SILU>(p, m0 + c_begin, row, acc + c_begin, bias,
+                                                                            row_ok, st);
+                        break;
+                    default:
+                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_NONE>(p, m0 + c_begin, row, acc + c_begin, bias,
+                                                                            row_ok, st);
+                        break;
+                }
+                tc_fence_before();
+                fence_proxy_async_shared();  // this lane's staging writes, before the TMA store reads them
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&accempty[b]);
+                    mbar_arrive(sfull);
+                }
+                if (ew == 0) {
+                    bool stored = true;
+                    if (lane == 0) {
+                        stored = mbar_wait(sfull, ns & 1, abort_flag);
+                        if (stored) {
+                            tma_store_2d(&ymap, ys, tile_row0 - p.n_offset, m0);
+                            bulk_commit_group();
+                            bulk_wait_group_read0();
+                        }
+                        mbar_arrive(sfree);
+                    }
+                    __syncwarp();
+                    if (!__shfl_sync(0xffffffffu, stored ? 1 : 0, 0)) break;
+                }
+                ++ns;
+            } else {
+                epilogue_span<OutT, kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if (rank == 0) mbar_arrive(&accempty[b]);
+                    else mbar_arrive_remote(map_to_rank(smem_u32(&accempty[b]), 0));
+                }
             }
+        }
+        if constexpr (C::kYStageBytes > 0) {
+            if (ew == 0 && lane == 0 && ns > 0) bulk_wait_group0();  // the stores have completed before the CTA exits
         }
     }
 
@@ -610,10 +713,11 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     }
 }
 
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT>
-int launch_persistent(const CUtensorMap& xmap, const Params& p, int units_n, int tiles_m, cudaStream_t stream) {
-    using C = ConfigPersistent<BN, S, SA, kPair>;
-    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT>;
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage = 0>
+int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const Params& p, int units_n, int tiles_m,
+                      cudaStream_t stream) {
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage>;
+    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT, kYStage>;
     static unsigned long long configured = 0;
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -637,17 +741,25 @@ int launch_persistent(const CUtensorMap& xmap, const Params& p, int units_n, int
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = kPair ? 1 : 0;
-    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, p, sched));
+    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, ymap, p, sched));
     return IDOL_OK;
 }
 
-// kind 0: CTA pair, 128- or 192-token tiles; kind 1: one CTA, 192-token tiles.
+// kind 0: CTA pair, 128- or 192-token tiles; kind 1: one CTA, 192-token tiles (with p.y_tma through the 48 KB
+// staging tile and TMA stores, with five stages; otherwise six stages and direct stores).
 template <bool kBF16, typename OutT>
-int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const Params& p, int units, int tiles_m,
-                        cudaStream_t stream) {
-    if (kind == 1) return launch_persistent<192, 6, 4, false, kBF16, OutT>(xmap, p, units, tiles_m, stream);
-    if (bn == 128) return launch_persistent<128, 8, 8, true, kBF16, OutT>(xmap, p, units, tiles_m, stream);
-    return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, p, units, tiles_m, stream);
+int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtensorMap& ymap, const Params& p,
+                        int units, int tiles_m, cudaStream_t stream) {
+    if (kind == 1) {
+        if constexpr (sizeof(OutT) == 2) {
+            if (p.y_tma)
+                return launch_persistent<192, 5, 4, false, kBF16, OutT, 192 * kRowsPerTile * 2>(xmap, ymap, p, units,
+                                                                                              tiles_m, stream);
+        }
+        return launch_persistent<192, 6, 4, false, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
+    }
+    if (bn == 128) return launch_persistent<128, 8, 8, true, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
+    return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT>
@@ -697,6 +809,15 @@ int env_int(const char* name, int fallback) {
 }
 
 }  // namespace
+
+// Whether the output window can leave the one-CTA persistent kernel through TMA stores (see the kernel): a 2-byte
+// output, a window starting on a 128-row tile, a 16-byte aligned base and row stride, and at least one full tile.
+// IDOL_B200_GEMM_YTMA = 0 turns it off.
+static bool staged_output_ok(const GemmCall& c) {
+    return c.y_dtype != IDOL_F32 && c.n >= kRowsPerTile && c.m >= 192 && c.n_offset % kRowsPerTile == 0 &&
+           (c.ldy * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(c.y) % 16 == 0 &&
+           env_int("IDOL_B200_GEMM_YTMA", 1) != 0;
+}
 
 // Token-tile width and split-K factor by M (the strategy choice). IDOL_B200_GEMM_BN and IDOL_B200_GEMM_SPLITS force
 // them for tests and sweeps.
@@ -779,8 +900,17 @@ int q8_gemm(const GemmCall& c) {
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
     const bool pair = bn >= 128 && (forced_pair == 1 ||
                                     (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
-    // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator): IDOL_B200_GEMM_PERSIST = 1.
-    const bool persist1 = !pair && bn >= 256 && env_int("IDOL_B200_GEMM_PERSIST", 0) == 1;
+    // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator, a 2-byte output leaving
+    // through a staging tile and TMA stores): measured on B200 it pays at K <= 1024 once the 192-token tiles number
+    // eight or more per SM (M = 16384, K = 1024: 864 -> 910 TFLOP/s at N = 3072, 900 -> 930 at N = 4096); with
+    // fewer tiles, longer K or direct stores the non-persistent kernel is faster. IDOL_B200_GEMM_PERSIST = 1 / 0
+    // forces it on / off.
+    const bool staged = staged_output_ok(c);
+    const int forced_persist = env_int("IDOL_B200_GEMM_PERSIST", -1);
+    const long long tiles192 = (long long)tiles_n * ((c.m + 191) / 192);
+    const bool persist1 = !pair && bn >= 256 &&
+                          (forced_persist == 1 || (forced_persist != 0 && staged && p.stages_total <= 16 &&
+                                                   tiles192 >= 8LL * num_sms(w.device)));
     if (pair || persist1) {
         const int kind = pair ? 0 : 1;
         const int pbn = kind == 1 ? 192 : bn >= 256 ? 192 : 128;  // two accumulators fit TMEM beside the A slots
@@ -796,15 +926,31 @@ int q8_gemm(const GemmCall& c) {
                                       c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK,
                                       kind == 0 ? pbn / 2 : pbn, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc != IDOL_OK) return rc;
+        // The output tensor map of the staged epilogue (one CTA, 2-byte output): the window [c.n features x M
+        // tokens], one 128 x 192 box per tile. A TMA store needs a 16-byte aligned base and row stride, and an x
+        // coordinate (tile start - n_offset) that is a non-negative multiple of 8 elements: windows that start on
+        // a 128-row tile.
+        CUtensorMap ymap = xmap;
+        p.y_tma = 0;
+        if (kind == 1 && staged) {
+            if (encode_tmap_2d(&ymap, c.y_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                               c.y, (uint64_t)c.n, (uint64_t)c.m, (uint64_t)c.ldy * 2, kRowsPerTile, pbn,
+                               CU_TENSOR_MAP_SWIZZLE_NONE) == IDOL_OK)
+                p.y_tma = 1;
+            else
+                ymap = xmap;
+        }
         const bool bf16 = c.x_dtype == IDOL_BF16;
         if (c.y_dtype == IDOL_F32)
-            return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, p, units, tiles_m, c.stream)
-                        : dispatch_persistent<false, float>(kind, pbn, xmap, p, units, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
+                        : dispatch_persistent<false, float>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream);
         if (c.y_dtype == IDOL_BF16)
-            return bf16 ? dispatch_persistent<true, __nv_bfloat16>(kind, pbn, xmap, p, units, tiles_m, c.stream)
-                        : dispatch_persistent<false, __nv_bfloat16>(kind, pbn, xmap, p, units, tiles_m, c.stream);
-        return bf16 ? dispatch_persistent<true, __half>(kind, pbn, xmap, p, units, tiles_m, c.stream)
-                    : dispatch_persistent<false, __half>(kind, pbn, xmap, p, units, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, __nv_bfloat16>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
+                        : dispatch_persistent<false, __nv_bfloat16>(kind, pbn, xmap, ymap, p, units, tiles_m,
+                                                                    c.stream);
+        return bf16 ? dispatch_persistent<true, __half>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
+                    : dispatch_persistent<false, __half>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream);
     }
     p.stages_per_split = (p.stages_total + splits - 1) / splits;
     splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // every split gets >= 1 stage
