@@ -294,9 +294,18 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         // The A buffer of slot s was last read by stage i - S. Its MMA has completed once full[s] completes for stage
         // i: the producer issues stage i's copies only after that MMA's commit (empty[s]), so one wait covers both.
+        // With an odd S the two groups alternate on a slot: stage i and stage i - S of slot s belong to different
+        // groups, and a parity wait cannot tell phase u of full[s] from phase u - 2. So the group first waits for the
+        // commit of stage i - S (empty[s]; commits complete in order, and the group has seen the commit of its own
+        // previous stage's predecessor, so that wait is exact): stage i - S had landed before its MMA, so full[s]
+        // is then in phase u and the parity wait below is exact too.
         for (int i = half; i < nks; i += 2) {
             const int s = i % S, u = i / S;
-            const bool got = mbar_wait(&full[s], u & 1, abort_flag);
+            bool got = true;
+            if constexpr (S % 2 == 1) {
+                if (i >= S) got = mbar_wait(&empty[s], (u - 1) & 1, abort_flag);
+            }
+            if (got) got = mbar_wait(&full[s], u & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
             tc_fence_after();
             dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, min(2, p.kb - (ks_begin + i) * 2),
@@ -427,6 +436,9 @@ struct ConfigPersistent {
     static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kBarBytes = 8 * (3 * S + SA + 6) + 16;
     static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
+    // Dequant groups alternate by stage parity: an even SA keeps each A slot (afull) with one group; an odd S needs
+    // the A-slot wait (SA < S) to order the parity waits on a stage slot the two groups share.
+    static_assert(SA % 2 == 0 && (S % 2 == 0 || SA < S), "stage and A-slot counts");
     static constexpr int kSmemUsed = 1024 + S * kStageBytes + kYStage + kBarBytes;
     // At least 120 KB: one CTA per SM, so a TMEM allocation of 512 columns never waits on a neighbour.
     static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
@@ -603,14 +615,20 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 const int a = i % SA;
                 // A pair: this CTA's codes (cfull), and on the even CTA both token halves (xfull, see the MMA loop).
                 // One CTA: codes and tokens land together on xfull.
-                bool got = kPair ? mbar_wait(&cfull[s], u & 1, abort_flag) : true;
-                if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);
+                // The A-slot wait comes first: A slot a was last read by stage i - SA, and its commit (commits
+                // complete in order) implies that of stage i - S, so stage i - S has landed and the parity waits on
+                // xfull[s] / cfull[s] below cannot mistake phase u - 2 for phase u when the two groups alternate on a
+                // slot (odd S). With SA == S (S even: one group per slot, which sees its slot's phases in order),
+                // cfull[s] of stage i implies the commit of stage i - S (the producer waited for it).
+                bool got = true;
                 if constexpr (SA < S) {
-                    if (got && i >= SA) {  // A slot a was last read by stage i - SA
+                    if (i >= SA) {
                         const int r = i - SA;
                         got = mbar_wait(&empty[r % S], (r / S) & 1, abort_flag);
                     }
-                }  // with SA == S, cfull[s] of stage i implies the commit of stage i - S (the producer waited for it)
+                }
+                if (got && kPair) got = mbar_wait(&cfull[s], u & 1, abort_flag);
+                if (got && rank == 0) got = mbar_wait(&xfull[s], u & 1, abort_flag);
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
                 dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, valid ? min(2, p.kb - ks * 2) : 0,
