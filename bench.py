@@ -16,6 +16,8 @@ e2e        : the same metric through the drop-in API (fused_linear over GGUF Q8_
 roofline   : the GEMM kernel on the tensor-bound shapes (M >= 4096): 2 M N K per launch / CUDA-event duration, against
              the measured dense bf16 peak; roofline_small_m: the HBM-bound shapes (M <= 16), algorithmic bytes
              1.0625 N K + 2 M K + 2 M N + 4 N per launch against the measured HBM bandwidth.
+gpu_baselines: on the same GPU, per shape, the reference's unfused PackedLinear path (torch dequantize + F.linear)
+             and cuBLAS on dense bf16 weights, against the fused kernel's per-launch times (shapes[]).
 cpu_baseline: the reference's own CPU kernel (src/kernels.cpp gemm_packed, float kernel, OpenMP, compiled into
              oracle/_ref) on a bounded sample (M capped at 256 rows per shape), rank 0 at N=1.
 --impl reference: that CPU kernel alone, as the reference arm (rank 0 only under torchrun).
@@ -154,6 +156,59 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside)}
 
 
+# ------------------------------------------------------------------------------------------------ GPU baselines
+def dequantize_q8_torch(packed, n, k, dtype):
+    """The reference's unfused GPU path for a Q8_0 matrix (tools/idol_packed.py:25-31,71-79 PackedLinear.dequantize):
+    fp16 scale times int8 code in fp32 over the 34-byte blocks, then the activation dtype, in plain torch ops."""
+    import torch
+    blocks = packed.reshape(-1, 34)
+    scale = blocks[:, :2].contiguous().view(torch.float16).float()
+    codes = blocks[:, 2:].contiguous().view(torch.int8).float()
+    return (codes * scale).reshape(n, k).to(dtype)
+
+
+def measure_gpu_baselines(ops, stream, dev):
+    """Per sweep shape, CUDA-event time of (a) the reference's unfused PackedLinear.forward on the GPU (dequantize the
+    GGUF bytes to bf16, then F.linear = cuBLAS) and (b) cuBLAS alone on weights dequantized beforehand, each over R
+    operand copies in one CUDA graph (as the per-launch timing of the fused kernel). Returns per-shape microseconds."""
+    import torch
+    import torch.nn.functional as F
+    rows = []
+    for o in ops:
+        m, k, n = o["m"], o["k"], o["n"]
+        per_copy = n * k * 2 + m * k * 2
+        R = int(min(16, max(2, -(-256e6 // per_copy))))
+        xs = [o["x"].clone() for _ in range(R)]
+        packs = [o["packed"].clone() for _ in range(R)]
+        dense = [dequantize_q8_torch(pk, n, k, torch.bfloat16) for pk in packs]
+        res = {}
+        for name in ("unfused", "cublas"):
+            def run():
+                for r in range(R):
+                    w = dense[r] if name == "cublas" else dequantize_q8_torch(packs[r], n, k, torch.bfloat16)
+                    F.linear(xs[r], w, o["bias_bf16"])
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                run()
+                with torch.cuda.graph(g, stream=stream):
+                    run()
+                g.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(3):
+                    g.replay()
+                e1.record(stream)
+            stream.synchronize()
+            res[name] = e0.elapsed_time(e1) * 1e3 / (3 * R)
+            del g
+        rows.append(res)
+        del xs, packs, dense
+        torch.cuda.empty_cache()
+    return rows
+
+
 # ------------------------------------------------------------------------------------------------------ ours
 def run_ours(args, rank, world, local_rank):
     import torch
@@ -265,6 +320,10 @@ def run_ours(args, rank, world, local_rank):
         del copies, gs
     torch.cuda.empty_cache()
 
+    # GPU baselines on the same device (not part of the timed step): the reference's unfused PackedLinear path and
+    # cuBLAS on dense bf16 weights, per shape.
+    base_us = measure_gpu_baselines(ops, stream, dev) if not args.no_gpu_baselines else None
+
     # e2e through the drop-in API with host buffers
     host_x = [o["x"].cpu().pin_memory() for o in ops]
     host_y = [torch.empty(o["y"].shape, dtype=o["y"].dtype).pin_memory() for o in ops]
@@ -335,9 +394,13 @@ def run_ours(args, rank, world, local_rank):
         t = mean_ms[i] / 1e3
         tf = flops(o["m"], o["k"], o["n"]) / t / 1e12
         gb = alg_bytes(o["m"], o["k"], o["n"]) / t / 1e9
-        shape_rows.append({"M": o["m"], "K": o["k"], "N": o["n"], "copies": reps[i], "us": round(mean_ms[i] * 1e3, 2),
-                           "tflops": round(tf, 1), "gbs": round(gb, 1), "frac_tensor": round(tf / tc_peak, 3),
-                           "frac_hbm": round(gb / hbm_peak, 3)})
+        row = {"M": o["m"], "K": o["k"], "N": o["n"], "copies": reps[i], "us": round(mean_ms[i] * 1e3, 2),
+               "tflops": round(tf, 1), "gbs": round(gb, 1), "frac_tensor": round(tf / tc_peak, 3),
+               "frac_hbm": round(gb / hbm_peak, 3)}
+        if base_us is not None:
+            row["us_unfused"] = round(base_us[i]["unfused"], 2)
+            row["us_cublas_dense"] = round(base_us[i]["cublas"], 2)
+        shape_rows.append(row)
     big = [i for i, o in enumerate(ops) if o["m"] >= 4096]
     small = [i for i, o in enumerate(ops) if o["m"] <= 16]
     ach_t = sum(flops(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in big) / (sum(mean_ms[i] for i in big) / 1e3) / 1e12
@@ -385,6 +448,21 @@ def run_ours(args, rank, world, local_rank):
                          "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
                          "tflops": round(MLP_FLOPS * mlp_steps * world / (mlp_ms / 1e3) / 1e12, 1)},
     }
+    if base_us is not None:
+        sweep_unfused = sum(r["unfused"] for r in base_us) / 1e6
+        sweep_cublas = sum(r["cublas"] for r in base_us) / 1e6
+        sweep_ours = sum(mean_ms) / 1e3
+        line["gpu_baselines"] = {
+            "unit": UNIT, "timing": "per shape, R operand copies in one CUDA graph, CUDA events (as shapes[].us)",
+            "sweep_ours": round(step_flops / sweep_ours / 1e12, 1),
+            "packedlinear_unfused": {
+                "value": round(step_flops / sweep_unfused / 1e12, 1),
+                "what": "the reference's GPU path without the fused kernel (tools/idol_packed.py:71-79): dequantize "
+                        "the GGUF Q8_0 bytes to bf16 with torch ops every call, then F.linear (cuBLAS)"},
+            "cublas_bf16_dense": {
+                "value": round(step_flops / sweep_cublas / 1e12, 1),
+                "what": "F.linear (cuBLAS) on bf16 weights dequantized beforehand: 2 bytes per weight instead of "
+                        "1.0625, no dequantization in the call"}}
     if world == 1 and not args.no_cpu_baseline:
         v, cores, kind, sample = cpu_reference_sample()
         line["cpu_baseline"] = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
@@ -520,6 +598,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-baselines", action="store_true")
     ap.add_argument("--profile-shape", default=None,
                     help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture; 'block' or 'mlp' "
                          "runs the config-3 block or the config-4 MLP instead")
