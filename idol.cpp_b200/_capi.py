@@ -27,6 +27,11 @@ SIGNATURES = {
     "idol_b200_q8_repack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "idol_b200_q4_0_bytes": (_i64, [_i32, _i32]),
     "idol_b200_q4_0_repack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "idol_b200_q4_k_bytes": (_i64, [_i32, _i32]),
+    "idol_b200_q4_k_tiled_bytes": (_i64, [_i32, _i32]),
+    "idol_b200_q4_k_repack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "idol_b200_q4_k_dequantize": (_i32, [_vp, _i32, _i32, _vp, _i32, _vp]),
+    "idol_b200_q4_k_view": (_i32, [_vp, _vp, _i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "idol_b200_q8_unpack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "idol_b200_q8_dequantize": (_i32, [_vp, _i32, _i32, _vp, _i32, _vp]),
     "idol_b200_q8_upload": (_i32, [_vp, _i64, _i32, _i32, _vp, _i32, ctypes.POINTER(_vp)]),

@@ -157,6 +157,58 @@ int idol_b200_q4_0_repack(const void* q4_0, int out, int in, void* tiles, void* 
     return IDOL_OK;
 }
 
+int64_t idol_b200_q4_k_bytes(int out, int in) {
+    return (out >= 1 && in >= 256 && in % 256 == 0) ? (int64_t)out * (in / 256) * 144 : -1;
+}
+
+int64_t idol_b200_q4_k_tiled_bytes(int out, int in) {
+    return (out >= 1 && in >= 256 && in % 256 == 0) ? idol::q4k_tiled_bytes(out, in) : -1;
+}
+
+int idol_b200_q4_k_repack(const void* q4_k, int out, int in, void* tiles, void* stream) {
+    if (out < 1 || in < 256 || in % 256)
+        return fail(IDOL_ERR_INVALID, "q4_k_repack: out >= 1 and in a positive multiple of 256");
+    if (!q4_k || !tiles) return fail(IDOL_ERR_INVALID, "q4_k_repack: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(q4_k) % 16 || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q4_k_repack: q4_k and tiles must be 16-byte aligned");
+    IDOL_CUDA(idol::launch_q4_k_repack(static_cast<const uint8_t*>(q4_k), out, in, static_cast<uint8_t*>(tiles),
+                                       static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q4_k_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream) {
+    if (out < 1 || in < 256 || in % 256)
+        return fail(IDOL_ERR_INVALID, "q4_k_dequantize: out >= 1 and in a positive multiple of 256");
+    if (!tiles || !w) return fail(IDOL_ERR_INVALID, "q4_k_dequantize: NULL pointer");
+    if (reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q4_k_dequantize: tiles not 16-byte aligned");
+    if (w_dtype != IDOL_F32 && w_dtype != IDOL_BF16 && w_dtype != IDOL_F16)
+        return fail(IDOL_ERR_UNSUPPORTED, "q4_k_dequantize: output must be f32, bf16 or f16");
+    IDOL_CUDA(idol::launch_q4_k_dequant(static_cast<const uint8_t*>(tiles), out, in, w, w_dtype,
+                                        static_cast<cudaStream_t>(stream)));
+    return IDOL_OK;
+}
+
+int idol_b200_q4_k_view(const void* tiles, const float* bias_dev, int out, int in, int device,
+                        idol_q8_matrix** matrix) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q4_k_view: matrix is NULL");
+    *matrix = nullptr;
+    if (out < 1 || in < 256 || in % 256)
+        return fail(IDOL_ERR_INVALID, "q4_k_view: out >= 1 and in a positive multiple of 256");
+    if (!tiles || reinterpret_cast<uintptr_t>(tiles) % 16)
+        return fail(IDOL_ERR_INVALID, "q4_k_view: tiles must be a 16-byte aligned device pointer");
+    auto* h = new idol_q8_matrix();
+    h->m.device = device;
+    h->m.n = out;
+    h->m.k = in;
+    h->m.tiles = static_cast<uint8_t*>(const_cast<void*>(tiles));
+    h->m.bias = const_cast<float*>(bias_dev);
+    h->m.owns = false;
+    h->m.format = idol::kFmtQ4K;
+    *matrix = h;
+    return IDOL_OK;
+}
+
 int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stream) {
     if (!shape_ok(out, in)) return fail(IDOL_ERR_INVALID, "q8_unpack: out >= 1 and in a positive multiple of 32");
     if (!q8 || !tiles) return fail(IDOL_ERR_INVALID, "q8_unpack: NULL pointer");
@@ -270,12 +322,15 @@ int idol_b200_q8_info(const idol_q8_matrix* matrix, int* out, int* in, int* devi
     if (in) *in = matrix->m.k;
     if (device) *device = matrix->m.device;
     if (device_bytes)
-        *device_bytes = idol::tiled_bytes(matrix->m.n, matrix->m.k) + (matrix->m.bias ? 4 * (int64_t)matrix->m.n : 0);
+        *device_bytes = (matrix->m.format == idol::kFmtQ4K ? idol::q4k_tiled_bytes(matrix->m.n, matrix->m.k)
+                                                            : idol::tiled_bytes(matrix->m.n, matrix->m.k)) +
+                        (matrix->m.bias ? 4 * (int64_t)matrix->m.n : 0);
     return IDOL_OK;
 }
 
 int idol_b200_q8_export(const idol_q8_matrix* matrix, void* q8_dev, int64_t nbytes, void* stream) {
     if (!matrix || !q8_dev) return fail(IDOL_ERR_INVALID, "q8_export: NULL pointer");
+    if (matrix->m.format != idol::kFmtQ8) return fail(IDOL_ERR_UNSUPPORTED, "q8_export: the matrix holds Q4_K tiles");
     if (nbytes != (int64_t)matrix->m.n * (matrix->m.k / 32) * 34)
         return fail(IDOL_ERR_INVALID, "q8_export: byte count does not match the shape");
     IDOL_CUDA(cudaSetDevice(matrix->m.device));

@@ -24,13 +24,28 @@ __host__ __device__ inline int64_t tiled_bytes(int n, int k) {
     return (int64_t)row_tiles(n) * k_stages(k) * kChunkBytes;
 }
 
-// Device-resident Q8_0 matrix in the tiled layout.
+// Tiled device layout of a Q4_K matrix (see q8_format.cu): the same chunk grid, each chunk 4096 bytes of 4-bit codes
+// ([quarter][block][lane][16]: byte i holds the codes of k = 2i (low nibble) and 2i + 1 (high nibble) of the 32-deep
+// sub-block) followed by 2048 bytes of fp32 [A0, A1, B0, B1] per row ([quarter][lane]), weight = A code - B.
+constexpr int kQ4KCodeBytes = 4096;
+constexpr int kQ4KChunkBytes = 6144;
+__host__ __device__ inline int64_t q4k_tiled_bytes(int n, int k) {
+    return (int64_t)row_tiles(n) * k_stages(k) * kQ4KChunkBytes;
+}
+
+// Weight formats a matrix handle can hold.
+enum : int { kFmtQ8 = 0, kFmtQ4K = 1 };
+template <int kFmt>
+__host__ __device__ constexpr int chunk_bytes() { return kFmt == kFmtQ4K ? kQ4KChunkBytes : kChunkBytes; }
+
+// Device-resident quantized matrix in a tiled layout.
 struct Q8Matrix {
     int device = 0;
     int n = 0, k = 0;         // out, in features
     uint8_t* tiles = nullptr;
     float* bias = nullptr;    // n floats on the device, or nullptr
     bool owns = true;         // false for matrices over caller memory
+    int format = kFmtQ8;      // kFmtQ8: Q8_0 (and converted Q4_0) tiles; kFmtQ4K: Q4_K tiles
 };
 
 void set_error(const std::string& msg);
@@ -49,6 +64,8 @@ cudaError_t launch_q8_unpack(const uint8_t* tiles, int n, int k, uint8_t* q8, cu
 cudaError_t launch_q4_0_repack(const uint8_t* q4, int n, int k, uint8_t* tiles, cudaStream_t s);
 cudaError_t launch_q8_quantize(const float* w, int64_t rows, int64_t cols, uint8_t* q8, cudaStream_t s);
 cudaError_t launch_q8_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s);
+cudaError_t launch_q4_k_repack(const uint8_t* q4k, int n, int k, uint8_t* tiles, cudaStream_t s);
+cudaError_t launch_q4_k_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s);
 
 // The Q8_0 GEMM (q8_gemm.cu).
 struct GemmCall {

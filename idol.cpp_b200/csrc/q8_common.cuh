@@ -114,6 +114,31 @@ __device__ __forceinline__ void dequant16(uint4 c, float2 dd, float2 ncd, uint32
     }
 }
 
+// The 32 codes of one Q4_K sub-block (one uint4; byte i holds the codes of k = 2i and 2i + 1 in its low and high
+// nibble) with fp32 a = d sc and b = dmin m, as 16 packed registers of the operand type in k order. PRMT places a code
+// u in the mantissa of 32768 (f = 32768 + u exactly); one packed FMA forms f a - 32768 a = u a, exact because u a has
+// at most 21 significant bits; one packed add rounds u a - b once to fp32 - the reference's weight
+// (tools/idol_packed.py:41-54, tools/idol_triton.py:80) - and the pair is rounded to the operand type.
+template <bool kBF16>
+__device__ __forceinline__ void dequant32_q4k(uint4 c, float a, float b, uint32_t* out) {
+    const float2 aa = make_float2(a, a);
+    const float2 na = make_float2(-32768.0f * a, -32768.0f * a);
+    const float2 nb = make_float2(-b, -b);
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t sel = 0x7504u | ((uint32_t)j << 4);
+            const float f0 = __uint_as_float(__byte_perm(lo, 0x47000000u, sel));
+            const float f1 = __uint_as_float(__byte_perm(hi, 0x47000000u, sel));
+            const float2 v = __fadd2_rn(__ffma2_rn(make_float2(f0, f1), aa, na), nb);
+            out[4 * i + j] = kBF16 ? pack_bf16x2(v.x, v.y) : pack_f16x2(v.x, v.y);
+        }
+    }
+}
+
 }  // namespace q8
 
 // The streaming kernel for M <= 16 (q8_gemv.cu): the number of K splits it would use for `groups` 32-row groups and

@@ -1,4 +1,4 @@
-// q8_format.cu - the Q8_0 formats on the device.
+// q8_format.cu - the Q8_0 (and Q4_0, Q4_K) formats on the device.
 //
 // GGUF Q8_0 (the interchange format): per output row, K/32 blocks of 34 bytes: fp16 scale d, then 32 int8 codes;
 // weight = d * q (tools/idol_packed.py:28-31, tools/idol_triton.py:24-33).
@@ -85,6 +85,87 @@ __global__ void q4_0_repack_kernel(const uint8_t* __restrict__ q4, int n, int k,
     *reinterpret_cast<uint4*>(chunk + code_off(q, b, 0, lane)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *reinterpret_cast<uint4*>(chunk + code_off(q, b, 1, lane)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint16_t*>(chunk + scale_off(q, b, lane)) = d;
+}
+
+// GGUF Q4_K -> the Q4_K tiled layout. A 144-byte Q4_K super-block covers 256 k of one row: fp16 d, fp16 dmin, 12 bytes
+// packing a 6-bit scale and a 6-bit min for each of its eight 32-deep sub-blocks, then 128 bytes of 4-bit codes
+// (sub-blocks 2g and 2g + 1 are the low and high nibbles of bytes 32 g .. 32 g + 31); weight = d sc code - dmin m
+// (tools/idol_triton.py:64-82, tools/idol_packed.py:41-54). A 64-deep stage s is sub-blocks 2g, 2g + 1 of super-block
+// s / 4 with g = s % 4. The repack stores A = d sc and B = dmin m as fp32 - both products of an 11-bit and a 6-bit
+// integer, hence exact - and the codes two per byte in k order, so a kernel forms fl(A code - B): the reference's
+// fp32 weight bit for bit (A code is exact too). One warp per (row tile, stage, quarter); lane r handles row
+// 128 t + 32 q + r. The source must be 16-byte aligned (144 = 9 x 16, so every super-block is).
+__global__ void q4_k_repack_kernel(const uint8_t* __restrict__ q4k, int n, int k, uint8_t* __restrict__ tiles,
+                                   int64_t units) {
+    const int ks = k_stages(k), sbs = k / 256;
+    const int64_t unit = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (unit >= units) return;
+    const int lane = threadIdx.x % 32;
+    const int q = (int)(unit % 4);
+    const int64_t ts = unit / 4;
+    const int s = (int)(ts % ks);
+    const int t = (int)(ts / ks);
+    const int64_t row = (int64_t)t * kTileRows + q * 32 + lane;
+    uint32_t codes[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    float4 prm = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (row < n) {
+        const uint8_t* sb = q4k + (row * sbs + s / 4) * 144;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(sb);
+        const int g = s % 4;
+        uint8_t qs[32];
+        *reinterpret_cast<uint4*>(qs) = *reinterpret_cast<const uint4*>(sb + 16 + 32 * g);
+        *reinterpret_cast<uint4*>(qs + 16) = *reinterpret_cast<const uint4*>(sb + 32 + 32 * g);
+        uint8_t sc8[12];
+        *reinterpret_cast<uint32_t*>(sc8) = hdr.y;
+        *reinterpret_cast<uint32_t*>(sc8 + 4) = hdr.z;
+        *reinterpret_cast<uint32_t*>(sc8 + 8) = hdr.w;
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+        float a[2], bm[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * g + h;
+            const int sc = j < 4 ? (sc8[j] & 63) : ((sc8[j + 4] & 15) | ((sc8[j - 4] >> 6) << 4));
+            const int mn = j < 4 ? (sc8[j + 4] & 63) : ((sc8[j + 4] >> 4) | ((sc8[j] >> 6) << 4));
+            a[h] = d * (float)sc;
+            bm[h] = dmin * (float)mn;
+        }
+        prm = make_float4(a[0], a[1], bm[0], bm[1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t lo = (qs[2 * i] >> (4 * h)) & 15u, hi = (qs[2 * i + 1] >> (4 * h)) & 15u;
+                codes[h][i / 4] |= (lo | (hi << 4)) << (8 * (i % 4));
+            }
+    }
+    uint8_t* chunk = tiles + ((int64_t)t * ks + s) * kQ4KChunkBytes;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        *reinterpret_cast<uint4*>(chunk + q * 1024 + h * 512 + lane * 16) =
+            make_uint4(codes[h][0], codes[h][1], codes[h][2], codes[h][3]);
+    *reinterpret_cast<float4*>(chunk + kQ4KCodeBytes + (q * 32 + lane) * 16) = prm;
+}
+
+__global__ void q4_k_dequant_kernel(const uint8_t* __restrict__ tiles, int n, int k, void* __restrict__ out,
+                                    int dtype) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)n * k) return;
+    const int64_t row = idx / k;
+    const int col = (int)(idx % k);
+    const int ks = k_stages(k);
+    const int t = (int)(row / kTileRows), rq = (int)(row % kTileRows);
+    const int q = rq / 32, r = rq % 32, s = col / 64, b = (col % 64) / 32, e = col % 32;
+    const uint8_t* chunk = tiles + ((int64_t)t * ks + s) * kQ4KChunkBytes;
+    const int code = (chunk[q * 1024 + b * 512 + r * 16 + e / 2] >> (4 * (e % 2))) & 15;
+    const float* prm = reinterpret_cast<const float*>(chunk + kQ4KCodeBytes + (q * 32 + r) * 16);
+    const float v = fmaf(prm[b], (float)code, -prm[2 + b]);  // A code is exact: one rounding, as A * code - B
+    if (dtype == IDOL_F32)
+        static_cast<float*>(out)[idx] = v;
+    else if (dtype == IDOL_BF16)
+        static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+    else
+        static_cast<__half*>(out)[idx] = __float2half_rn(v);
 }
 
 __global__ void q8_unpack_kernel(const uint8_t* __restrict__ tiles, int n, int k, uint8_t* __restrict__ q8,
@@ -178,6 +259,20 @@ cudaError_t launch_q4_0_repack(const uint8_t* q4, int n, int k, uint8_t* tiles, 
     const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 8;
     const int warps = 8;
     q4_0_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q4, n, k, tiles, units);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_k_repack(const uint8_t* q4k, int n, int k, uint8_t* tiles, cudaStream_t s) {
+    const int64_t units = (int64_t)row_tiles(n) * k_stages(k) * 4;
+    const int warps = 8;
+    q4_k_repack_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(q4k, n, k, tiles, units);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_k_dequant(const uint8_t* tiles, int n, int k, void* w, int w_dtype, cudaStream_t s) {
+    const int64_t total = (int64_t)n * k;
+    if (total == 0) return cudaSuccess;
+    q4_k_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(tiles, n, k, w, w_dtype);
     return cudaGetLastError();
 }
 

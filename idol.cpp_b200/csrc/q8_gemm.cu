@@ -45,10 +45,11 @@ constexpr int kThreads = 64 + 32 * kDequantWarps;  // warp 0 producer, warp 1 MM
 // One stage of weights = one chunk of the tiled layout: 8192 code bytes + 512 scale bytes, one bulk copy.
 static_assert(kTileRows == kRowsPerTile && kTileK == kStageK, "the GEMM stage is the layout's chunk");
 
-template <int BN, int S>
+template <int BN, int S, int kFmt = kFmtQ8>
 struct Config {
     static constexpr int kXBytes = BN * 128;                         // BN rows of 64 bf16
-    static constexpr int kStageBytes = kXBytes + kChunkBytes;
+    static constexpr int kChunk = chunk_bytes<kFmt>();                // one stage of weights: 8704 (Q8) / 6144 (Q4_K)
+    static constexpr int kStageBytes = kXBytes + kChunk;
     static constexpr int kACol0 = BN < 32 ? 32 : BN;                 // TMEM column of A stage 0 (D at column 0)
     static constexpr int kColsNeeded = kACol0 + S * 32;
     static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
@@ -79,6 +80,27 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* chunk, int q, int l
             const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
             dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase), dd, ncd, regs + 16 * b);
             dequant16<kBF16>(*reinterpret_cast<const uint4*>(cbase + 512), dd, ncd, regs + 16 * b + 8);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) regs[16 * b + j] = 0u;
+        }
+    }
+    tmem_st16(col, *reinterpret_cast<const uint32_t(*)[16]>(regs));
+    tmem_st16(col + 16, *reinterpret_cast<const uint32_t(*)[16]>(regs + 16));
+    tmem_st_wait();
+}
+
+// The same for a Q4_K chunk: rows 32 q .. 32 q + 31, both 32-deep sub-blocks (codes two per byte, fp32 A and B of
+// the row), weights fl(A code - B) rounded to the operand type, into TMEM columns col .. col + 31.
+template <bool kBF16>
+__device__ __forceinline__ void dequant_stage_q4k(const uint8_t* chunk, int q, int lane, int blocks, uint32_t col) {
+    const float4 prm = *reinterpret_cast<const float4*>(chunk + kQ4KCodeBytes + (q * 32 + lane) * 16);
+    uint32_t regs[32];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if (b < blocks) {
+            const uint4 c = *reinterpret_cast<const uint4*>(chunk + q * 1024 + b * 512 + lane * 16);
+            dequant32_q4k<kBF16>(c, b ? prm.y : prm.x, b ? prm.w : prm.z, regs + 16 * b);
         } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) regs[16 * b + j] = 0u;
@@ -200,15 +222,15 @@ __device__ __forceinline__ void epilogue_span_staged(const Params& p, int m0, in
     }
 }
 
-template <int BN, int S, bool kBF16, typename OutT>
+template <int BN, int S, bool kBF16, typename OutT, int kFmt>
 __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Params p) {
-    using C = Config<BN, S>;
+    using C = Config<BN, S, kFmt>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // The 128-byte swizzle needs 1024-aligned tiles in the shared address space.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;                                        // S x kXBytes, each 1024-aligned
     uint8_t* ws = xs + S * C::kXBytes;                         // S x 8704: codes then scales of the stage
-    uint64_t* full = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ws + S * C::kChunk);
     uint64_t* empty = full + S;
     uint64_t* afull = empty + S;
     uint64_t* accfull = afull + S;
@@ -255,10 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
                 const int b0 = ks * 2;
                 const int nb = min(2, p.kb - b0);
                 (void)nb;
-                mbar_arrive_expect_tx(&full[s], C::kXBytes + kChunkBytes);
+                mbar_arrive_expect_tx(&full[s], C::kXBytes + C::kChunk);
                 tma_load_2d(xs + s * C::kXBytes, &xmap, ks * kStageK, m0, &full[s]);
-                bulk_load(ws + s * kChunkBytes, p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes,
-                          kChunkBytes, &full[s]);
+                bulk_load(ws + s * C::kChunk, p.tiles + ((long long)t128 * p.layout_stages + ks) * C::kChunk,
+                          C::kChunk, &full[s]);
             }
             // The last load into each stage has landed before the CTA can leave (see mbar_drain).
             for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) mbar_drain(&full[i % S], (i / S) & 1);
@@ -308,8 +330,12 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
             if (got) got = mbar_wait(&full[s], u & 1, abort_flag);
             if (!__all_sync(0xffffffffu, got)) break;  // tcgen05.st below is warp-collective
             tc_fence_after();
-            dequant_stage<kBF16>(ws + s * kChunkBytes, q, lane, min(2, p.kb - (ks_begin + i) * 2),
-                                 tmem + lane_base + C::kACol0 + s * 32);
+            if constexpr (kFmt == kFmtQ4K)
+                dequant_stage_q4k<kBF16>(ws + s * C::kChunk, q, lane, min(2, p.kb - (ks_begin + i) * 2),
+                                         tmem + lane_base + C::kACol0 + s * 32);
+            else
+                dequant_stage<kBF16>(ws + s * C::kChunk, q, lane, min(2, p.kb - (ks_begin + i) * 2),
+                                     tmem + lane_base + C::kACol0 + s * 32);
             tc_fence_before();
             __syncwarp();  // every lane's stores are complete and fenced before lane 0 reports the warp
             if (lane == 0) mbar_arrive(&afull[s]);
@@ -780,10 +806,10 @@ int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtenso
     return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
 }
 
-template <int BN, int S, bool kBF16, typename OutT>
+template <int BN, int S, bool kBF16, typename OutT, int kFmt>
 int launch(const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits, cudaStream_t stream) {
-    using C = Config<BN, S>;
-    auto kern = q8_gemm_kernel<BN, S, kBF16, OutT>;
+    using C = Config<BN, S, kFmt>;
+    auto kern = q8_gemm_kernel<BN, S, kBF16, OutT, kFmt>;
     static unsigned long long configured = 0;  // one bit per device: the shared-memory opt-in is set once
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -807,18 +833,25 @@ int launch(const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, i
     return IDOL_OK;
 }
 
-template <bool kBF16, typename OutT>
-int dispatch(int bn, const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits,
-             cudaStream_t stream) {
+template <bool kBF16, typename OutT, int kFmt>
+int dispatch_fmt(int bn, const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits,
+                 cudaStream_t stream) {
     switch (bn) {
-        case 16: return launch<16, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
-        case 32: return launch<32, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
-        case 64: return launch<64, 6, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
-        case 128: return launch<128, 4, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 16: return launch<16, 6, kBF16, OutT, kFmt>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 32: return launch<32, 6, kBF16, OutT, kFmt>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 64: return launch<64, 6, kBF16, OutT, kFmt>(xmap, p, tiles_n, tiles_m, splits, stream);
+        case 128: return launch<128, 4, kBF16, OutT, kFmt>(xmap, p, tiles_n, tiles_m, splits, stream);
         // Five stages (204 KB): at M = 16384 the fifth stage hides the TMA latency that four leave exposed (measured
         // +6-16% on B200); six do not fit.
-        default: return launch<256, 5, kBF16, OutT>(xmap, p, tiles_n, tiles_m, splits, stream);
+        default: return launch<256, 5, kBF16, OutT, kFmt>(xmap, p, tiles_n, tiles_m, splits, stream);
     }
+}
+
+template <bool kBF16, typename OutT>
+int dispatch(int fmt, int bn, const CUtensorMap& xmap, const Params& p, int tiles_n, int tiles_m, int splits,
+             cudaStream_t stream) {
+    return fmt == kFmtQ4K ? dispatch_fmt<kBF16, OutT, kFmtQ4K>(bn, xmap, p, tiles_n, tiles_m, splits, stream)
+                          : dispatch_fmt<kBF16, OutT, kFmtQ8>(bn, xmap, p, tiles_n, tiles_m, splits, stream);
 }
 
 int env_int(const char* name, int fallback) {
@@ -916,7 +949,8 @@ int q8_gemm(const GemmCall& c) {
     // 512->512 layers: 0.50 against 0.57 ms per MLP step); with longer K the single-CTA kernel is 5-15% faster.
     // IDOL_B200_GEMM_PAIR = 1 / 0 forces it on (for 128- or 256-token tiles) / off.
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
-    const bool pair = bn >= 128 && (forced_pair == 1 ||
+    const bool q8 = w.format == kFmtQ8;  // the persistent kernels read Q8_0 tiles only
+    const bool pair = q8 && bn >= 128 && (forced_pair == 1 ||
                                     (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
     // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator, a 2-byte output leaving
     // through a staging tile and TMA stores): measured on B200 it pays at K <= 1024 once the 192-token tiles number
@@ -926,7 +960,7 @@ int q8_gemm(const GemmCall& c) {
     const bool staged = staged_output_ok(c);
     const int forced_persist = env_int("IDOL_B200_GEMM_PERSIST", -1);
     const long long tiles192 = (long long)tiles_n * ((c.m + 191) / 192);
-    const bool persist1 = !pair && bn >= 256 &&
+    const bool persist1 = q8 && !pair && bn >= 256 &&
                           (forced_persist == 1 || (forced_persist != 0 && staged && p.stages_total <= 16 &&
                                                    tiles192 >= 8LL * num_sms(w.device)));
     if (pair || persist1) {
@@ -984,13 +1018,13 @@ int q8_gemm(const GemmCall& c) {
 
     const bool bf16 = c.x_dtype == IDOL_BF16;
     if (c.y_dtype == IDOL_F32)
-        return bf16 ? dispatch<true, float>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
-                    : dispatch<false, float>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+        return bf16 ? dispatch<true, float>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                    : dispatch<false, float>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
     if (c.y_dtype == IDOL_BF16)
-        return bf16 ? dispatch<true, __nv_bfloat16>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
-                    : dispatch<false, __nv_bfloat16>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
-    return bf16 ? dispatch<true, __half>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
-                : dispatch<false, __half>(bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+        return bf16 ? dispatch<true, __nv_bfloat16>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                    : dispatch<false, __nv_bfloat16>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+    return bf16 ? dispatch<true, __half>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
+                : dispatch<false, __half>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
 }
 
 }  // namespace idol

@@ -1,4 +1,4 @@
-// q8_gemv.cu - the Q8_0 linear for decode-sized batches (1 <= M <= 16 tokens): Y = X . dequant(W)^T + bias (+ residual)
+// q8_gemv.cu - the Q8_0 (and Q4_K) linear for decode-sized batches (1 <= M <= 16 tokens): Y = X . dequant(W)^T + bias (+ residual)
 // (-> act), the small-M strategy of the reference's GPU path (tools/idol_triton.py:36-126 fused_linear at M <= 16,
 // src/kernels.cpp:246-296 gemm_quant on the CPU).
 //
@@ -85,7 +85,7 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 __device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // grid: x = 32-row groups of the output window, z = K splits (a cluster along z when > 1); kThreads threads.
-template <bool kBF16, typename OutT>
+template <bool kBF16, typename OutT, int kFmt>
 __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const Params p, const GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int krange = a.stages_per_split * 64;
@@ -103,17 +103,26 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const Params p, const
     const int ks1 = min(ks0 + a.stages_per_split, p.stages_total);
 
     // 1. This warp's codes and scales: stages ks0 + warp and ks0 + warp + kWarps, all loads in flight at once.
-    uint4 codes[2][4];
+    // Q8_0: four 16-code loads and two fp16 scales per stage; Q4_K: two 32-code loads and one [A0, A1, B0, B1] load.
+    constexpr int kCodeLoads = kFmt == kFmtQ4K ? 2 : 4;
+    uint4 codes[2][kCodeLoads];
     uint16_t scales[2][2];
+    uint4 prm[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int ks = ks0 + warp + i * kWarps;
         if (ks < ks1) {
-            const uint8_t* chunk = p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes;
+            const uint8_t* chunk = p.tiles + ((long long)t128 * p.layout_stages + ks) * chunk_bytes<kFmt>();
+            if constexpr (kFmt == kFmtQ4K) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) codes[i][j] = ld_stream_v4(chunk + q * 2048 + j * 512 + lane * 16);
-            scales[i][0] = ld_stream_u16(chunk + kChunkCodeBytes + q * 128 + lane * 2);
-            scales[i][1] = ld_stream_u16(chunk + kChunkCodeBytes + q * 128 + 64 + lane * 2);
+                for (int j = 0; j < 2; ++j) codes[i][j] = ld_stream_v4(chunk + q * 1024 + j * 512 + lane * 16);
+                prm[i] = ld_stream_v4(chunk + kQ4KCodeBytes + (q * 32 + lane) * 16);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) codes[i][j] = ld_stream_v4(chunk + q * 2048 + j * 512 + lane * 16);
+                scales[i][0] = ld_stream_u16(chunk + kChunkCodeBytes + q * 128 + lane * 2);
+                scales[i][1] = ld_stream_u16(chunk + kChunkCodeBytes + q * 128 + 64 + lane * 2);
+            }
         }
     }
     grid_dependents_launch();
@@ -158,13 +167,20 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const Params p, const
         const int ks = ks0 + warp + i * kWarps;
         if (ks >= ks1) break;
         uint32_t w[32];
+        if constexpr (kFmt == kFmtQ4K) {
+            const float4 pf = make_float4(__uint_as_float(prm[i].x), __uint_as_float(prm[i].y),
+                                          __uint_as_float(prm[i].z), __uint_as_float(prm[i].w));
+            dequant32_q4k<kBF16>(codes[i][0], pf.x, pf.z, w);
+            dequant32_q4k<kBF16>(codes[i][1], pf.y, pf.w, w + 16);
+        } else {
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            const float d = __half2float(__ushort_as_half(scales[i][b]));
-            const float2 dd = make_float2(d, d);
-            const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
-            dequant16<kBF16>(codes[i][2 * b], dd, ncd, w + 16 * b);
-            dequant16<kBF16>(codes[i][2 * b + 1], dd, ncd, w + 16 * b + 8);
+            for (int b = 0; b < 2; ++b) {
+                const float d = __half2float(__ushort_as_half(scales[i][b]));
+                const float2 dd = make_float2(d, d);
+                const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
+                dequant16<kBF16>(codes[i][2 * b], dd, ncd, w + 16 * b);
+                dequant16<kBF16>(codes[i][2 * b + 1], dd, ncd, w + 16 * b + 8);
+            }
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -238,9 +254,9 @@ int smem_bytes(int stages_per_split) {
     return kTokens * (stages_per_split * 64 * 2 + 16) + kWarps * kWarpTileBytes + kTokens * 32 * 4;
 }
 
-template <bool kBF16, typename OutT>
-int launch(const Params& p, const GemvArgs& a, int groups, int splits, cudaStream_t stream) {
-    auto kern = q8_gemv_kernel<kBF16, OutT>;
+template <bool kBF16, typename OutT, int kFmt>
+int launch_fmt(const Params& p, const GemvArgs& a, int groups, int splits, cudaStream_t stream) {
+    auto kern = q8_gemv_kernel<kBF16, OutT, kFmt>;
     const int smem = smem_bytes(a.stages_per_split);
     static unsigned long long configured = 0;  // one bit per device: the shared-memory opt-in is set once
     int dev = 0;
@@ -281,6 +297,12 @@ int launch(const Params& p, const GemvArgs& a, int groups, int splits, cudaStrea
     return IDOL_OK;
 }
 
+template <bool kBF16, typename OutT>
+int launch(int fmt, const Params& p, const GemvArgs& a, int groups, int splits, cudaStream_t stream) {
+    return fmt == kFmtQ4K ? launch_fmt<kBF16, OutT, kFmtQ4K>(p, a, groups, splits, stream)
+                          : launch_fmt<kBF16, OutT, kFmtQ8>(p, a, groups, splits, stream);
+}
+
 }  // namespace
 
 // K splits for the streaming kernel: as few as the kMaxStagesPerCta limit allows. Measured on B200 (CUDA graphs,
@@ -301,14 +323,15 @@ int q8_gemv(const GemmCall& c, const Params& p, int splits) {
     a.ldx = c.ldx;
     a.stages_per_split = (p.stages_total + splits - 1) / splits;
     const bool bf16 = c.x_dtype == IDOL_BF16;
+    const int fmt = c.w->format;
     if (c.y_dtype == IDOL_F32)
-        return bf16 ? launch<true, float>(p, a, groups, splits, c.stream)
-                    : launch<false, float>(p, a, groups, splits, c.stream);
+        return bf16 ? launch<true, float>(fmt, p, a, groups, splits, c.stream)
+                    : launch<false, float>(fmt, p, a, groups, splits, c.stream);
     if (c.y_dtype == IDOL_BF16)
-        return bf16 ? launch<true, __nv_bfloat16>(p, a, groups, splits, c.stream)
-                    : launch<false, __nv_bfloat16>(p, a, groups, splits, c.stream);
-    return bf16 ? launch<true, __half>(p, a, groups, splits, c.stream)
-                : launch<false, __half>(p, a, groups, splits, c.stream);
+        return bf16 ? launch<true, __nv_bfloat16>(fmt, p, a, groups, splits, c.stream)
+                    : launch<false, __nv_bfloat16>(fmt, p, a, groups, splits, c.stream);
+    return bf16 ? launch<true, __half>(fmt, p, a, groups, splits, c.stream)
+                : launch<false, __half>(fmt, p, a, groups, splits, c.stream);
 }
 
 }  // namespace idol

@@ -22,6 +22,8 @@ Q8_0_KIND = 8  # tools/idol_triton.py kind code for GGML Q8_0
 Q4_0_KIND = 4  # ... and for GGML Q4_0
 _GGML_Q8_0 = 8  # gguf.GGMLQuantizationType.Q8_0 enum value
 _GGML_Q4_0 = 2  # gguf.GGMLQuantizationType.Q4_0 enum value
+Q4_K_KIND = 44  # ... and for GGML Q4_K
+_GGML_Q4_K = 12  # gguf.GGMLQuantizationType.Q4_K enum value
 
 _DTYPES = {torch.float32: C.F32, torch.float16: C.F16, torch.bfloat16: C.BF16}
 
@@ -82,6 +84,34 @@ def repack_q4_0(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
     return tiles
 
 
+def q4_k_bytes(n: int, k: int) -> int:
+    v = C.lib().idol_b200_q4_k_bytes(n, k)
+    if v < 0:
+        raise ValueError(f"invalid Q4_K shape ({n}, {k}): K must be a positive multiple of 256")
+    return v
+
+
+def q4_k_tiled_bytes(n: int, k: int) -> int:
+    v = C.lib().idol_b200_q4_k_tiled_bytes(n, k)
+    if v < 0:
+        raise ValueError(f"invalid Q4_K shape ({n}, {k}): K must be a positive multiple of 256")
+    return v
+
+
+def repack_q4_k(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """GGUF Q4_K bytes (CUDA uint8) -> the Q4_K tiled layout: 4-bit codes plus fp32 A = d sc and B = dmin m per
+    32-deep sub-block, from which the kernels form the reference's fp32 weight A code - B exactly
+    (tools/idol_packed.py:41-54)."""
+    if not packed.is_cuda or packed.dtype != torch.uint8 or packed.numel() != q4_k_bytes(n, k):
+        raise ValueError("repack_q4_k: expected CUDA uint8 Q4_K bytes of the given shape")
+    packed = packed.contiguous()
+    if packed.data_ptr() % 16:
+        packed = packed.clone()
+    tiles = torch.empty(q4_k_tiled_bytes(n, k), dtype=torch.uint8, device=packed.device)
+    C.check(C.lib().idol_b200_q4_k_repack(_ptr(packed), n, k, _ptr(tiles), _stream(packed.device)))
+    return tiles
+
+
 def unpack(tiles: torch.Tensor, n: int, k: int) -> torch.Tensor:
     """Tiled layout -> GGUF Q8_0 bytes, the exact inverse of ``repack``."""
     out = torch.empty(q8_bytes(n, k), dtype=torch.uint8, device=tiles.device)
@@ -94,15 +124,26 @@ _views: "collections.OrderedDict[tuple, int]" = collections.OrderedDict()
 _VIEW_CACHE = 4096
 
 
+def _tiles_format(tiles, n, k):
+    """Q8_0 (also converted Q4_0) or Q4_K tiles, told apart by their size (8704 or 6144 bytes per chunk)."""
+    if tiles.numel() == tiled_bytes(n, k):
+        return 0
+    if k % 256 == 0 and tiles.numel() == q4_k_tiled_bytes(n, k):
+        return 1
+    raise ValueError(f"tiles of {tiles.numel()} bytes are neither Q8_0 nor Q4_K tiles of shape ({n}, {k})")
+
+
 def _view(tiles, bias, n, k, device_index):
     """A C-ABI matrix handle over tensors the caller holds (cached; a handle is a few host bytes)."""
-    key = (tiles.data_ptr(), 0 if bias is None else bias.data_ptr(), n, k, device_index)
+    fmt = _tiles_format(tiles, n, k)
+    key = (tiles.data_ptr(), 0 if bias is None else bias.data_ptr(), n, k, device_index, fmt)
     h = _views.get(key)
     if h is not None:
         _views.move_to_end(key)
         return h
     out = ctypes.c_void_p()
-    C.check(C.lib().idol_b200_q8_view(_ptr(tiles), _ptr(bias), n, k, device_index, ctypes.byref(out)))
+    make = C.lib().idol_b200_q4_k_view if fmt == 1 else C.lib().idol_b200_q8_view
+    C.check(make(_ptr(tiles), _ptr(bias), n, k, device_index, ctypes.byref(out)))
     _views[key] = out.value
     if len(_views) > _VIEW_CACHE:
         _, old = _views.popitem(last=False)
@@ -133,7 +174,8 @@ def _aligned_rows(x2: torch.Tensor) -> torch.Tensor:
 @torch.library.custom_op("idol_b200::q8_linear", mutates_args=())
 def q8_linear(x: torch.Tensor, tiles: torch.Tensor, bias: Optional[torch.Tensor], n: int, k: int, act: int = 0,
               flags: int = 0) -> torch.Tensor:
-    """x [..., k] bf16/f16 -> [..., n] in x's dtype; tiles from ``repack``; bias is fp32 [n] or None."""
+    """x [..., k] bf16/f16 -> [..., n] in x's dtype; tiles from ``repack`` / ``repack_q4_0`` / ``repack_q4_k``; bias
+    is fp32 [n] or None."""
     x2 = _aligned_rows(x.reshape(-1, k))
     y = torch.empty((x2.shape[0], n), dtype=x.dtype, device=x.device)
     if x2.shape[0]:
@@ -158,7 +200,8 @@ def _tiled_for(packed: torch.Tensor, n: int, k: int, kind: int = Q8_0_KIND):
     if hit is not None and hit[0]() is packed:
         _tiled_cache.move_to_end(key)
         return hit[1]
-    tiles = repack_q4_0(packed, n, k) if kind == Q4_0_KIND else repack(packed, n, k)
+    pack = {Q4_0_KIND: repack_q4_0, Q4_K_KIND: repack_q4_k}.get(kind, repack)
+    tiles = pack(packed, n, k)
     _tiled_cache[key] = (weakref.ref(packed), tiles)
     if len(_tiled_cache) > 256:
         _tiled_cache.popitem(last=False)
@@ -166,10 +209,10 @@ def _tiled_for(packed: torch.Tensor, n: int, k: int, kind: int = Q8_0_KIND):
 
 
 def fused_linear(value, packed, shape, kind, bias=None):
-    """Multiply FP16/BF16 activations by Q8_0 (kind 8) or Q4_0 (kind 4) weights on CUDA, with the contract of
-    tools/idol_triton.py:94-126: same argument checks and ValueError messages, output in value's dtype, bias added
-    after the product is rounded to that dtype. Q4_0 runs the same kernels (an exact conversion to the tiled Q8_0
-    layout); Q4_K (kind 44) is not part of this build and raises ValueError."""
+    """Multiply FP16/BF16 activations by Q8_0 (kind 8), Q4_0 (kind 4) or Q4_K (kind 44) weights on CUDA, with the
+    contract of tools/idol_triton.py:94-126: same argument checks and ValueError messages, output in value's dtype,
+    bias added after the product is rounded to that dtype. Q4_0 runs the Q8_0 kernels (an exact conversion to the
+    tiled Q8_0 layout); Q4_K runs them on its own tiled layout, which the kernels dequantise as A code - B."""
     if (not value.is_cuda or not packed.is_cuda or packed.dtype != torch.uint8
             or value.device != packed.device or value.dtype not in (torch.float16, torch.bfloat16)
             or len(shape) != 2 or value.shape[-1] != shape[1] or kind not in (4, 8, 44)):
@@ -182,8 +225,6 @@ def fused_linear(value, packed, shape, kind, bias=None):
         raise ValueError('invalid packed linear dimensions')
     if bias is not None and (bias.shape != (n,) or bias.device != value.device or bias.dtype != value.dtype):
         raise ValueError('invalid fused linear bias')
-    if kind not in (Q8_0_KIND, Q4_0_KIND):
-        raise ValueError('unsupported fused linear input: only Q8_0 and Q4_0 are implemented on sm_100a')
     tiles = _tiled_for(packed, n, k, kind)
     b32 = None if bias is None else bias.float()
     return torch.ops.idol_b200.q8_linear(value, tiles, b32, n, k, C.ACT_NONE, C.EPI_BIAS_AFTER_ROUND)
@@ -191,17 +232,17 @@ def fused_linear(value, packed, shape, kind, bias=None):
 
 # ----------------------------------------------------------------------------------- PackedLinear (drop-in)
 class PackedLinear(torch.nn.Module):
-    """Mirror of tools/idol_packed.py:12-82 for Q8_0 and Q4_0 matrices: keeps the GGUF bytes as the ``packed`` buffer,
-    and when ``fused`` is set and the input is CUDA fp16/bf16 without grad, runs the sm_100a kernels on a tiled copy
-    made once per device. Unfused calls expand the weights (our dequant kernel on CUDA) and use F.linear, as the
-    reference's expansion path does. The reference's other expansion-only kinds (F16, Q2_K, Q4_K, Q6_K) are outside
-    this build and raise ValueError here."""
+    """Mirror of tools/idol_packed.py:12-82 for Q8_0, Q4_0 and Q4_K matrices (the kinds the reference's fused path
+    takes): keeps the GGUF bytes as the ``packed`` buffer, and when ``fused`` is set and the input is CUDA fp16/bf16
+    without grad, runs the sm_100a kernels on a tiled copy made once per device. Unfused calls expand the weights (our
+    dequant kernels on CUDA) and use F.linear, as the reference's expansion path does. The reference's expansion-only
+    kinds (F16, Q2_K, Q6_K) are outside this build and raise ValueError here."""
 
     def __init__(self, source, bias):
         super().__init__()
         self.shape = tuple(reversed([int(s) for s in source.shape]))
         self.kind = int(source.tensor_type)
-        if len(self.shape) != 2 or self.kind not in (_GGML_Q8_0, _GGML_Q4_0):
+        if len(self.shape) != 2 or self.kind not in (_GGML_Q8_0, _GGML_Q4_0, _GGML_Q4_K):
             raise ValueError("unsupported packed matrix")
         import numpy as np
         self.register_buffer("packed", torch.from_numpy(np.array(source.data, copy=True)).reshape(-1))
@@ -213,7 +254,7 @@ class PackedLinear(torch.nn.Module):
         # Valid while it was made from this very buffer at this version (moving the module replaces the buffer).
         if (self._tiled is None or self._tiled[0]() is not self.packed
                 or self._tiled[1] != self.packed._version):
-            pack = repack_q4_0 if self.kind == _GGML_Q4_0 else repack
+            pack = {_GGML_Q4_0: repack_q4_0, _GGML_Q4_K: repack_q4_k}.get(self.kind, repack)
             self._tiled = (weakref.ref(self.packed), self.packed._version, pack(self.packed, *self.shape))
         return self._tiled[2]
 
@@ -221,6 +262,18 @@ class PackedLinear(torch.nn.Module):
         n, k = self.shape
         if self.packed.is_cuda:
             return dequantize_tiled(self._tiles(), n, k, dtype)
+        if self.kind == _GGML_Q4_K:  # 144-byte super-blocks of 256: d, dmin, 6-bit scales / mins, 4-bit codes
+            blocks = self.packed.reshape(-1, 144)
+            d = blocks[:, :2].contiguous().view(torch.float16).float()
+            dmin = blocks[:, 2:4].contiguous().view(torch.float16).float()
+            sm = blocks[:, 4:16].reshape(-1, 3, 4)
+            lo, mid, top = sm[:, 0], sm[:, 1], sm[:, 2]
+            sc = torch.cat((lo & 63, (top & 15) | ((lo >> 2) & 48)), dim=1).float()
+            mn = torch.cat((mid & 63, (top >> 4) | ((mid >> 2) & 48)), dim=1).float()
+            q = blocks[:, 16:].reshape(-1, 4, 1, 32)
+            codes = torch.cat(((q & 15), (q >> 4)), dim=2).reshape(-1, 8, 32).float()
+            w = (d * sc).reshape(-1, 8, 1) * codes - (dmin * mn).reshape(-1, 8, 1)
+            return w.reshape(self.shape).to(dtype)
         if self.kind == _GGML_Q4_0:  # 18-byte blocks: fp16 d, then low nibbles = elements 0-15, high = 16-31
             blocks = self.packed.reshape(-1, 18)
             nib = blocks[:, 2:]
@@ -235,7 +288,7 @@ class PackedLinear(torch.nn.Module):
         needs_grad = torch.is_grad_enabled() and (value.requires_grad or
                                                   (self.bias is not None and self.bias.requires_grad))
         if self.fused and value.is_cuda and value.dtype in (torch.float16, torch.bfloat16) and not needs_grad:
-            kind = Q4_0_KIND if self.kind == _GGML_Q4_0 else Q8_0_KIND
+            kind = {_GGML_Q4_0: Q4_0_KIND, _GGML_Q4_K: Q4_K_KIND}.get(self.kind, Q8_0_KIND)
             return fused_linear(value, self.packed, self.shape, kind, self.bias)
         return F.linear(value, self.dequantize(value.dtype), self.bias)
 
@@ -251,7 +304,9 @@ def enable_fused_packed(model):
 
 
 def dequantize_tiled(tiles, n, k, dtype=torch.float32):
-    """Dense [n, k] weights d * q from the tiled layout (fp32 exact; bf16/fp16 rounded from the fp32 product)."""
+    """Dense [n, k] weights from Q8_0 tiles (d q) or Q4_K tiles (A code - B): fp32 exact, bf16/fp16 rounded from the
+    fp32 value."""
     out = torch.empty((n, k), dtype=dtype, device=tiles.device)
-    C.check(C.lib().idol_b200_q8_dequantize(_ptr(tiles), n, k, _ptr(out), _DTYPES[out.dtype], _stream(tiles.device)))
+    fn = C.lib().idol_b200_q4_k_dequantize if _tiles_format(tiles, n, k) == 1 else C.lib().idol_b200_q8_dequantize
+    C.check(fn(_ptr(tiles), n, k, _ptr(out), _DTYPES[out.dtype], _stream(tiles.device)))
     return out

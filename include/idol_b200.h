@@ -76,6 +76,18 @@ int idol_b200_q8_unpack(const void* tiles, int out, int in, void* q8, void* stre
 int64_t idol_b200_q4_0_bytes(int out, int in);
 int idol_b200_q4_0_repack(const void* q4_0, int out, int in, void* tiles, void* stream);
 
+/* GGUF Q4_K (fused_linear kind 44, tools/idol_triton.py:64-82, 103-104; tools/idol_packed.py:41-54 dequantize): 144
+ * bytes per 256 weights of a row (fp16 d, fp16 dmin, 12 bytes of 6-bit sub-block scales and mins, 128 bytes of
+ * 4-bit codes), weight = d sc code - dmin m. `in` must be a positive multiple of 256. q4_k_repack converts it into
+ * the Q4_K tiled layout (q4_k_tiled_bytes bytes; both pointers 16-byte aligned), which keeps fp32 A = d sc and
+ * B = dmin m per 32-deep sub-block so that the kernels form the reference's fp32 weight A code - B exactly.
+ * idol_b200_q4_k_view (below) wraps such tiles in a matrix handle for idol_b200_q8_gemm and the block / MLP
+ * builders; q4_k_dequantize writes the dense [out, in] weights (f32 exact; bf16 / f16 rounded from the f32 value). */
+int64_t idol_b200_q4_k_bytes(int out, int in);
+int64_t idol_b200_q4_k_tiled_bytes(int out, int in);
+int idol_b200_q4_k_repack(const void* q4_k, int out, int in, void* tiles, void* stream);
+int idol_b200_q4_k_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream);
+
 /* Tiled layout -> dense out x in weights d * q (w_dtype IDOL_F32 exact; IDOL_BF16 / IDOL_F16 rounded from the fp32
  * product). Replaces src/kernels.cpp:535-550 dequantize_linear and tools/idol_packed.py:25-31 dequantize. */
 int idol_b200_q8_dequantize(const void* tiles, int out, int in, void* w, int w_dtype, void* stream);
@@ -99,6 +111,9 @@ int idol_b200_q8_import(const void* q8_dev, int64_t nbytes, int out, int in, con
 /* A matrix handle over a tiled buffer (and an optional fp32 bias) that the caller already holds on `device`, e.g.
  * tensors of a PyTorch module; nothing is allocated on the device and idol_b200_q8_free releases only the handle. */
 int idol_b200_q8_view(const void* tiles, const float* bias_dev, int out, int in, int device, idol_q8_matrix** matrix);
+/* The same over Q4_K tiles (idol_b200_q4_k_repack); idol_b200_q8_export refuses such a handle. */
+int idol_b200_q4_k_view(const void* tiles, const float* bias_dev, int out, int in, int device,
+                        idol_q8_matrix** matrix);
 
 int idol_b200_q8_free(idol_q8_matrix* matrix);
 

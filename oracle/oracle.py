@@ -40,6 +40,7 @@ def lib():
         L.orc_q8_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_q4_0_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_q4_0_to_q8.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _u8p]
+        L.orc_q4_k_dequantize.argtypes = [_u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
         L.orc_panel_blob_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
         L.orc_panel_blob_bytes.restype = ctypes.c_int64
         L.orc_q8_to_panels.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p]
@@ -126,6 +127,15 @@ def q4_0_dequantize(q4: np.ndarray, rows: int, cols: int) -> np.ndarray:
     q4 = np.ascontiguousarray(q4, dtype=np.uint8)
     out = np.empty((rows, cols), np.float32)
     lib().orc_q4_0_dequantize(_ptr(q4, _u8p), rows, cols, _ptr(out))
+    return out
+
+
+def q4_k_dequantize(q4k: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """GGUF Q4_K bytes -> fp32 [rows, cols] (the reference's expansion, tools/idol_packed.py:41-54)."""
+    q4k = np.ascontiguousarray(q4k, dtype=np.uint8).reshape(-1)
+    assert q4k.size == rows * (cols // 256) * 144 and cols % 256 == 0
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_q4_k_dequantize(_ptr(q4k, _u8p), rows, cols, _ptr(out))
     return out
 
 

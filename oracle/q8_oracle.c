@@ -161,6 +161,36 @@ void orc_q4_0_to_q8(const uint8_t* q4, int64_t rows, int64_t cols, uint8_t* q8) 
 }
 
 /* ------------------------------------------------------------------------------------------------------------------
+ * GGUF Q4_K (kind 44): 144-byte super-blocks of 256 elements: fp16 d, fp16 dmin, 12 bytes of 6-bit scales and mins
+ * for the eight 32-element sub-blocks (sub-block j < 4: scale = s[j] & 63, min = s[j + 4] & 63; j >= 4: scale =
+ * (s[j + 4] & 15) | (s[j - 4] >> 6) << 4, min = (s[j + 4] >> 4) | (s[j] >> 6) << 4), then 128 bytes of codes
+ * (sub-blocks 2g and 2g + 1 are the low and high nibbles of bytes 32 g .. 32 g + 31). Element = (d scale) code -
+ * dmin min in fp32, each product formed first: restates tools/idol_packed.py:41-54 (the expansion path) and
+ * tools/idol_triton.py:64-82 (the fused kernel's decoder), and gguf-py 0.19.0 Q4_K.dequantize_blocks.
+ * ---------------------------------------------------------------------------------------------------------------- */
+void orc_q4_k_dequantize(const uint8_t* blocks, int64_t rows, int64_t cols, float* w) {
+    const int64_t nsb = cols / 256;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t b = 0; b < nsb; ++b) {
+            const uint8_t* sb = blocks + (r * nsb + b) * 144;
+            const float d = orc_f16_to_f32((uint16_t)(sb[0] | (sb[1] << 8)));
+            const float dmin = orc_f16_to_f32((uint16_t)(sb[2] | (sb[3] << 8)));
+            const uint8_t* s = sb + 4;
+            const uint8_t* qs = sb + 16;
+            for (int j = 0; j < 8; ++j) {
+                const int sc = j < 4 ? (s[j] & 63) : ((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
+                const int mn = j < 4 ? (s[j + 4] & 63) : ((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+                const float a = d * (float)sc, bm = dmin * (float)mn;
+                for (int i = 0; i < 32; ++i) {
+                    const int code = (qs[(j / 2) * 32 + i] >> (4 * (j % 2))) & 15;
+                    const float prod = a * (float)code;
+                    w[r * cols + b * 256 + j * 32 + i] = prod - bm;
+                }
+            }
+        }
+}
+
+/* ------------------------------------------------------------------------------------------------------------------
  * Q8_0 -> idol panel blob, bits 8, group 32: restates tools/gguf_to_decoder.py:16-40 (code = q + 128, scale = fp16 d,
  * min = fp16(-128 d), rejected unless exact) and tools/idolq.py:137-166 (16 output columns per panel; per group a 64-byte
  * header of 16 fp16 scales then 16 fp16 minimums, then 32 rows of k x 16 columns of codes). Returns 0, or -1 when a

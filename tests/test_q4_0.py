@@ -95,8 +95,14 @@ def test_packed_linear_q4_0_meets_the_reference_bar(pkg, cuda, dtype):
 
 
 @pytest.mark.gpu
-def test_q4_k_is_refused_with_the_references_error_type(pkg, cuda):
-    n, k = 16, 256
-    packed = torch.zeros(n * (k // 256) * 144, dtype=torch.uint8, device=cuda)
-    with pytest.raises(ValueError, match="only Q8_0 and Q4_0"):
-        pkg.fused_linear(torch.zeros(2, k, device=cuda, dtype=torch.bfloat16), packed, (n, k), 44)
+def test_fused_linear_keeps_the_references_argument_errors(pkg, cuda):
+    """Wrong byte counts and a K that is not a multiple of the kind's group raise ValueError for every kind."""
+    x = torch.zeros(2, 256, device=cuda, dtype=torch.bfloat16)
+    for kind, size in ((8, 16 * 8 * 34), (4, 16 * 8 * 18), (44, 16 * 144)):
+        with pytest.raises(ValueError, match="invalid packed linear dimensions"):
+            pkg.fused_linear(x, torch.zeros(size + 1, dtype=torch.uint8, device=cuda), (16, 256), kind)
+    with pytest.raises(ValueError, match="invalid packed linear dimensions"):
+        pkg.fused_linear(torch.zeros(2, 96, device=cuda, dtype=torch.bfloat16),
+                         torch.zeros(16 * 144, dtype=torch.uint8, device=cuda), (16, 96), 44)
+    with pytest.raises(ValueError, match="unsupported fused linear input"):
+        pkg.fused_linear(x, torch.zeros(16 * 8 * 34, dtype=torch.uint8, device=cuda), (16, 256), 6)
