@@ -377,12 +377,15 @@ def run_ours(args, rank, world, local_rank):
     block_ms = measure_block(pkg, dev, stream, block_steps, world)
     mlp_steps = max(3, min(args.steps, 30))
     mlp_ms = measure_mlp(pkg, dev, stream, mlp_steps, world)
+    gs_steps = max(3, min(args.steps, 20))
+    gs_ms = measure_gs_block(pkg, dev, stream, gs_steps, world)
     status = max(status, pkg._capi.device_status(local_rank))
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, status, block_ms, mlp_ms = float(t[0]), float(t[1]), int(t[2]), float(t[3]), float(t[4])
+        gs_ms = float(t[5])
     clk = clocks.stop(wall0, wall1) if rank == 0 else None
     if rank != 0:
         return
@@ -443,6 +446,13 @@ def run_ours(args, rank, world, local_rank):
                   "frac_tensor": round(BLOCK_FLOPS / (block_ms / block_steps / 1e3) / 1e12 / tc_peak, 3),
                   "scaling": "weak (each GPU runs its own images; no collective)",
                   "work": "343.6 GFLOP per step (206.2 linears + 137.4 attention)"},
+        "gaussian_block": {"metric": "Gaussian-decoder block steps/s (src/decoders.cpp:296-313: 8192 anchors, "
+                                     "self-attention, cross-attention to 8192 latent tokens x 16 conditions, MLP "
+                                     "1024->4096->1024, D 1024, 16 heads, fp32 residual)",
+                           "value": round(gs_steps * world / (gs_ms / 1e3), 2), "unit": "block-steps/s",
+                           "ms_per_step": round(gs_ms / gs_steps, 3), "steps": gs_steps,
+                           "tflops": round(GS_FLOPS * gs_steps * world / (gs_ms / 1e3) / 1e12, 1),
+                           "work": f"{GS_FLOPS / 1e9:.1f} GFLOP per step"},
         "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
                                    "heads)", "value": round(MLP_POINTS * mlp_steps * world / (mlp_ms / 1e3), 0),
                          "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
@@ -508,6 +518,10 @@ def run_profile_shape(args):
 BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
 BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
+GS_ANCHORS, GS_LATENTS, GS_COND = 8192, 8192, 16
+GS_FLOPS = (2.0 * GS_ANCHORS * (3 + 1 + 1 + 1 + 2 * BLOCK_H // BLOCK_D) * BLOCK_D * BLOCK_D
+            + 4.0 * GS_ANCHORS * GS_ANCHORS * BLOCK_D + 4.0 * GS_ANCHORS * GS_LATENTS * BLOCK_D
+            + 2.0 * GS_LATENTS * GS_COND * 2 * BLOCK_D)
 MLP_POINTS = 262144
 MLP_FLOPS = 2.0 * MLP_POINTS * (128 * 512 + 512 * 512 + 512 * 14)
 
@@ -553,6 +567,29 @@ def measure_block(pkg, dev, stream, steps, world):
     x = torch.randn((BLOCK_IMAGES * BLOCK_TOKENS, D), device=dev, generator=g)
     blk.forward_(x, images=BLOCK_IMAGES)  # sizes the workspace outside the graph
     return _graph_ms(torch, stream, lambda: blk.forward_(x, images=BLOCK_IMAGES), steps, world)
+
+
+def measure_gs_block(pkg, dev, stream, steps, world):
+    """The real Gaussian decoder's block (src/decoders.cpp:296-313) at its model size: 8192 anchors attending to
+    themselves and to 8192 latent tokens of 16 conditions, D 1024, 16 heads, fp32 residual stream in place."""
+    import torch
+    from idol_b200.block import GaussianBlock, Q8Weight
+    g = torch.Generator(device=dev).manual_seed(78)
+    D, H = BLOCK_D, BLOCK_H
+    w = {}
+    for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "cq": (D, D), "co": (D, D), "ff1": (H, D),
+                         "ff2": (D, H)}.items():
+        w[name] = Q8Weight.from_float(torch.randn((n, k), device=dev, generator=g) * 0.02,
+                                      torch.randn(n, device=dev, generator=g) * 0.01)
+    vec = [1 + 0.1 * torch.randn(D, device=dev, generator=g) for _ in range(5)] + [
+        0.1 * torch.randn(D, device=dev, generator=g)]
+    blk = GaussianBlock(w["qkv"], w["out"], w["cq"], w["co"], w["ff1"], w["ff2"], *vec,
+                        torch.randn((2 * D, GS_COND), device=dev, generator=g) * 0.25,
+                        torch.randn(2 * D, device=dev, generator=g) * 0.01, BLOCK_HEADS)
+    x = torch.randn((GS_ANCHORS, D), device=dev, generator=g)
+    cond = torch.randn((GS_LATENTS, GS_COND), device=dev, generator=g)
+    blk.forward_(x, cond)  # sizes the workspace outside the graph
+    return _graph_ms(torch, stream, lambda: blk.forward_(x, cond), steps, world)
 
 
 def measure_mlp(pkg, dev, stream, steps, world):

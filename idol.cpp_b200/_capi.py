@@ -51,6 +51,10 @@ SIGNATURES = {
     "idol_b200_block_free": (_i32, [_vp]),
     "idol_b200_block_workspace_bytes": (_i64, [_vp, _i64]),
     "idol_b200_block_forward": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp]),
+    "idol_b200_gs_block_create": (_i32, [_vp] * 14 + [_i32, _i32, ctypes.c_float, ctypes.POINTER(_vp)]),
+    "idol_b200_gs_block_free": (_i32, [_vp]),
+    "idol_b200_gs_block_workspace_bytes": (_i64, [_vp, _i64, _i64]),
+    "idol_b200_gs_block_forward": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
     "idol_b200_gaussian_mlp_create": (_i32, [_vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "idol_b200_gaussian_mlp_free": (_i32, [_vp]),
     "idol_b200_gaussian_mlp_workspace_bytes": (_i64, [_vp, _i64]),

@@ -4,6 +4,8 @@
                      made once from GGUF Q8_0 bytes, as src/weights.cpp + quantized_linear make theirs once.
 * ``DenoiserBlock`` - scope row A14: LN -> QKV -> rms q,k -> attention -> out + res -> LN -> ff1 (GELU tanh) -> ff2 +
                      res (src/decoders.cpp:296-313 without the cross-attention), in place on the residual stream.
+* ``GaussianBlock`` - the Gaussian decoder's block (src/decoders.cpp:296-313): the same plus a cross-attention to
+                     the latent tokens between the self-attention and the MLP.
 * ``GaussianMLP``  - scope row A15: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14 -> activated heads.
 
 Workspaces are device tensors owned by the Python objects and reused across calls.
@@ -105,6 +107,61 @@ class DenoiserBlock:
         if h:
             try:
                 C.lib().idol_b200_block_free(ctypes.c_void_p(h))
+            except Exception:
+                pass
+            self.handle = None
+
+
+class GaussianBlock:
+    """The Gaussian decoder's block (src/decoders.cpp:296-313): DenoiserBlock's sublayers plus the cross-attention to
+    the latent tokens. Weights: Q8Weight for qkv/out/cross_q/cross_out/ff1/ff2; fp32 tensors for the gammas, norm2's
+    gamma/beta ([D]) and the dense to_kv weight [2D, cond_dim] and bias [2D]."""
+
+    def __init__(self, qkv: Q8Weight, out: Q8Weight, cross_q: Q8Weight, cross_out: Q8Weight, ff1: Q8Weight,
+                 ff2: Q8Weight, q_gamma, k_gamma, cross_q_gamma, cross_k_gamma, norm2_gamma, norm2_beta,
+                 kv_weight: torch.Tensor, kv_bias: Optional[torch.Tensor], heads: int, eps: float = 1e-6):
+        self.weights = (qkv, out, cross_q, cross_out, ff1, ff2)
+        dev = qkv.device
+
+        def f32(t):
+            return t.detach().to(device=dev, dtype=torch.float32).contiguous()
+
+        self.vectors = [f32(t) for t in (q_gamma, k_gamma, cross_q_gamma, cross_k_gamma, norm2_gamma, norm2_beta)]
+        self.kv_weight = f32(kv_weight)
+        self.kv_bias = None if kv_bias is None else f32(kv_bias)
+        self.cond_dim = self.kv_weight.shape[1]
+        h = ctypes.c_void_p()
+        C.check(C.lib().idol_b200_gs_block_create(*(ctypes.c_void_p(w.handle) for w in self.weights),
+                                                  *(_ptr(v) for v in self.vectors), _ptr(self.kv_weight),
+                                                  _ptr(self.kv_bias), self.cond_dim, heads, float(eps),
+                                                  ctypes.byref(h)))
+        self.handle = h.value
+        self.dim, self.heads, self.device = out.out, heads, dev
+        self.ws = _Workspace()
+
+    def workspace_bytes(self, rows: int, cond_rows_total: int) -> int:
+        return int(C.lib().idol_b200_gs_block_workspace_bytes(ctypes.c_void_p(self.handle), rows, cond_rows_total))
+
+    def forward_(self, x: torch.Tensor, cond: torch.Tensor, images: int = 1) -> torch.Tensor:
+        """In place on x: [images * tokens, D] (fp32 or bf16, contiguous); cond: fp32 [images * cond_rows,
+        cond_dim] on the same device."""
+        if not x.is_contiguous() or x.dim() != 2 or x.shape[1] != self.dim or x.shape[0] % images:
+            raise ValueError("GaussianBlock: x must be a contiguous [images * tokens, D] tensor")
+        if (cond.dtype != torch.float32 or not cond.is_contiguous() or cond.dim() != 2
+                or cond.shape[1] != self.cond_dim or cond.shape[0] % images or cond.device != x.device):
+            raise ValueError("GaussianBlock: cond must be a contiguous fp32 [images * cond_rows, cond_dim] tensor")
+        rows, crows = x.shape[0], cond.shape[0]
+        ws = self.ws.get(self.workspace_bytes(rows, crows), x.device)
+        C.check(C.lib().idol_b200_gs_block_forward(ctypes.c_void_p(self.handle), _ptr(x), _DTYPES[x.dtype],
+                                                   rows // images, images, _ptr(cond), crows // images, _ptr(ws),
+                                                   ws.numel(), _stream(x.device)))
+        return x
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            try:
+                C.lib().idol_b200_gs_block_free(ctypes.c_void_p(h))
             except Exception:
                 pass
             self.handle = None

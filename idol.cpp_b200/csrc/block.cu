@@ -12,6 +12,10 @@
 //       x = f W_ff2^T + b + x                            q8 GEMM, residual in place
 //   The residual stream x is fp32 (as the reference's X) or bf16; everything a GEMM reads is bf16.
 //
+//   Gaussian decoder block (src/decoders.cpp:296-313, with the cross-attention): the block above with, between the
+//   self-attention and the MLP, h = LN(x) * gamma2 + beta2; q = rms(h W_q^T); kv = cond W_kv^T + b (dense fp32,
+//   the 16-wide condition), rms on k; a = attention of each image's rows over its cond rows; x = a W_o^T + b + x.
+//
 //   Gaussian MLP (scope row A15, config 4): 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the output heads
 //   (pos identity, scale exp, rotation f * 0.1 + (1, 0, 0, 0) normalised as src/decoders.cpp:422-428, colour and
 //   opacity sigmoid as :429).
@@ -64,6 +68,38 @@ __global__ void gaussian_heads_kernel(const void* __restrict__ raw, int dtype, l
     for (int c = 10; c < 14; ++c) o[c] = 1.0f / (1.0f + expf(-f[c]));
 }
 
+// The cross-attention's key/value projection of the latent tokens (src/decoders.cpp:237, `to_kv`, which the
+// reference keeps as a dense fp32 matrix since its depth is the 16-wide condition): kv[r, j] = sum_c cond[r, c]
+// w[j, c] (fp32 FMA chain in c order) + b[j], stored as bf16 [rows, 2D]. A block takes 256 output columns and 16 rows:
+// each thread keeps its column's weights in registers, the rows' conditions are staged in shared memory.
+constexpr int kKvMaxCond = 64;
+__global__ void kv_project_kernel(const float* __restrict__ cond, long long rows, int cdim,
+                                  const float* __restrict__ w, const float* __restrict__ b, int cols,
+                                  __nv_bfloat16* __restrict__ kv) {
+    __shared__ float cs[16][kKvMaxCond];
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const long long r0 = (long long)blockIdx.y * 16;
+    for (int i = threadIdx.x; i < 16 * cdim; i += blockDim.x) {
+        const long long r = r0 + i / cdim;
+        cs[i / cdim][i % cdim] = r < rows ? cond[r * cdim + i % cdim] : 0.0f;
+    }
+    __syncthreads();
+    if (j >= cols) return;
+    float wr[kKvMaxCond];
+#pragma unroll
+    for (int c = 0; c < kKvMaxCond; ++c) wr[c] = c < cdim ? w[(long long)j * cdim + c] : 0.0f;
+    const float bj = b ? b[j] : 0.0f;
+    for (int i = 0; i < 16; ++i) {
+        const long long r = r0 + i;
+        if (r >= rows) break;
+        float acc = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kKvMaxCond; ++c)
+            if (c < cdim) acc = fmaf(cs[i][c], wr[c], acc);
+        kv[r * cols + j] = __float2bfloat16_rn(acc + bj);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
@@ -86,6 +122,19 @@ struct idol_block {
     const float* k_gamma;
     int heads, dim, hidden, device;
     float eps;
+};
+
+struct idol_gs_block {
+    idol_block self;                     // LN -> QKV -> rms -> self-attention -> out, and the MLP
+    const idol_q8_matrix* cross_q;
+    const idol_q8_matrix* cross_out;
+    const float* cq_gamma;
+    const float* ck_gamma;
+    const float* norm2_gamma;
+    const float* norm2_beta;
+    const float* kv_w;                   // fp32 [2D, cond_dim]
+    const float* kv_b;                   // fp32 [2D] or NULL
+    int cond_dim;
 };
 
 struct idol_gaussian_mlp {
@@ -167,6 +216,111 @@ int idol_b200_block_forward(const idol_block* b, void* x, int x_dtype, int64_t t
     if (rc != IDOL_OK) return rc;
     rc = gemm(b->out, h, rows, D, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
     if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
+                                     nullptr, s));
+    rc = gemm(b->ff1, h, rows, D, nullptr, 0, IDOL_ACT_GELU_TANH, big, IDOL_BF16, b->hidden, s);
+    if (rc != IDOL_OK) return rc;
+    return gemm(b->ff2, big, rows, b->hidden, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+}
+
+int idol_b200_gs_block_create(const idol_q8_matrix* qkv, const idol_q8_matrix* out, const idol_q8_matrix* cross_q,
+                              const idol_q8_matrix* cross_out, const idol_q8_matrix* ff1, const idol_q8_matrix* ff2,
+                              const float* q_gamma, const float* k_gamma, const float* cross_q_gamma,
+                              const float* cross_k_gamma, const float* norm2_gamma, const float* norm2_beta,
+                              const float* kv_weight, const float* kv_bias, int cond_dim, int heads, float eps,
+                              idol_gs_block** block) {
+    if (!block) return fail(IDOL_ERR_INVALID, "gs_block_create: block is NULL");
+    *block = nullptr;
+    idol_block* self = nullptr;
+    int rc = idol_b200_block_create(qkv, out, ff1, ff2, q_gamma, k_gamma, heads, eps, &self);
+    if (rc != IDOL_OK) return rc;
+    const int D = self->dim;
+    if (!cross_q || !cross_out || !cross_q_gamma || !cross_k_gamma || !norm2_gamma || !norm2_beta || !kv_weight) {
+        delete self;
+        return fail(IDOL_ERR_INVALID, "gs_block_create: NULL");
+    }
+    if (cross_q->m.n != D || cross_q->m.k != D || cross_out->m.n != D || cross_out->m.k != D ||
+        cross_q->m.device != self->device || cross_out->m.device != self->device) {
+        delete self;
+        return fail(IDOL_ERR_INVALID, "gs_block_create: cross q and out must be D x D on the block's device");
+    }
+    if (cond_dim < 1 || cond_dim > idol::kKvMaxCond) {
+        delete self;
+        return fail(IDOL_ERR_UNSUPPORTED, "gs_block_create: cond_dim must be 1..64");
+    }
+    *block = new idol_gs_block{*self, cross_q, cross_out, cross_q_gamma, cross_k_gamma, norm2_gamma, norm2_beta,
+                               kv_weight, kv_bias, cond_dim};
+    delete self;
+    return IDOL_OK;
+}
+
+int idol_b200_gs_block_free(idol_gs_block* block) {
+    delete block;
+    return IDOL_OK;
+}
+
+int64_t idol_b200_gs_block_workspace_bytes(const idol_gs_block* b, int64_t rows, int64_t cond_rows_total) {
+    if (!b || rows < 0 || cond_rows_total < 0) return -1;
+    return idol_b200_block_workspace_bytes(&b->self, rows) + align256(cond_rows_total * 2 * b->self.dim * 2);
+}
+
+int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int64_t tokens, int images,
+                               const float* cond, int64_t cond_rows, void* workspace, int64_t workspace_bytes,
+                               void* stream) {
+    if (!g || !x || !cond) return fail(IDOL_ERR_INVALID, "gs_block_forward: NULL");
+    if (x_dtype != IDOL_F32 && x_dtype != IDOL_BF16)
+        return fail(IDOL_ERR_UNSUPPORTED, "gs_block_forward: x is f32 or bf16");
+    if (tokens < 1 || images < 1 || cond_rows < 1)
+        return fail(IDOL_ERR_INVALID, "gs_block_forward: tokens, images and cond_rows must be >= 1");
+    if (cond_rows * images > 65535LL * 16)
+        return fail(IDOL_ERR_INVALID, "gs_block_forward: more than 1,048,560 condition rows in one call");
+    const idol_block* b = &g->self;
+    const int64_t rows = tokens * images, crows = cond_rows * images;
+    if (!workspace || workspace_bytes < idol_b200_gs_block_workspace_bytes(g, rows, crows) ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(IDOL_ERR_INVALID, "gs_block_forward: workspace smaller than idol_b200_gs_block_workspace_bytes "
+                                      "or not 256-byte aligned");
+    IDOL_CUDA(cudaSetDevice(b->device));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int D = b->dim;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int64_t self_bytes = idol_b200_block_workspace_bytes(b, rows);
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws);                            // rows x D
+    __nv_bfloat16* big = reinterpret_cast<__nv_bfloat16*>(ws + align256(rows * D * 2));  // rows x max(3D, H)
+    __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(ws + self_bytes);              // crows x 2D
+
+    // Self-attention sublayer.
+    IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
+                                     nullptr, s));
+    int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
+    if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, 3 * D, rows, b->heads, b->q_gamma, s));
+    IDOL_CUDA(idol::launch_rms_heads(big + D, IDOL_BF16, 3 * D, rows, b->heads, b->k_gamma, s));
+    idol::AttentionCall sa = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
+    rc = idol::attention(sa);
+    if (rc != IDOL_OK) return rc;
+    rc = gemm(b->out, h, rows, D, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+    if (rc != IDOL_OK) return rc;
+
+    // Cross-attention sublayer (src/decoders.cpp:304-306, 232-240).
+    IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, g->norm2_gamma, g->norm2_beta,
+                                     nullptr, nullptr, s));
+    rc = gemm(g->cross_q, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, D, s);
+    if (rc != IDOL_OK) return rc;
+    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, D, rows, b->heads, g->cq_gamma, s));
+    {
+        const dim3 grid((unsigned)((2 * D + 255) / 256), (unsigned)((crows + 15) / 16));
+        idol::kv_project_kernel<<<grid, 256, 0, s>>>(cond, crows, g->cond_dim, g->kv_w, g->kv_b, 2 * D, kv);
+        IDOL_CUDA(cudaGetLastError());
+    }
+    IDOL_CUDA(idol::launch_rms_heads(kv, IDOL_BF16, 2 * D, crows, b->heads, g->ck_gamma, s));
+    idol::AttentionCall ca = {big, kv, kv + D, h, tokens, cond_rows, D, 2 * D, D, b->heads, 64, images, s};
+    rc = idol::attention(ca);
+    if (rc != IDOL_OK) return rc;
+    rc = gemm(g->cross_out, h, rows, D, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+    if (rc != IDOL_OK) return rc;
+
+    // MLP sublayer.
     IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
                                      nullptr, s));
     rc = gemm(b->ff1, h, rows, D, nullptr, 0, IDOL_ACT_GELU_TANH, big, IDOL_BF16, b->hidden, s);

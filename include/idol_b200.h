@@ -177,6 +177,28 @@ int64_t idol_b200_block_workspace_bytes(const idol_block* block, int64_t rows);
 int idol_b200_block_forward(const idol_block* block, void* x, int x_dtype, int64_t tokens, int images, void* workspace,
                             int64_t workspace_bytes, void* stream);
 
+/* The Gaussian decoder's block (src/decoders.cpp:296-313, next-row (f)1): the block above with a cross-attention
+ * sublayer between the self-attention and the MLP: h = LN(x, eps) * norm2_gamma + norm2_beta; q = h W_q^T (cross_q,
+ * D x D) then rms_heads with cross_q_gamma; kv = cond W_kv^T + kv_bias with W_kv dense fp32 [2D, cond_dim] on the
+ * device (the reference keeps this 16-deep `to_kv` in fp32), then rms_heads of its k half with cross_k_gamma; each
+ * image's rows attend over that image's cond_rows latent rows (src/decoders.cpp:232-240); x += a W_o^T + b
+ * (cross_out, D x D). cond_dim 1..64 (the real decoder's is 16); all vectors fp32 on the device. */
+typedef struct idol_gs_block idol_gs_block;
+int idol_b200_gs_block_create(const idol_q8_matrix* qkv, const idol_q8_matrix* out, const idol_q8_matrix* cross_q,
+                              const idol_q8_matrix* cross_out, const idol_q8_matrix* ff1, const idol_q8_matrix* ff2,
+                              const float* q_gamma, const float* k_gamma, const float* cross_q_gamma,
+                              const float* cross_k_gamma, const float* norm2_gamma, const float* norm2_beta,
+                              const float* kv_weight, const float* kv_bias, int cond_dim, int heads, float eps,
+                              idol_gs_block** block);
+int idol_b200_gs_block_free(idol_gs_block* block);
+/* Device workspace for `rows` = tokens * images rows and cond_rows_total = cond_rows * images condition rows. */
+int64_t idol_b200_gs_block_workspace_bytes(const idol_gs_block* block, int64_t rows, int64_t cond_rows_total);
+/* x: [images * tokens, D] residual stream (IDOL_F32 or IDOL_BF16), in place; cond: fp32 [images * cond_rows,
+ * cond_dim] on the device, image i's latent rows at i * cond_rows. */
+int idol_b200_gs_block_forward(const idol_gs_block* block, void* x, int x_dtype, int64_t tokens, int images,
+                               const float* cond, int64_t cond_rows, void* workspace, int64_t workspace_bytes,
+                               void* stream);
+
 /* The Gaussian decoder MLP of config 4 (scope row A15): x [points, in] bf16 -> l0 (SiLU) -> l1 (SiLU) -> l2 (14
  * outputs) -> heads: pos identity, scale exp, rotation r = f * 0.1 + (1, 0, 0, 0) divided by max(|r|, 1e-12)
  * (src/decoders.cpp:422-428 with the default lr_rotation), colour and opacity sigmoid (:429). out: fp32 [points, 14]; raw_out: fp32 [points, 14] pre-activation values, or NULL. */

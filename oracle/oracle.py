@@ -246,6 +246,45 @@ def block_forward(x, layers, heads, eps=1e-6, images=1):
     return x
 
 
+def gs_block_forward(x, cond, layers, heads, eps=1e-6, images=1, bf16_stream=False):
+    """The Gaussian decoder's block (src/decoders.cpp:296-313), composed from the pinned functions in the reference's
+    order: LN -> QKV -> rms q,k -> self-attention -> out + res; LN * gamma2 + beta2 -> cross-attention
+    (src/decoders.cpp:232-240: q = h Wq, rms q; kv = cond Wkv + b with the dense fp32 to_kv, rms k; attention of the
+    image's rows over its cond rows) -> out + res; LN -> ff1 -> gelu_tanh -> ff2 + res.
+    x: [images * L, D]; cond: [images * Lc, cond_dim] fp32; layers: the block's dict plus cq, co (q8, bias, N, K),
+    kv_w [2D, cond_dim], kv_b [2D], cq_gamma, ck_gamma, norm2_gamma, norm2_beta. bf16_stream: the residual stream
+    is stored in bf16, so x is rounded to bf16 after each residual sublayer (as a bf16 caller's stream is)."""
+    rnd = f32_to_bf16_round if bf16_stream else (lambda v: v)
+    x = c32(x)
+    cond = c32(cond)
+    rows, D = x.shape
+    hd = D // heads
+    L = rows // images
+    Lc = cond.shape[0] // images
+    h = norm_rows(x, eps)
+    qkv = gemm_q8(h, *layers["qkv"])
+    qkv = rms_heads(qkv, heads, hd, layers["q_gamma"], col0=0)
+    qkv = rms_heads(qkv, heads, hd, layers["k_gamma"], col0=D)
+    a = np.empty((rows, D), np.float32)
+    for i in range(images):
+        blk = qkv[i * L:(i + 1) * L]
+        a[i * L:(i + 1) * L] = attention(blk[:, :D], np.ascontiguousarray(blk[:, D:2 * D]),
+                                         np.ascontiguousarray(blk[:, 2 * D:]), heads, hd)
+    x = rnd(gemm_q8(a, *layers["out"], residual=x))
+    h = norm_rows(x, eps, layers["norm2_gamma"], layers["norm2_beta"])
+    q = rms_heads(gemm_q8(h, *layers["cq"]), heads, hd, layers["cq_gamma"], col0=0)
+    kv = (cond.astype(np.float64) @ c32(layers["kv_w"]).astype(np.float64).T + layers["kv_b"]).astype(np.float32)
+    kv = rms_heads(kv, heads, hd, layers["ck_gamma"], col0=0)
+    for i in range(images):
+        kvi = kv[i * Lc:(i + 1) * Lc]
+        a[i * L:(i + 1) * L] = attention(q[i * L:(i + 1) * L], np.ascontiguousarray(kvi[:, :D]),
+                                         np.ascontiguousarray(kvi[:, D:]), heads, hd)
+    x = rnd(gemm_q8(a, *layers["co"], residual=x))
+    h = norm_rows(x, eps)
+    f = gemm_q8(h, *layers["ff1"], act=ACT_GELU_TANH)
+    return rnd(gemm_q8(f, *layers["ff2"], residual=x))
+
+
 def gaussian_mlp(x, layers):
     """Synthetic Gaussian MLP: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the activated heads."""
     h = gemm_q8(x, *layers[0], act=ACT_SILU)
