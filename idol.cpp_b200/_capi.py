@@ -55,6 +55,12 @@ SIGNATURES = {
     "idol_b200_gs_block_free": (_i32, [_vp]),
     "idol_b200_gs_block_workspace_bytes": (_i64, [_vp, _i64, _i64]),
     "idol_b200_gs_block_forward": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
+    "idol_b200_gs_decoder_create": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, ctypes.c_float, _vp,
+                                            ctypes.POINTER(_vp)]),
+    "idol_b200_gs_decoder_free": (_i32, [_vp]),
+    "idol_b200_gs_decoder_workspace_bytes": (_i64, [_vp, _i64, _i64]),
+    "idol_b200_gs_decoder_features": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp]),
+    "idol_b200_gs_to_gaussians": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "idol_b200_gaussian_mlp_create": (_i32, [_vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "idol_b200_gaussian_mlp_free": (_i32, [_vp]),
     "idol_b200_gaussian_mlp_workspace_bytes": (_i64, [_vp, _i64]),

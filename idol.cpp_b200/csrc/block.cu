@@ -27,6 +27,7 @@
 #include <cmath>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "internal.h"
 
@@ -66,6 +67,75 @@ __global__ void gaussian_heads_kernel(const void* __restrict__ raw, int dtype, l
     for (int c = 0; c < 4; ++c) o[6 + c] = r[c] / nrm;
 #pragma unroll
     for (int c = 10; c < 14; ++c) o[c] = 1.0f / (1.0f + expf(-f[c]));
+}
+
+// The Gaussian decoder's input (src/decoders.cpp:289-290): x[r, j] = sum_c points[r, c] w_in[j, c] (fp32 FMA chain)
+// + b_in[j] + pos_embed(points[r])[j], where pos_embed (src/decoders.cpp:215-230) is sin((v f) pi) for column
+// 2 c fd + i and cos((v f) pi) for 2 c fd + fd + i (v the row's coordinate c, f = freqs[i]), zero from 6 fd on.
+// The sines use the full-range sinf/cosf: the angles reach thousands of radians. Written as bf16 (the next GEMM's
+// input). One thread per element.
+constexpr float kPiF = 3.14159265358979323846f;
+__global__ void gs_input_kernel(const float* __restrict__ points, long long rows, int dim,
+                                const float* __restrict__ w, const float* __restrict__ b,
+                                const float* __restrict__ freqs, int fd, __nv_bfloat16* __restrict__ out) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= rows * dim) return;
+    const long long r = idx / dim;
+    const int j = (int)(idx % dim);
+    const float p0 = points[r * 3], p1 = points[r * 3 + 1], p2 = points[r * 3 + 2];
+    float acc = fmaf(p0, w[j * 3], 0.0f);
+    acc = fmaf(p1, w[j * 3 + 1], acc);
+    acc = fmaf(p2, w[j * 3 + 2], acc);
+    float v = acc + (b ? b[j] : 0.0f);
+    if (j < 6 * fd) {
+        const int c = j / (2 * fd), i = j % (2 * fd);
+        const float coord = c == 0 ? p0 : (c == 1 ? p1 : p2);
+        const float ang = (coord * freqs[i < fd ? i : i - fd]) * kPiF;
+        v += i < fd ? sinf(ang) : cosf(ang);
+    }
+    out[idx] = __float2bfloat16_rn(v);
+}
+
+// Decoders::to_gaussians (src/decoders.cpp:393-433), one thread per Gaussian (anchor a, g < G): from the anchor's
+// 15 G raw features, offset xyz = tanh(f lr_xyz + perturbation) 0.5 perturbe softplus(f_os + base_offset_scale)
+// placed around the anchor and shifted by -0.5; colour f lr_dc; scale sqrt(softplus(f lr_scaling + scale_offset)^2 +
+// kernel^2); rotation (f lr_rotation + (1, 0, 0, 0)) normalised (|.| floored at 1e-12); opacity sigmoid(f lr_opacity
+// + opacity_offset). softplus(x) = x above 20, else log1p(exp(x)) (src/decoders.cpp:90). The offsets are computed
+// on the host in double as the reference does.
+struct GsRep {
+    float perturbe, kernel, lr_xyz, lr_dc, lr_opacity, lr_scaling, lr_rotation, scale_offset, opacity_offset,
+        base_offset_scale;
+};
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+__global__ void to_gaussians_kernel(const float* __restrict__ anchors, long long rows, const float* __restrict__ f,
+                                    int G, const float* __restrict__ perturbation, GsRep rp,
+                                    float* __restrict__ xyz, float* __restrict__ f_dc, float* __restrict__ scale,
+                                    float* __restrict__ rotation, float* __restrict__ opacity) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * G) return;
+    const long long a = i / G;
+    const int g = (int)(i % G);
+    const float* fa = f + a * (long long)G * 15;
+    const float offset_scale = softplus_f(fa[G * 14 + g] + rp.base_offset_scale);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float o = tanhf(fa[g * 3 + c] * rp.lr_xyz + perturbation[g * 3 + c]) * 0.5f * rp.perturbe *
+                        offset_scale;
+        xyz[i * 3 + c] = (o + anchors[a * 3 + c]) - 0.5f;
+        f_dc[i * 3 + c] = fa[G * 3 + g * 3 + c] * rp.lr_dc;
+        const float sp = softplus_f(fa[G * 6 + g * 3 + c] * rp.lr_scaling + rp.scale_offset);
+        scale[i * 3 + c] = sqrtf(sp * sp + rp.kernel * rp.kernel);
+    }
+    float q[4], norm = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        q[c] = fa[G * 9 + g * 4 + c] * rp.lr_rotation + (c == 0 ? 1.0f : 0.0f);
+        norm += q[c] * q[c];
+    }
+    norm = fmaxf(sqrtf(norm), 1e-12f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) rotation[i * 4 + c] = q[c] / norm;
+    opacity[i] = 1.0f / (1.0f + expf(-(fa[G * 13 + g] * rp.lr_opacity + rp.opacity_offset)));
 }
 
 // The cross-attention's key/value projection of the latent tokens (src/decoders.cpp:237, `to_kv`, which the
@@ -135,6 +205,18 @@ struct idol_gs_block {
     const float* kv_w;                   // fp32 [2D, cond_dim]
     const float* kv_b;                   // fp32 [2D] or NULL
     int cond_dim;
+};
+
+struct idol_gs_decoder {
+    std::vector<const idol_gs_block*> blocks;
+    const float* in_w;                   // fp32 [D, 3]
+    const float* in_b;                   // fp32 [D] or NULL
+    const idol_q8_matrix* input_layer;   // D x D
+    const idol_q8_matrix* out_proj;      // per_anchor * 15 x D
+    const float* freqs;                  // fp32 [n_freqs]
+    int n_freqs, per_anchor, dim, device;
+    const float* perturbation;           // fp32 [per_anchor * 3]
+    idol::GsRep rep;
 };
 
 struct idol_gaussian_mlp {
@@ -326,6 +408,113 @@ int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int
     rc = gemm(b->ff1, h, rows, D, nullptr, 0, IDOL_ACT_GELU_TANH, big, IDOL_BF16, b->hidden, s);
     if (rc != IDOL_OK) return rc;
     return gemm(b->ff2, big, rows, b->hidden, x, D, IDOL_ACT_NONE, x, x_dtype, D, s);
+}
+
+int idol_b200_gs_decoder_create(const idol_gs_block* const* blocks, int nblocks, const float* in_w, const float* in_b,
+                                const idol_q8_matrix* input_layer, const idol_q8_matrix* out_proj, const float* freqs,
+                                int n_freqs, int per_anchor, const float* perturbation, float base_offset_scale,
+                                const float* rep, idol_gs_decoder** decoder) {
+    if (!decoder) return fail(IDOL_ERR_INVALID, "gs_decoder_create: decoder is NULL");
+    *decoder = nullptr;
+    if (nblocks < 0 || (nblocks > 0 && !blocks) || !in_w || !input_layer || !out_proj || !freqs || !perturbation ||
+        !rep)
+        return fail(IDOL_ERR_INVALID, "gs_decoder_create: NULL");
+    const int D = input_layer->m.n;
+    if (input_layer->m.k != D || out_proj->m.k != D || per_anchor < 1 || out_proj->m.n != per_anchor * 15)
+        return fail(IDOL_ERR_INVALID, "gs_decoder_create: input_layer D x D and out_proj (15 per_anchor) x D expected");
+    if (n_freqs < 0 || 6 * n_freqs > D) return fail(IDOL_ERR_INVALID, "gs_decoder_create: 6 n_freqs must be <= D");
+    if (!idol::norm_dim_ok(D)) return fail(IDOL_ERR_UNSUPPORTED, "gs_decoder_create: width not supported by norm_rows");
+    const int dev = input_layer->m.device;
+    for (int i = 0; i < nblocks; ++i)
+        if (!blocks[i] || blocks[i]->self.dim != D || blocks[i]->self.device != dev)
+            return fail(IDOL_ERR_INVALID, "gs_decoder_create: every block must have width D on the decoder's device");
+    if (out_proj->m.device != dev) return fail(IDOL_ERR_INVALID, "gs_decoder_create: matrices on different devices");
+    // rep: perturbe, kernel, scaling_bias, opacity_bias, lr_xyz, lr_dc, lr_opacity, lr_scaling, lr_rotation
+    // (src/weights.hpp:25-28); the two activation offsets in double as src/decoders.cpp:397-399 forms them.
+    const double sb = rep[2], ob = rep[3];
+    if (!(sb > 0.0) || !(ob > 0.0 && ob < 1.0))
+        return fail(IDOL_ERR_INVALID, "gs_decoder_create: scaling_bias > 0 and 0 < opacity_bias < 1 expected");
+    idol::GsRep rp = {rep[0], rep[1], rep[4], rep[5], rep[6], rep[7], rep[8],
+                      (float)(sb + std::log(-std::expm1(-sb))), (float)std::log(ob / (1.0 - ob)), base_offset_scale};
+    auto* d = new idol_gs_decoder();
+    d->blocks.assign(blocks, blocks + nblocks);
+    d->in_w = in_w;
+    d->in_b = in_b;
+    d->input_layer = input_layer;
+    d->out_proj = out_proj;
+    d->freqs = freqs;
+    d->n_freqs = n_freqs;
+    d->per_anchor = per_anchor;
+    d->dim = D;
+    d->device = dev;
+    d->perturbation = perturbation;
+    d->rep = rp;
+    *decoder = d;
+    return IDOL_OK;
+}
+
+int idol_b200_gs_decoder_free(idol_gs_decoder* decoder) {
+    delete decoder;
+    return IDOL_OK;
+}
+
+int64_t idol_b200_gs_decoder_workspace_bytes(const idol_gs_decoder* d, int64_t rows, int64_t cond_rows) {
+    if (!d || rows < 0 || cond_rows < 0) return -1;
+    int64_t blk = 0;
+    for (const idol_gs_block* b : d->blocks) {
+        const int64_t v = idol_b200_gs_block_workspace_bytes(b, rows, cond_rows);
+        blk = v > blk ? v : blk;
+    }
+    const int64_t own = align256(rows * d->dim * 4) + align256(rows * d->dim * 2);  // x (fp32) + h (bf16)
+    return own + blk;
+}
+
+int idol_b200_gs_decoder_features(const idol_gs_decoder* d, const float* points, int64_t rows, const float* cond,
+                                  int64_t cond_rows, float* features, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+    if (!d || !points || !features || (!d->blocks.empty() && !cond))
+        return fail(IDOL_ERR_INVALID, "gs_decoder_features: NULL");
+    if (rows < 1 || cond_rows < 1) return fail(IDOL_ERR_INVALID, "gs_decoder_features: rows and cond_rows >= 1");
+    if (!workspace || workspace_bytes < idol_b200_gs_decoder_workspace_bytes(d, rows, cond_rows) ||
+        reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(IDOL_ERR_INVALID, "gs_decoder_features: workspace smaller than "
+                                      "idol_b200_gs_decoder_workspace_bytes or not 256-byte aligned");
+    IDOL_CUDA(cudaSetDevice(d->device));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int D = d->dim;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* x = reinterpret_cast<float*>(ws);                                          // rows x D fp32
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(ws + align256(rows * D * 4));  // rows x D bf16
+    uint8_t* blk_ws = ws + align256(rows * D * 4) + align256(rows * D * 2);
+    const int64_t blk_bytes = workspace_bytes - (blk_ws - ws);
+
+    const long long n = rows * D;
+    idol::gs_input_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(points, rows, D, d->in_w, d->in_b, d->freqs,
+                                                                       d->n_freqs, h);
+    IDOL_CUDA(cudaGetLastError());
+    int rc = gemm(d->input_layer, h, rows, D, nullptr, 0, IDOL_ACT_NONE, x, IDOL_F32, D, s);
+    if (rc != IDOL_OK) return rc;
+    for (const idol_gs_block* b : d->blocks) {
+        rc = idol_b200_gs_block_forward(b, x, IDOL_F32, rows, 1, cond, cond_rows, blk_ws, blk_bytes, stream);
+        if (rc != IDOL_OK) return rc;
+    }
+    IDOL_CUDA(idol::launch_norm_rows(x, IDOL_F32, D, h, IDOL_BF16, D, rows, D, 1e-5f, nullptr, nullptr, nullptr,
+                                     nullptr, s));
+    return gemm(d->out_proj, h, rows, D, nullptr, 0, IDOL_ACT_NONE, features, IDOL_F32, d->out_proj->m.n, s);
+}
+
+int idol_b200_gs_to_gaussians(const idol_gs_decoder* d, const float* anchors, int64_t rows, const float* features,
+                              float* xyz, float* f_dc, float* scale, float* rotation, float* opacity, void* stream) {
+    if (!d || !anchors || !features || !xyz || !f_dc || !scale || !rotation || !opacity)
+        return fail(IDOL_ERR_INVALID, "gs_to_gaussians: NULL");
+    if (rows < 0) return fail(IDOL_ERR_INVALID, "gs_to_gaussians: rows < 0");
+    if (rows == 0) return IDOL_OK;
+    IDOL_CUDA(cudaSetDevice(d->device));
+    const long long n = rows * d->per_anchor;
+    idol::to_gaussians_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        anchors, rows, features, d->per_anchor, d->perturbation, d->rep, xyz, f_dc, scale, rotation, opacity);
+    IDOL_CUDA(cudaGetLastError());
+    return IDOL_OK;
 }
 
 int idol_b200_gaussian_mlp_create(const idol_q8_matrix* l0, const idol_q8_matrix* l1, const idol_q8_matrix* l2,

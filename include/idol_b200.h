@@ -199,6 +199,29 @@ int idol_b200_gs_block_forward(const idol_gs_block* block, void* x, int x_dtype,
                                const float* cond, int64_t cond_rows, void* workspace, int64_t workspace_bytes,
                                void* stream);
 
+/* The Gaussian decoder (Decoders::gaussian_features and to_gaussians, src/decoders.cpp:284-316, 393-433) over
+ * resident weights, for one image: x = in_proj(points) + pos_embed(points) (in_w dense fp32 [D, 3], in_b [D] or NULL;
+ * pos_embed with the export's n_freqs fp32 frequencies, 6 n_freqs <= D) -> input_layer (D x D) -> the blocks ->
+ * LN (eps 1e-5) -> out_proj (per_anchor * 15 x D) = features. rep: 9 host floats perturbe, kernel, scaling_bias,
+ * opacity_bias, lr_xyz, lr_dc, lr_opacity, lr_scaling, lr_rotation (src/weights.hpp:25-28); perturbation fp32
+ * [per_anchor * 3] on the device. The handle keeps pointers only. */
+typedef struct idol_gs_decoder idol_gs_decoder;
+int idol_b200_gs_decoder_create(const idol_gs_block* const* blocks, int nblocks, const float* in_w, const float* in_b,
+                                const idol_q8_matrix* input_layer, const idol_q8_matrix* out_proj, const float* freqs,
+                                int n_freqs, int per_anchor, const float* perturbation, float base_offset_scale,
+                                const float* rep, idol_gs_decoder** decoder);
+int idol_b200_gs_decoder_free(idol_gs_decoder* decoder);
+int64_t idol_b200_gs_decoder_workspace_bytes(const idol_gs_decoder* decoder, int64_t rows, int64_t cond_rows);
+/* points fp32 [rows, 3] (anchors in [0, 1]^3), cond fp32 [cond_rows, cond_dim] -> features fp32
+ * [rows, 15 per_anchor]. */
+int idol_b200_gs_decoder_features(const idol_gs_decoder* decoder, const float* points, int64_t rows, const float* cond,
+                                  int64_t cond_rows, float* features, void* workspace, int64_t workspace_bytes,
+                                  void* stream);
+/* Activated Gaussians: xyz, f_dc, scale fp32 [rows * per_anchor, 3], rotation [.., 4], opacity [..]. */
+int idol_b200_gs_to_gaussians(const idol_gs_decoder* decoder, const float* anchors, int64_t rows,
+                              const float* features, float* xyz, float* f_dc, float* scale, float* rotation,
+                              float* opacity, void* stream);
+
 /* The Gaussian decoder MLP of config 4 (scope row A15): x [points, in] bf16 -> l0 (SiLU) -> l1 (SiLU) -> l2 (14
  * outputs) -> heads: pos identity, scale exp, rotation r = f * 0.1 + (1, 0, 0, 0) divided by max(|r|, 1e-12)
  * (src/decoders.cpp:422-428 with the default lr_rotation), colour and opacity sigmoid (:429). out: fp32 [points, 14]; raw_out: fp32 [points, 14] pre-activation values, or NULL. */

@@ -53,6 +53,9 @@ def lib():
         L.orc_attention.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
         L.orc_gaussian_heads.argtypes = [_f32p, ctypes.c_int64, _f32p]
+        L.orc_pos_embed.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.orc_to_gaussians.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p, ctypes.c_float, _f32p,
+                                       _f32p, _f32p, _f32p, _f32p, _f32p]
         L.orc_f32_to_f16.argtypes = [ctypes.c_float]
         L.orc_f32_to_f16.restype = ctypes.c_uint16
         L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
@@ -98,6 +101,13 @@ def ref():
         R.ref_gelu_scalar.restype = ctypes.c_float
         R.ref_attention.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        R.ref_decoders_open.argtypes = [ctypes.c_char_p]
+        R.ref_decoders_open.restype = ctypes.c_void_p
+        R.ref_decoders_free.argtypes = [ctypes.c_void_p]
+        R.ref_gaussian_features.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, ctypes.c_int, _f32p,
+                                            ctypes.c_int]
+        R.ref_to_gaussians.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                       _f32p]
         _ref = R
     return _ref
 
@@ -285,6 +295,48 @@ def gs_block_forward(x, cond, layers, heads, eps=1e-6, images=1, bf16_stream=Fal
     return rnd(gemm_q8(f, *layers["ff2"], residual=x))
 
 
+# The reference's Representation defaults (src/weights.hpp:25-28), in orc_to_gaussians' order.
+REPRESENTATION = dict(perturbe=1.5, kernel=0.0009, scaling_bias=0.004, opacity_bias=0.1, lr_xyz=1.0, lr_dc=1.0,
+                      lr_opacity=1.0, lr_scaling=1.0, lr_rotation=0.1)
+
+
+def pos_embed(points, freqs, dim):
+    points, freqs = c32(points), c32(freqs)
+    out = np.empty((points.shape[0], dim), np.float32)
+    lib().orc_pos_embed(_ptr(points), points.shape[0], _ptr(freqs), freqs.size, dim, _ptr(out))
+    return out
+
+
+def to_gaussians(anchors, features, per_anchor, perturbation, base_offset_scale, rep=None):
+    """Decoders::to_gaussians (src/decoders.cpp:393-433) -> dict of xyz, f_dc, scale, rotation, opacity."""
+    rep = dict(REPRESENTATION, **(rep or {}))
+    r = c32([rep[k] for k in REPRESENTATION])
+    anchors, features, perturbation = c32(anchors), c32(features), c32(perturbation)
+    n = anchors.shape[0] * per_anchor
+    out = {k: np.empty((n, w), np.float32) for k, w in (("xyz", 3), ("f_dc", 3), ("scale", 3), ("rotation", 4),
+                                                         ("opacity", 1))}
+    lib().orc_to_gaussians(_ptr(anchors), anchors.shape[0], _ptr(features), per_anchor, _ptr(perturbation),
+                           float(base_offset_scale), _ptr(r), *(_ptr(out[k]) for k in
+                                                                ("xyz", "f_dc", "scale", "rotation", "opacity")))
+    out["opacity"] = out["opacity"].reshape(-1)
+    return out
+
+
+def gaussian_features(points, cond, dec, heads, eps=1e-6):
+    """Decoders::Impl::gaussian_features (src/decoders.cpp:284-316) for one image: pos_embed + in_proj (dense fp32,
+    K = 3) as its residual -> input_layer -> the blocks -> LN (eps 1e-5) -> out_proj. dec: in_w [D, 3], in_b [D],
+    input (q8, bias, N, K), blocks (list of gs_block_forward layer dicts), out (q8, bias, N, K), freqs."""
+    points = c32(points)
+    D = dec["in_w"].shape[0]
+    h = pos_embed(points, dec["freqs"], D)
+    x = (points @ c32(dec["in_w"]).T + dec["in_b"] + h).astype(np.float32)
+    x = gemm_q8(x, *dec["input"])
+    for layers in dec["blocks"]:
+        x = gs_block_forward(x, cond, layers, heads, eps)
+    h = norm_rows(x, 1e-5)
+    return gemm_q8(h, *dec["out"])
+
+
 def gaussian_mlp(x, layers):
     """Synthetic Gaussian MLP: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the activated heads."""
     h = gemm_q8(x, *layers[0], act=ACT_SILU)
@@ -329,3 +381,35 @@ def ref_threads(n=None):
         n = os.cpu_count() or 1
     ref().ref_set_threads(int(n))
     return int(n)
+
+
+class RefDecoders:
+    """The reference's Decoders (include/idol/decoders.hpp) loaded from a native export directory."""
+
+    def __init__(self, path):
+        self.h = ref().ref_decoders_open(str(path).encode())
+        if not self.h:
+            raise ValueError(ref().ref_last_error().decode())
+
+    def gaussian_features(self, points, cond, outs, mode=0):
+        """mode 0: the float kernel production forces (tools/idol_generate.py:356); 1: the AVX-VNNI kernel."""
+        points, cond = c32(points), c32(cond)
+        out = np.empty((points.shape[0], outs), np.float32)
+        ref().ref_gaussian_features(self.h, _ptr(points), points.shape[0], _ptr(cond), cond.shape[0], _ptr(out),
+                                    mode)
+        return out
+
+    def to_gaussians(self, anchors, features, per_anchor):
+        anchors, features = c32(anchors), c32(features)
+        n = anchors.shape[0] * per_anchor
+        out = {k: np.empty((n, w), np.float32) for k, w in (("xyz", 3), ("f_dc", 3), ("scale", 3), ("rotation", 4),
+                                                             ("opacity", 1))}
+        ref().ref_to_gaussians(self.h, _ptr(anchors), anchors.shape[0], _ptr(features),
+                               *(_ptr(out[k]) for k in ("xyz", "f_dc", "scale", "rotation", "opacity")))
+        out["opacity"] = out["opacity"].reshape(-1)
+        return out
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().ref_decoders_free(self.h)
+            self.h = None

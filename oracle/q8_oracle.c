@@ -399,6 +399,78 @@ void orc_attention(const float* q, int lq, int ldq, const float* k, const float*
  *   with the default lr_rotation 0.1 (src/weights.hpp:27), divided by max(|r|, 1e-12); color 10..12 sigmoid;
  *   opacity 13 sigmoid (src/decoders.cpp:429).
  * ---------------------------------------------------------------------------------------------------------------- */
+/* ------------------------------------------------------------------------------------------------------------------
+ * The Gaussian decoder's position embedding (src/decoders.cpp:215-230 pos_embed): per row, for each of the 3
+ * coordinates v and each of the fd frequencies f, sin((v f) pi) then, fd columns later, cos((v f) pi); columns from
+ * 6 fd on are zero. out: [rows, dim].
+ * ---------------------------------------------------------------------------------------------------------------- */
+void orc_pos_embed(const float* x, int64_t rows, const float* freqs, int fd, int dim, float* out) {
+    const float pi = 3.14159265358979323846f;
+    for (int64_t r = 0; r < rows; ++r) {
+        float* o = out + r * dim;
+        for (int c = 0; c < 3; ++c) {
+            const float v = x[r * 3 + c];
+            for (int j = 0; j < fd; ++j) {
+                const float ang = (v * freqs[j]) * pi;
+                o[c * 2 * fd + j] = sinf(ang);
+                o[c * 2 * fd + fd + j] = cosf(ang);
+            }
+        }
+        for (int j = 6 * fd; j < dim; ++j) o[j] = 0.0f;
+    }
+}
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * Decoders::to_gaussians (src/decoders.cpp:393-433): per anchor a (xyz anchors[a]) and Gaussian g of per_anchor G,
+ * from the anchor's 15 G features (xyz offsets at 0, colour at 3G, scale at 6G, rotation at 9G, opacity at 13G,
+ * offset scale at 14G):
+ *   offset_scale = softplus(f_os + base_offset_scale)
+ *   xyz = (tanh(f_xyz lr_xyz + perturbation[g]) * 0.5 perturbe offset_scale + anchor) - 0.5
+ *   f_dc = f_dc lr_dc; scale = sqrt(softplus(f_sc lr_scaling + scale_offset)^2 + kernel^2) with
+ *   scale_offset = sb + log(-expm1(-sb)) in double (inverse softplus of sb = scaling_bias)
+ *   rotation = (f_rot lr_rotation + (1, 0, 0, 0)) / max(|.|, 1e-12)
+ *   opacity = 1 / (1 + exp(-(f_op lr_opacity + log(ob / (1 - ob))))) with ob = opacity_bias
+ * softplus(x) = x above 20, else log1p(exp(x)) (src/decoders.cpp:90). rep = [perturbe, kernel, scaling_bias,
+ * opacity_bias, lr_xyz, lr_dc, lr_opacity, lr_scaling, lr_rotation] (src/weights.hpp:25-28). Outputs: xyz, f_dc,
+ * scale [anchors G, 3], rotation [anchors G, 4], opacity [anchors G].
+ * ---------------------------------------------------------------------------------------------------------------- */
+static float orc_softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+void orc_to_gaussians(const float* anchors, int64_t rows, const float* features, int G, const float* perturbation,
+                      float base_offset_scale, const float* rep, float* xyz, float* f_dc, float* scale,
+                      float* rotation, float* opacity) {
+    const float perturbe = rep[0], kernel = rep[1];
+    const double sb = rep[2], ob = rep[3];
+    const float lr_xyz = rep[4], lr_dc = rep[5], lr_opacity = rep[6], lr_scaling = rep[7], lr_rotation = rep[8];
+    const float scale_offset = (float)(sb + log(-expm1(-sb)));
+    const float opacity_offset = (float)log(ob / (1.0 - ob));
+    const int stride = G * 15, xyz0 = 0, dc0 = G * 3, sc0 = G * 6, rot0 = G * 9, op0 = G * 13, os0 = G * 14;
+    for (int64_t a = 0; a < rows; ++a) {
+        const float* f = features + a * stride;
+        for (int g = 0; g < G; ++g) {
+            const int64_t i = a * G + g;
+            const float offset_scale = orc_softplus(f[os0 + g] + base_offset_scale);
+            for (int c = 0; c < 3; ++c) {
+                const float o = tanhf(f[xyz0 + g * 3 + c] * lr_xyz + perturbation[g * 3 + c]) * 0.5f * perturbe *
+                                offset_scale;
+                xyz[i * 3 + c] = (o + anchors[a * 3 + c]) - 0.5f;
+                f_dc[i * 3 + c] = f[dc0 + g * 3 + c] * lr_dc;
+                const float s = orc_softplus(f[sc0 + g * 3 + c] * lr_scaling + scale_offset);
+                scale[i * 3 + c] = sqrtf(s * s + kernel * kernel);
+            }
+            float q[4], norm = 0.0f;
+            for (int c = 0; c < 4; ++c) {
+                q[c] = f[rot0 + g * 4 + c] * lr_rotation + (c == 0 ? 1.0f : 0.0f);
+                norm += q[c] * q[c];
+            }
+            norm = sqrtf(norm);
+            if (norm < 1e-12f) norm = 1e-12f;
+            for (int c = 0; c < 4; ++c) rotation[i * 4 + c] = q[c] / norm;
+            opacity[i] = 1.0f / (1.0f + expf(-(f[op0 + g] * lr_opacity + opacity_offset)));
+        }
+    }
+}
+
 void orc_gaussian_heads(const float* raw, int64_t points, float* out) {
     for (int64_t p = 0; p < points; ++p) {
         const float* f = raw + p * 14;

@@ -95,4 +95,37 @@ void ref_attention(const float* q, int lq, int ldq, const float* k, const float*
     idol::detail::attention(q, lq, ldq, k, v, lk, ldkv, heads, head_dim, out, dim);
 }
 
+// The reference's decoders, loaded from a native export directory (manifest.txt + weights.bin, src/weights.cpp:25-104),
+// through their public API (include/idol/decoders.hpp). Returns nullptr on error (ref_last_error says why).
+void* ref_decoders_open(const char* dir) {
+    try {
+        return new idol::Decoders(dir);
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return nullptr;
+    }
+}
+
+void ref_decoders_free(void* h) { delete static_cast<idol::Decoders*>(h); }
+
+// mode selects the quantized GEMM kernel as in ref_gemm: 0 the float kernel that production forces
+// (tools/idol_generate.py:356), 1 the AVX-VNNI integer kernel (the library's default on such CPUs).
+void ref_gaussian_features(void* h, const float* points, int rows, const float* cond, int cond_rows, float* out,
+                           int mode) {
+    idol::detail::set_quant_kernel(mode);
+    static_cast<idol::Decoders*>(h)->gaussian_features(points, rows, cond, cond_rows, out);
+}
+
+// Decoders::to_gaussians, copied out of the GaussianCloud: xyz, f_dc, scale [rows * per_anchor, 3], rotation [.., 4],
+// opacity [..].
+void ref_to_gaussians(void* h, const float* anchors, int rows, const float* features, float* xyz, float* f_dc,
+                      float* scale, float* rotation, float* opacity) {
+    const idol::GaussianCloud c = static_cast<idol::Decoders*>(h)->to_gaussians(anchors, rows, features);
+    std::memcpy(xyz, c.xyz.data(), c.xyz.size() * sizeof(float));
+    std::memcpy(f_dc, c.f_dc.data(), c.f_dc.size() * sizeof(float));
+    std::memcpy(scale, c.scale.data(), c.scale.size() * sizeof(float));
+    std::memcpy(rotation, c.rotation.data(), c.rotation.size() * sizeof(float));
+    std::memcpy(opacity, c.opacity.data(), c.opacity.size() * sizeof(float));
+}
+
 }  // extern "C"
