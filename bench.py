@@ -379,13 +379,16 @@ def run_ours(args, rank, world, local_rank):
     mlp_ms = measure_mlp(pkg, dev, stream, mlp_steps, world)
     gs_steps = max(3, min(args.steps, 20))
     gs_ms = measure_gs_block(pkg, dev, stream, gs_steps, world)
+    dec_steps = max(3, min(args.steps, 5))
+    dec_ms = measure_gs_decoder(pkg, dev, stream, dec_steps, world)
     status = max(status, pkg._capi.device_status(local_rank))
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms, dec_ms], device=dev,
+                         dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, status, block_ms, mlp_ms = float(t[0]), float(t[1]), int(t[2]), float(t[3]), float(t[4])
-        gs_ms = float(t[5])
+        gs_ms, dec_ms = float(t[5]), float(t[6])
     clk = clocks.stop(wall0, wall1) if rank == 0 else None
     if rank != 0:
         return
@@ -453,6 +456,12 @@ def run_ours(args, rank, world, local_rank):
                            "ms_per_step": round(gs_ms / gs_steps, 3), "steps": gs_steps,
                            "tflops": round(GS_FLOPS * gs_steps * world / (gs_ms / 1e3) / 1e12, 1),
                            "work": f"{GS_FLOPS / 1e9:.1f} GFLOP per step"},
+        "gaussian_decoder": {"metric": "Gaussian decodes/s (Decoders::gaussian_features + to_gaussians: 8192 "
+                                       "anchors -> 262,144 Gaussians, 16 blocks, 8192 latent tokens x 16, D 1024)",
+                             "value": round(dec_steps * world / (dec_ms / 1e3), 3), "unit": "decodes/s",
+                             "ms_per_step": round(dec_ms / dec_steps, 3), "steps": dec_steps,
+                             "gaussians_per_s": round(GS_ANCHORS * 32 * dec_steps * world / (dec_ms / 1e3), 0),
+                             "tflops": round(GS_FLOPS * GS_BLOCKS * dec_steps * world / (dec_ms / 1e3) / 1e12, 1)},
         "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
                                    "heads)", "value": round(MLP_POINTS * mlp_steps * world / (mlp_ms / 1e3), 0),
                          "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
@@ -518,7 +527,7 @@ def run_profile_shape(args):
 BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
 BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
-GS_ANCHORS, GS_LATENTS, GS_COND = 8192, 8192, 16
+GS_ANCHORS, GS_LATENTS, GS_COND, GS_BLOCKS = 8192, 8192, 16, 16
 GS_FLOPS = (2.0 * GS_ANCHORS * (3 + 1 + 1 + 1 + 2 * BLOCK_H // BLOCK_D) * BLOCK_D * BLOCK_D
             + 4.0 * GS_ANCHORS * GS_ANCHORS * BLOCK_D + 4.0 * GS_ANCHORS * GS_LATENTS * BLOCK_D
             + 2.0 * GS_LATENTS * GS_COND * 2 * BLOCK_D)
@@ -569,12 +578,10 @@ def measure_block(pkg, dev, stream, steps, world):
     return _graph_ms(torch, stream, lambda: blk.forward_(x, images=BLOCK_IMAGES), steps, world)
 
 
-def measure_gs_block(pkg, dev, stream, steps, world):
-    """The real Gaussian decoder's block (src/decoders.cpp:296-313) at its model size: 8192 anchors attending to
-    themselves and to 8192 latent tokens of 16 conditions, D 1024, 16 heads, fp32 residual stream in place."""
+def _random_gs_block(dev, g):
+    """A Gaussian-decoder block of the real model's shape with seeded random weights (Q8_0 on the device)."""
     import torch
     from idol_b200.block import GaussianBlock, Q8Weight
-    g = torch.Generator(device=dev).manual_seed(78)
     D, H = BLOCK_D, BLOCK_H
     w = {}
     for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "cq": (D, D), "co": (D, D), "ff1": (H, D),
@@ -583,13 +590,48 @@ def measure_gs_block(pkg, dev, stream, steps, world):
                                       torch.randn(n, device=dev, generator=g) * 0.01)
     vec = [1 + 0.1 * torch.randn(D, device=dev, generator=g) for _ in range(5)] + [
         0.1 * torch.randn(D, device=dev, generator=g)]
-    blk = GaussianBlock(w["qkv"], w["out"], w["cq"], w["co"], w["ff1"], w["ff2"], *vec,
-                        torch.randn((2 * D, GS_COND), device=dev, generator=g) * 0.25,
-                        torch.randn(2 * D, device=dev, generator=g) * 0.01, BLOCK_HEADS)
+    return GaussianBlock(w["qkv"], w["out"], w["cq"], w["co"], w["ff1"], w["ff2"], *vec,
+                         torch.randn((2 * D, GS_COND), device=dev, generator=g) * 0.25,
+                         torch.randn(2 * D, device=dev, generator=g) * 0.01, BLOCK_HEADS)
+
+
+def measure_gs_block(pkg, dev, stream, steps, world):
+    """The real Gaussian decoder's block (src/decoders.cpp:296-313) at its model size: 8192 anchors attending to
+    themselves and to 8192 latent tokens of 16 conditions, D 1024, 16 heads, fp32 residual stream in place."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(78)
+    blk = _random_gs_block(dev, g)
+    D = BLOCK_D
     x = torch.randn((GS_ANCHORS, D), device=dev, generator=g)
     cond = torch.randn((GS_LATENTS, GS_COND), device=dev, generator=g)
     blk.forward_(x, cond)  # sizes the workspace outside the graph
     return _graph_ms(torch, stream, lambda: blk.forward_(x, cond), steps, world)
+
+
+def measure_gs_decoder(pkg, dev, stream, steps, world):
+    """The whole Gaussian decoder (Decoders::gaussian_features + to_gaussians, src/decoders.cpp:284-316, 393-433) at
+    the real model's size: 8192 anchors (262,144 Gaussians), 16 blocks, 8192 latent tokens x 16, D 1024, 480 raw
+    features per anchor."""
+    import torch
+    from idol_b200.block import Q8Weight
+    from idol_b200.native import GaussianDecoder
+    g = torch.Generator(device=dev).manual_seed(79)
+    D, G = BLOCK_D, 32
+    blocks = [_random_gs_block(dev, g) for _ in range(GS_BLOCKS)]
+    dec = GaussianDecoder(blocks, torch.randn((D, 3), device=dev, generator=g) * 0.5,
+                          torch.randn(D, device=dev, generator=g) * 0.01,
+                          Q8Weight.from_float(torch.randn((D, D), device=dev, generator=g) * 0.03),
+                          Q8Weight.from_float(torch.randn((15 * G, D), device=dev, generator=g) * 0.03),
+                          2.0 ** torch.linspace(0, 10, D // 6), G, torch.randn(3 * G, device=dev, generator=g) * 0.1,
+                          -1.0)
+    pts = torch.rand((GS_ANCHORS, 3), device=dev, generator=g)
+    cond = torch.randn((GS_LATENTS, GS_COND), device=dev, generator=g)
+
+    def step():
+        dec.to_gaussians(pts, dec.features(pts, cond))
+
+    step()  # sizes the workspace outside the graph
+    return _graph_ms(torch, stream, step, steps, world)
 
 
 def measure_mlp(pkg, dev, stream, steps, world):
