@@ -61,6 +61,20 @@ SIGNATURES = {
     "idol_b200_gs_decoder_workspace_bytes": (_i64, [_vp, _i64, _i64]),
     "idol_b200_gs_decoder_features": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp]),
     "idol_b200_gs_to_gaussians": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "idol_b200_oct_block_create": (_i32, [_vp] * 8 + [_i32, _i32, ctypes.POINTER(_vp)]),
+    "idol_b200_oct_block_free": (_i32, [_vp]),
+    "idol_b200_oct_decoder_create": (_i32, [_vp, _i32] + [_vp] * 8 + [_i32, _vp, _i32, ctypes.c_float,
+                                                                         ctypes.POINTER(_vp)]),
+    "idol_b200_oct_decoder_free": (_i32, [_vp]),
+    "idol_b200_oct_decoder_workspace_bytes": (_i64, [_vp, _i64, _i64]),
+    "idol_b200_oct_logits": (_i32, [_vp, _vp, _i64, ctypes.c_float, _vp, _i64, _vp, _vp, _i64, _vp]),
+    "idol_b200_oct_sample_anchors": (_i32, [_vp, _vp, _i64, _i32, _i32, ctypes.c_uint64, _vp, _vp, _i64, _vp]),
+    "idol_b200_oct_sampler_create": (_i32, [_i32, _i32, ctypes.c_uint64, ctypes.POINTER(_vp)]),
+    "idol_b200_oct_sampler_free": (_i32, [_vp]),
+    "idol_b200_oct_sampler_cells": (_i32, [_vp, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_float)]),
+    "idol_b200_oct_sampler_centres": (_i32, [_vp, _vp]),
+    "idol_b200_oct_sampler_step": (_i32, [_vp, _vp]),
+    "idol_b200_oct_sampler_points": (_i32, [_vp, _vp]),
     "idol_b200_gaussian_mlp_create": (_i32, [_vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "idol_b200_gaussian_mlp_free": (_i32, [_vp]),
     "idol_b200_gaussian_mlp_workspace_bytes": (_i64, [_vp, _i64]),

@@ -172,6 +172,23 @@ __global__ void kv_project_kernel(const float* __restrict__ cond, long long rows
 
 }  // namespace
 
+cudaError_t launch_decoder_input(const float* points, long long rows, int dim, const float* w, const float* b,
+                                 const float* freqs, int fd, __nv_bfloat16* out, cudaStream_t s) {
+    const long long n = rows * dim;
+    if (n == 0) return cudaSuccess;
+    gs_input_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(points, rows, dim, w, b, freqs, fd, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_project(const float* cond, long long rows, int cdim, const float* w, const float* b, int cols,
+                              __nv_bfloat16* kv, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    if (cdim < 1 || cdim > kKvMaxCond || rows > 65535LL * 16) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((cols + 255) / 256), (unsigned)((rows + 15) / 16));
+    kv_project_kernel<<<grid, 256, 0, s>>>(cond, rows, cdim, w, b, cols, kv);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
                                   cudaStream_t s) {
     if (points == 0) return cudaSuccess;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -119,6 +120,12 @@ cudaError_t take_device_error_attention(unsigned int* flags);
 
 cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
                                   cudaStream_t s);
+// The decoders' input (in_proj of 3 coordinates + bias + pos_embed, bf16 out) and the dense fp32 key/value projection
+// of the condition rows (block.cu).
+cudaError_t launch_decoder_input(const float* points, long long rows, int dim, const float* w, const float* b,
+                                 const float* freqs, int fd, __nv_bfloat16* out, cudaStream_t s);
+cudaError_t launch_kv_project(const float* cond, long long rows, int cdim, const float* w, const float* b, int cols,
+                              __nv_bfloat16* kv, cudaStream_t s);
 
 }  // namespace idol
 

@@ -222,6 +222,50 @@ int idol_b200_gs_to_gaussians(const idol_gs_decoder* decoder, const float* ancho
                               const float* features, float* xyz, float* f_dc, float* scale, float* rotation,
                               float* opacity, void* stream);
 
+/* The octree decoder (Decoders::octree_logits and sample_anchors, src/decoders.cpp:242-282, 335-391) over resident
+ * weights. A block is the cross-attention half and the MLP half of src/decoders.cpp:268-279, each added to the
+ * residual stream through its adaLN gate: to_q / to_out D x D, ff1 H x D, ff2 D x H, the dense fp32 to_kv [2D,
+ * cond_dim] (+ bias [2D] or NULL), q/k rms gammas [D]. The decoder: in_proj dense fp32 [D, 3] (+ bias), input_layer
+ * D x D, the level embedder l1 D x 256 and l2 D x D, the adaLN modulation ada 6D x D, out_proj 8 x D, pos_embed
+ * frequencies [n_freqs] (6 n_freqs <= D) and the 128 level frequencies, all on the device; eps is the blocks' LN
+ * epsilon (1e-6 in the reference). Handles keep pointers only. */
+typedef struct idol_oct_block idol_oct_block;
+typedef struct idol_oct_decoder idol_oct_decoder;
+int idol_b200_oct_block_create(const idol_q8_matrix* cross_q, const idol_q8_matrix* cross_out,
+                               const idol_q8_matrix* ff1, const idol_q8_matrix* ff2, const float* cross_q_gamma,
+                               const float* cross_k_gamma, const float* kv_weight, const float* kv_bias, int cond_dim,
+                               int heads, idol_oct_block** block);
+int idol_b200_oct_block_free(idol_oct_block* block);
+int idol_b200_oct_decoder_create(const idol_oct_block* const* blocks, int nblocks, const float* in_w, const float* in_b,
+                                 const idol_q8_matrix* input_layer, const idol_q8_matrix* l1,
+                                 const idol_q8_matrix* l2, const idol_q8_matrix* ada, const idol_q8_matrix* out_proj,
+                                 const float* freqs, int n_freqs, const float* level_freqs, int heads, float eps,
+                                 idol_oct_decoder** decoder);
+int idol_b200_oct_decoder_free(idol_oct_decoder* decoder);
+/* Device workspace for a logits call over `rows` cells (for sample_anchors: rows = num_points). */
+int64_t idol_b200_oct_decoder_workspace_bytes(const idol_oct_decoder* decoder, int64_t rows, int64_t cond_rows);
+/* x: cell centres fp32 [rows, 3] on the device; resolution: the cells' octree resolution 2^level; cond fp32
+ * [cond_rows, cond_dim]; logits fp32 [rows, 8] (how a cell's points split among its children). */
+int idol_b200_oct_logits(const idol_oct_decoder* decoder, const float* x, int64_t rows, float resolution,
+                         const float* cond, int64_t cond_rows, float* logits, void* workspace, int64_t workspace_bytes,
+                         void* stream);
+/* Decoders::sample_anchors: descends from the root to `level` (1..20), the logits of each level's occupied cells
+ * on the GPU, the resampling on the host with the reference's generator and arithmetic (mt19937_64 seeded with
+ * `seed`); points: host fp32 [num_points, 3]. Synchronises `stream` once per level. */
+int idol_b200_oct_sample_anchors(const idol_oct_decoder* decoder, const float* cond, int64_t cond_rows,
+                                 int num_points, int level, uint64_t seed, float* points, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
+/* The host half of sample_anchors on its own, for callers that compute the logits themselves: create, then per level
+ * cells (the number of occupied cells and the resolution to evaluate them at; 0 cells once every level is done),
+ * centres (host fp32 [cells, 3]) and step (host fp32 logits [cells, 8]); finally points (host fp32 [num_points, 3]). */
+typedef struct idol_oct_sampler idol_oct_sampler;
+int idol_b200_oct_sampler_create(int num_points, int level, uint64_t seed, idol_oct_sampler** sampler);
+int idol_b200_oct_sampler_free(idol_oct_sampler* sampler);
+int idol_b200_oct_sampler_cells(const idol_oct_sampler* sampler, int64_t* cells, float* resolution);
+int idol_b200_oct_sampler_centres(const idol_oct_sampler* sampler, float* centres);
+int idol_b200_oct_sampler_step(idol_oct_sampler* sampler, const float* logits);
+int idol_b200_oct_sampler_points(idol_oct_sampler* sampler, float* points);
+
 /* The Gaussian decoder MLP of config 4 (scope row A15): x [points, in] bf16 -> l0 (SiLU) -> l1 (SiLU) -> l2 (14
  * outputs) -> heads: pos identity, scale exp, rotation r = f * 0.1 + (1, 0, 0, 0) divided by max(|r|, 1e-12)
  * (src/decoders.cpp:422-428 with the default lr_rotation), colour and opacity sigmoid (:429). out: fp32 [points, 14]; raw_out: fp32 [points, 14] pre-activation values, or NULL. */

@@ -54,6 +54,7 @@ def lib():
                                     ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
         L.orc_gaussian_heads.argtypes = [_f32p, ctypes.c_int64, _f32p]
         L.orc_pos_embed.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.orc_level_embed.argtypes = [ctypes.c_float, _f32p, _f32p]
         L.orc_to_gaussians.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.c_int, _f32p, ctypes.c_float, _f32p,
                                        _f32p, _f32p, _f32p, _f32p, _f32p]
         L.orc_f32_to_f16.argtypes = [ctypes.c_float]
@@ -108,6 +109,11 @@ def ref():
                                             ctypes.c_int]
         R.ref_to_gaussians.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p, _f32p,
                                        _f32p]
+        R.ref_octree_logits.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_float, _f32p, ctypes.c_int,
+                                        _f32p, ctypes.c_int]
+        R.ref_sample_anchors.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_uint64, _f32p, ctypes.c_int]
+        R.ref_sample_anchors.restype = ctypes.c_int
         _ref = R
     return _ref
 
@@ -337,6 +343,43 @@ def gaussian_features(points, cond, dec, heads, eps=1e-6):
     return gemm_q8(h, *dec["out"])
 
 
+def level_embed(resolution, freqs):
+    out = np.empty(256, np.float32)
+    lib().orc_level_embed(float(resolution), _ptr(c32(freqs)), _ptr(out))
+    return out
+
+
+def octree_logits(x, resolution, cond, dec, heads, eps=1e-6):
+    """Decoders::Impl::octree_logits (src/decoders.cpp:242-282): pos_embed + in_proj (dense fp32, K = 3) ->
+    input_layer; the level embedding -> l1 -> SiLU -> l2 -> SiLU -> adaLN modulation (shift, scale, gate for the
+    attention and the MLP half); per block: LN * (1 + scale_a) + shift_a -> cross-attention -> to_out, added with
+    gate_a; LN * (1 + scale_m) + shift_m -> ff1 -> gelu_tanh -> ff2, added with gate_m; LN (eps 1e-5) -> out_proj (8
+    logits). dec: in_w [D, 3], in_b, input, l1, l2, ada, out (q8, bias, N, K), freqs, level_freqs, blocks (dicts of
+    cq, co, ff1, ff2, kv_w, kv_b, cq_gamma, ck_gamma)."""
+    x, cond = c32(x), c32(cond)
+    D = dec["in_w"].shape[0]
+    hd = D // heads
+    h = pos_embed(x, dec["freqs"], D)
+    X = (x @ c32(dec["in_w"]).T + dec["in_b"] + h).astype(np.float32)
+    X = gemm_q8(X, *dec["input"])
+    emb = level_embed(resolution, dec["level_freqs"]).reshape(1, 256)
+    l1 = activate(gemm_q8(emb, *dec["l1"]), ACT_SILU)
+    l2 = activate(gemm_q8(l1, *dec["l2"]), ACT_SILU)
+    mod = gemm_q8(l2, *dec["ada"]).reshape(6, D)
+    shift_a, scale_a, gate_a, shift_m, scale_m, gate_m = mod
+    for L in dec["blocks"]:
+        h = norm_rows(X, eps, shift=shift_a, scale=scale_a)
+        q = rms_heads(gemm_q8(h, *L["cq"]), heads, hd, L["cq_gamma"], col0=0)
+        kv = (cond.astype(np.float64) @ c32(L["kv_w"]).astype(np.float64).T + L["kv_b"]).astype(np.float32)
+        kv = rms_heads(kv, heads, hd, L["ck_gamma"], col0=0)
+        a = attention(q, np.ascontiguousarray(kv[:, :D]), np.ascontiguousarray(kv[:, D:]), heads, hd)
+        X = (X + gemm_q8(a, *L["co"]) * gate_a).astype(np.float32)
+        h = norm_rows(X, eps, shift=shift_m, scale=scale_m)
+        f = gemm_q8(h, *L["ff1"], act=ACT_GELU_TANH)
+        X = (X + gemm_q8(f, *L["ff2"]) * gate_m).astype(np.float32)
+    return gemm_q8(norm_rows(X, 1e-5), *dec["out"])
+
+
 def gaussian_mlp(x, layers):
     """Synthetic Gaussian MLP: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14, then the activated heads."""
     h = gemm_q8(x, *layers[0], act=ACT_SILU)
@@ -397,6 +440,21 @@ class RefDecoders:
         out = np.empty((points.shape[0], outs), np.float32)
         ref().ref_gaussian_features(self.h, _ptr(points), points.shape[0], _ptr(cond), cond.shape[0], _ptr(out),
                                     mode)
+        return out
+
+    def octree_logits(self, x, resolution, cond, mode=0):
+        x, cond = c32(x), c32(cond)
+        out = np.empty((x.shape[0], 8), np.float32)
+        ref().ref_octree_logits(self.h, _ptr(x), x.shape[0], float(resolution), _ptr(cond), cond.shape[0], _ptr(out),
+                                mode)
+        return out
+
+    def sample_anchors(self, cond, num_points, level, seed, mode=0):
+        cond = c32(cond)
+        out = np.empty((num_points, 3), np.float32)
+        n = ref().ref_sample_anchors(self.h, _ptr(cond), cond.shape[0], num_points, level, seed, _ptr(out), mode)
+        if n < 0:
+            raise ValueError(ref().ref_last_error().decode())
         return out
 
     def to_gaussians(self, anchors, features, per_anchor):

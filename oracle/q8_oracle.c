@@ -421,6 +421,19 @@ void orc_pos_embed(const float* x, int64_t rows, const float* freqs, int fd, int
 }
 
 /* ------------------------------------------------------------------------------------------------------------------
+ * The octree decoder's level embedding (src/decoders.cpp:254-259): for the 128 level frequencies f,
+ * cos(((resolution f) 2) pi) then sin(((resolution f) 2) pi). out: 256 floats.
+ * ---------------------------------------------------------------------------------------------------------------- */
+void orc_level_embed(float resolution, const float* freqs, float* out) {
+    const float pi = 3.14159265358979323846f;
+    for (int i = 0; i < 128; ++i) {
+        const float ang = ((resolution * freqs[i]) * 2.0f) * pi;
+        out[i] = cosf(ang);
+        out[128 + i] = sinf(ang);
+    }
+}
+
+/* ------------------------------------------------------------------------------------------------------------------
  * Decoders::to_gaussians (src/decoders.cpp:393-433): per anchor a (xyz anchors[a]) and Gaussian g of per_anchor G,
  * from the anchor's 15 G features (xyz offsets at 0, colour at 3G, scale at 6G, rotation at 9G, opacity at 13G,
  * offset scale at 14G):

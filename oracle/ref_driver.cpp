@@ -116,6 +116,27 @@ void ref_gaussian_features(void* h, const float* points, int rows, const float* 
     static_cast<idol::Decoders*>(h)->gaussian_features(points, rows, cond, cond_rows, out);
 }
 
+void ref_octree_logits(void* h, const float* x, int rows, float resolution, const float* cond, int cond_rows,
+                       float* out, int mode) {
+    idol::detail::set_quant_kernel(mode);
+    static_cast<idol::Decoders*>(h)->octree_logits(x, rows, resolution, cond, cond_rows, out);
+}
+
+// Decoders::sample_anchors into points [num_points, 3]; returns num_points, or -1 (ref_last_error says why).
+int ref_sample_anchors(void* h, const float* cond, int cond_rows, int num_points, int level, std::uint64_t seed,
+                       float* points, int mode) {
+    try {
+        idol::detail::set_quant_kernel(mode);
+        const std::vector<float> p =
+            static_cast<idol::Decoders*>(h)->sample_anchors(cond, cond_rows, num_points, level, seed);
+        std::memcpy(points, p.data(), p.size() * sizeof(float));
+        return (int)(p.size() / 3);
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
+}
+
 // Decoders::to_gaussians, copied out of the GaussianCloud: xyz, f_dc, scale [rows * per_anchor, 3], rotation [.., 4],
 // opacity [..].
 void ref_to_gaussians(void* h, const float* anchors, int rows, const float* features, float* xyz, float* f_dc,

@@ -14,13 +14,15 @@ from pathlib import Path
 import numpy as np
 
 
-def write_decoders_export(path, oracle, D=256, heads=4, gs_blocks=2, cond=16, per_anchor=32, seed=0):
+def write_decoders_export(path, oracle, D=256, heads=4, gs_blocks=2, cond=16, per_anchor=32, seed=0, oct_blocks=0,
+                          with_octree=False):
     """Returns the Gaussian decoder as a dict: in_w [D, 3], in_b, input/out (q8, bias, N, K), freqs, perturbation,
-    base_offset_scale, blocks (list of layer dicts for oracle.gs_block_forward)."""
+    base_offset_scale, blocks (list of layer dicts for oracle.gs_block_forward). With with_octree, returns
+    (gaussian dict, octree dict) - the octree dict as oracle.octree_logits takes it."""
     path = Path(path)
     path.mkdir(parents=True, exist_ok=True)
     rng = np.random.default_rng(seed)
-    lines = [f"decoders {D} {heads} 0 {gs_blocks} {cond} {per_anchor}",
+    lines = [f"decoders {D} {heads} {oct_blocks} {gs_blocks} {cond} {per_anchor}",
              "rep 1.5 0.0009 0.004 0.1 1 1 1 1 0.1"]
     blob = bytearray()
 
@@ -56,15 +58,28 @@ def write_decoders_export(path, oracle, D=256, heads=4, gs_blocks=2, cond=16, pe
 
     fd = D // 3 // 2
     freqs = (2.0 ** np.linspace(0, 10, fd)).astype(np.float32)
-    # The octree decoder's tensors: read by the constructor, unused by the Gaussian decoder.
-    dense("oct.in_proj", D, 3, 0.5)
-    quant("oct.input_layer", D, D)
-    dense("oct.l_embedder.mlp.0", D, 256, 0.02)
-    quant("oct.l_embedder.mlp.2", D, D)
-    quant("oct.adaLN_modulation.1", 6 * D, D)
-    dense("oct.out_proj", 8, D, 0.02)
+    # The octree decoder (src/decoders.cpp:163-175, 200-202).
+    octd = {"freqs": freqs}
+    octd["in_w"], octd["in_b"] = dense("oct.in_proj", D, 3, 0.5)
+    octd["input"] = quant("oct.input_layer", D, D, 0.05)
+    octd["l1"] = quant("oct.l_embedder.mlp.0", D, 256, 0.1)
+    octd["l2"] = quant("oct.l_embedder.mlp.2", D, D, 0.05)
+    octd["ada"] = quant("oct.adaLN_modulation.1", 6 * D, D, 0.05)
+    octd["out"] = quant("oct.out_proj", 8, D, 0.1)
     tensor("oct.pos_embedder.freqs", freqs)
-    tensor("oct.l_embedder.freqs", np.exp(-np.log(1024.0) * np.arange(128) / 128).astype(np.float32))
+    octd["level_freqs"] = np.exp(-np.log(1024.0) * np.arange(128) / 128).astype(np.float32)
+    tensor("oct.l_embedder.freqs", octd["level_freqs"])
+    octd["blocks"] = []
+    for i in range(oct_blocks):
+        p = f"oct.blocks.{i}."
+        L = {"cq": quant(p + "cross_attn.to_q", D, D)}
+        L["kv_w"], L["kv_b"] = dense(p + "cross_attn.to_kv", 2 * D, cond, 0.25)
+        L["co"] = quant(p + "cross_attn.to_out", D, D)
+        L["cq_gamma"] = vec(p + "cross_attn.q_rms_norm.gamma", D)
+        L["ck_gamma"] = vec(p + "cross_attn.k_rms_norm.gamma", D)
+        L["ff1"] = quant(p + "mlp.mlp.0", 4 * D, D)
+        L["ff2"] = quant(p + "mlp.mlp.2", D, 4 * D)
+        octd["blocks"].append(L)
 
     dec = {"freqs": freqs}
     dec["in_w"], dec["in_b"] = dense("gs.in_proj", D, 3, 0.5)
@@ -90,4 +105,4 @@ def write_decoders_export(path, oracle, D=256, heads=4, gs_blocks=2, cond=16, pe
         dec["blocks"].append(L)
     (path / "manifest.txt").write_text("\n".join(lines) + "\n")
     (path / "weights.bin").write_bytes(bytes(blob))
-    return dec
+    return (dec, octd) if with_octree else dec
