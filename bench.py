@@ -381,14 +381,16 @@ def run_ours(args, rank, world, local_rank):
     gs_ms = measure_gs_block(pkg, dev, stream, gs_steps, world)
     dec_steps = max(3, min(args.steps, 5))
     dec_ms = measure_gs_decoder(pkg, dev, stream, dec_steps, world)
+    full_steps = 3
+    full_ms = measure_decode(pkg, dev, stream, full_steps, world)
     status = max(status, pkg._capi.device_status(local_rank))
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms, dec_ms], device=dev,
+        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms, dec_ms, full_ms], device=dev,
                          dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, status, block_ms, mlp_ms = float(t[0]), float(t[1]), int(t[2]), float(t[3]), float(t[4])
-        gs_ms, dec_ms = float(t[5]), float(t[6])
+        gs_ms, dec_ms, full_ms = float(t[5]), float(t[6]), float(t[7])
     clk = clocks.stop(wall0, wall1) if rank == 0 else None
     if rank != 0:
         return
@@ -462,6 +464,13 @@ def run_ours(args, rank, world, local_rank):
                              "ms_per_step": round(dec_ms / dec_steps, 3), "steps": dec_steps,
                              "gaussians_per_s": round(GS_ANCHORS * 32 * dec_steps * world / (dec_ms / 1e3), 0),
                              "tflops": round(GS_FLOPS * GS_BLOCKS * dec_steps * world / (dec_ms / 1e3) / 1e12, 1)},
+        "decode": {"metric": "Decoders::decode calls/s (latent 8192 x 16 -> sample_anchors to level 7 through the "
+                             "octree decoder, 4 blocks -> Gaussian decoder, 16 blocks -> 262,144 activated Gaussians; "
+                             "D 1024)", "value": round(full_steps * world / (full_ms / 1e3), 3), "unit": "decodes/s",
+                   "ms_per_step": round(full_ms / full_steps, 2), "steps": full_steps,
+                   "reference_published": "36.99 s on 8 threads and 0.34 s with the upstream GPU modules on an RTX "
+                                          "4090, both octree + Gaussian decoders at 262,144 Gaussians "
+                                          "(docs/data/decoder-cpu-vs-gpu.json); context only, other hardware"},
         "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
                                    "heads)", "value": round(MLP_POINTS * mlp_steps * world / (mlp_ms / 1e3), 0),
                          "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
@@ -527,7 +536,7 @@ def run_profile_shape(args):
 BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
 BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
-GS_ANCHORS, GS_LATENTS, GS_COND, GS_BLOCKS = 8192, 8192, 16, 16
+GS_ANCHORS, GS_LATENTS, GS_COND, GS_BLOCKS, OCT_BLOCKS, DECODE_LEVEL = 8192, 8192, 16, 16, 4, 7
 GS_FLOPS = (2.0 * GS_ANCHORS * (3 + 1 + 1 + 1 + 2 * BLOCK_H // BLOCK_D) * BLOCK_D * BLOCK_D
             + 4.0 * GS_ANCHORS * GS_ANCHORS * BLOCK_D + 4.0 * GS_ANCHORS * GS_LATENTS * BLOCK_D
             + 2.0 * GS_LATENTS * GS_COND * 2 * BLOCK_D)
@@ -608,22 +617,76 @@ def measure_gs_block(pkg, dev, stream, steps, world):
     return _graph_ms(torch, stream, lambda: blk.forward_(x, cond), steps, world)
 
 
+def _random_gaussian_decoder(dev, g):
+    import torch
+    from idol_b200.block import Q8Weight
+    from idol_b200.native import GaussianDecoder
+    D, G = BLOCK_D, 32
+    blocks = [_random_gs_block(dev, g) for _ in range(GS_BLOCKS)]
+    return GaussianDecoder(blocks, torch.randn((D, 3), device=dev, generator=g) * 0.5,
+                           torch.randn(D, device=dev, generator=g) * 0.01,
+                           Q8Weight.from_float(torch.randn((D, D), device=dev, generator=g) * 0.03),
+                           Q8Weight.from_float(torch.randn((15 * G, D), device=dev, generator=g) * 0.03),
+                           2.0 ** torch.linspace(0, 10, D // 6), G, torch.randn(3 * G, device=dev, generator=g) * 0.1,
+                           -1.0)
+
+
+def _random_octree_decoder(dev, g):
+    """The octree decoder of the real model's shape (4 blocks, D 1024) with seeded random weights."""
+    import torch
+    from idol_b200.block import Q8Weight
+    from idol_b200.native import OctreeDecoder
+    D, H = BLOCK_D, BLOCK_H
+
+    def q8(n, k, sd=0.02):
+        return Q8Weight.from_float(torch.randn((n, k), device=dev, generator=g) * sd,
+                                   torch.randn(n, device=dev, generator=g) * 0.01)
+
+    blocks = [{"cq": q8(D, D), "co": q8(D, D), "ff1": q8(H, D), "ff2": q8(D, H),
+               "kv_w": torch.randn((2 * D, GS_COND), device=dev, generator=g) * 0.25,
+               "kv_b": torch.randn(2 * D, device=dev, generator=g) * 0.01,
+               "cq_gamma": 1 + 0.1 * torch.randn(D, device=dev, generator=g),
+               "ck_gamma": 1 + 0.1 * torch.randn(D, device=dev, generator=g)} for _ in range(OCT_BLOCKS)]
+    return OctreeDecoder(blocks, torch.randn((D, 3), device=dev, generator=g) * 0.5,
+                         torch.randn(D, device=dev, generator=g) * 0.01, q8(D, D, 0.03), q8(D, 256, 0.1),
+                         q8(D, D, 0.03), q8(6 * D, D, 0.03), q8(8, D, 0.1), 2.0 ** torch.linspace(0, 10, D // 6),
+                         torch.exp(-torch.log(torch.tensor(1024.0)) * torch.arange(128) / 128), BLOCK_HEADS)
+
+
+def measure_decode(pkg, dev, stream, steps, world):
+    """Decoders::decode at the real model's size: sample_anchors through the octree decoder (4 blocks) down to level
+    DECODE_LEVEL for 8192 anchors, the Gaussian decoder (16 blocks) and to_gaussians: 262,144 Gaussians from 8192
+    latent tokens x 16. The octree levels synchronise the stream (the host resamples between them), so the decode is
+    timed by CUDA events around whole calls rather than replayed from a graph."""
+    import torch
+    import torch.distributed as dist
+    from idol_b200.native import decode
+    g = torch.Generator(device=dev).manual_seed(80)
+    octree, gaussian = _random_octree_decoder(dev, g), _random_gaussian_decoder(dev, g)
+    cond = torch.randn((GS_LATENTS, GS_COND), device=dev, generator=g)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            decode(octree, gaussian, cond, GS_ANCHORS * 32, DECODE_LEVEL, 7)
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(steps):
+            decode(octree, gaussian, cond, GS_ANCHORS * 32, DECODE_LEVEL, 7 + i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
 def measure_gs_decoder(pkg, dev, stream, steps, world):
     """The whole Gaussian decoder (Decoders::gaussian_features + to_gaussians, src/decoders.cpp:284-316, 393-433) at
     the real model's size: 8192 anchors (262,144 Gaussians), 16 blocks, 8192 latent tokens x 16, D 1024, 480 raw
     features per anchor."""
     import torch
-    from idol_b200.block import Q8Weight
-    from idol_b200.native import GaussianDecoder
     g = torch.Generator(device=dev).manual_seed(79)
-    D, G = BLOCK_D, 32
-    blocks = [_random_gs_block(dev, g) for _ in range(GS_BLOCKS)]
-    dec = GaussianDecoder(blocks, torch.randn((D, 3), device=dev, generator=g) * 0.5,
-                          torch.randn(D, device=dev, generator=g) * 0.01,
-                          Q8Weight.from_float(torch.randn((D, D), device=dev, generator=g) * 0.03),
-                          Q8Weight.from_float(torch.randn((15 * G, D), device=dev, generator=g) * 0.03),
-                          2.0 ** torch.linspace(0, 10, D // 6), G, torch.randn(3 * G, device=dev, generator=g) * 0.1,
-                          -1.0)
+    dec = _random_gaussian_decoder(dev, g)
     pts = torch.rand((GS_ANCHORS, 3), device=dev, generator=g)
     cond = torch.randn((GS_LATENTS, GS_COND), device=dev, generator=g)
 
