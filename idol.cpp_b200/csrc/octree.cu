@@ -372,16 +372,18 @@ int idol_b200_oct_sampler_points(idol_oct_sampler* s, float* points) {
 int idol_b200_oct_sample_anchors(const idol_oct_decoder* d, const float* cond, int64_t cond_rows, int num_points,
                                  int level, uint64_t seed, float* points, void* workspace, int64_t workspace_bytes,
                                  void* stream) {
-    if (!d || !points) return fail(IDOL_ERR_INVALID, "oct_sample_anchors: NULL");
+    if (!d || !points || (!d->blocks.empty() && !cond)) return fail(IDOL_ERR_INVALID, "oct_sample_anchors: NULL");
+    if (cond_rows < 1 || cond_rows > 65535LL * 16)
+        return fail(IDOL_ERR_INVALID, "oct_sample_anchors: cond_rows must be 1..1,048,560");
     if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 ||
         workspace_bytes < idol_b200_oct_decoder_workspace_bytes(d, num_points, cond_rows))
         return fail(IDOL_ERR_INVALID, "oct_sample_anchors: workspace smaller than "
                                       "idol_b200_oct_decoder_workspace_bytes(decoder, num_points, cond_rows) or not "
                                       "256-byte aligned");
+    IDOL_CUDA(cudaSetDevice(d->device));
     idol_oct_sampler* s = nullptr;
     int rc = idol_b200_oct_sampler_create(num_points, level, seed, &s);
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(cudaSetDevice(d->device));
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     std::vector<float> centres, logits;
     for (int l = 0; l < level && rc == IDOL_OK; ++l) {

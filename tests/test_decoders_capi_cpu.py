@@ -1,0 +1,97 @@
+"""Argument checks of the decoders' C-ABI entry points that answer before touching a GPU (runs without one): matrix
+handles are views over placeholder addresses that are never dereferenced, since every call here is refused first."""
+import ctypes
+
+import pytest
+
+FAKE = 1 << 20  # a 256-byte aligned placeholder "device" address; never dereferenced
+
+
+def _view(C, out, inp):
+    h = ctypes.c_void_p()
+    C.check(C.lib().idol_b200_q8_view(ctypes.c_void_p(FAKE), None, out, inp, 0, ctypes.byref(h)))
+    return h
+
+
+def _oct_block(C, D=256, cond=16):
+    h = ctypes.c_void_p()
+    q, o, f1, f2 = _view(C, D, D), _view(C, D, D), _view(C, 4 * D, D), _view(C, D, 4 * D)
+    C.check(C.lib().idol_b200_oct_block_create(q, o, f1, f2, ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE),
+                                               ctypes.c_void_p(FAKE), None, cond, D // 64, ctypes.byref(h)))
+    return h
+
+
+def test_oct_block_and_decoder_shape_checks(pkg):
+    C = pkg._capi
+    L = C.lib()
+    D = 256
+    h = ctypes.c_void_p()
+    # head_dim must be 64; cond_dim 1..64
+    assert L.idol_b200_oct_block_create(_view(C, D, D), _view(C, D, D), _view(C, 4 * D, D), _view(C, D, 4 * D),
+                                        ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE), None,
+                                        16, 3, ctypes.byref(h)) == C.ERR_UNSUPPORTED
+    assert L.idol_b200_oct_block_create(_view(C, D, D), _view(C, D, D), _view(C, 4 * D, D), _view(C, D, 4 * D),
+                                        ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE), None,
+                                        65, 4, ctypes.byref(h)) == C.ERR_UNSUPPORTED
+    blk = _oct_block(C)
+    arr = (ctypes.c_void_p * 1)(blk.value)
+    dec = ctypes.c_void_p()
+    args = [ctypes.cast(arr, ctypes.c_void_p), 1, ctypes.c_void_p(FAKE), None, _view(C, D, D), _view(C, D, 256),
+            _view(C, D, D), _view(C, 6 * D, D)]
+    # out_proj must have 8 outputs
+    assert L.idol_b200_oct_decoder_create(*args, _view(C, 7, D), ctypes.c_void_p(FAKE), 42, ctypes.c_void_p(FAKE),
+                                          4, ctypes.c_float(1e-6), ctypes.byref(dec)) == C.ERR_INVALID
+    C.check(L.idol_b200_oct_decoder_create(*args, _view(C, 8, D), ctypes.c_void_p(FAKE), 42, ctypes.c_void_p(FAKE),
+                                           4, ctypes.c_float(1e-6), ctypes.byref(dec)))
+    ws = L.idol_b200_oct_decoder_workspace_bytes(dec, 1000, 500)
+    assert ws > 1000 * D * 4
+    pts = (ctypes.c_float * 30)()
+    # refused before any device call: no condition for a decoder with blocks, empty condition, small workspace
+    assert L.idol_b200_oct_sample_anchors(dec, None, 500, 10, 3, 1, pts, ctypes.c_void_p(FAKE), ws,
+                                          None) == C.ERR_INVALID
+    assert L.idol_b200_oct_sample_anchors(dec, ctypes.c_void_p(FAKE), 0, 10, 3, 1, pts, ctypes.c_void_p(FAKE), ws,
+                                          None) == C.ERR_INVALID
+    need = L.idol_b200_oct_decoder_workspace_bytes(dec, 10, 500)
+    assert L.idol_b200_oct_sample_anchors(dec, ctypes.c_void_p(FAKE), 500, 10, 3, 1, pts, ctypes.c_void_p(FAKE),
+                                          need - 256, None) == C.ERR_INVALID
+    assert b"workspace" in L.idol_b200_last_error()
+    L.idol_b200_oct_decoder_free(dec)
+    L.idol_b200_oct_block_free(blk)
+
+
+def test_gs_block_and_decoder_checks(pkg):
+    C = pkg._capi
+    L = C.lib()
+    D = 256
+    g = ctypes.c_void_p()
+    vecs = [ctypes.c_void_p(FAKE)] * 6
+    base = [_view(C, 3 * D, D), _view(C, D, D), _view(C, D, D), _view(C, D, D), _view(C, 4 * D, D),
+            _view(C, D, 4 * D)]
+    assert L.idol_b200_gs_block_create(*base, *vecs, ctypes.c_void_p(FAKE), None, 65, 4, ctypes.c_float(1e-6),
+                                       ctypes.byref(g)) == C.ERR_UNSUPPORTED
+    C.check(L.idol_b200_gs_block_create(*base, *vecs, ctypes.c_void_p(FAKE), None, 16, 4, ctypes.c_float(1e-6),
+                                        ctypes.byref(g)))
+    arr = (ctypes.c_void_p * 1)(g.value)
+    dec = ctypes.c_void_p()
+    rep = (ctypes.c_float * 9)(1.5, 0.0009, 0.004, 0.1, 1, 1, 1, 1, 0.1)
+    # out_proj must hold 15 per_anchor rows
+    assert L.idol_b200_gs_decoder_create(ctypes.cast(arr, ctypes.c_void_p), 1, ctypes.c_void_p(FAKE), None,
+                                         _view(C, D, D), _view(C, 470, D), ctypes.c_void_p(FAKE), 42, 32,
+                                         ctypes.c_void_p(FAKE), ctypes.c_float(-1.0), rep,
+                                         ctypes.byref(dec)) == C.ERR_INVALID
+    bad = (ctypes.c_float * 9)(1.5, 0.0009, 0.004, 1.5, 1, 1, 1, 1, 0.1)  # opacity bias outside (0, 1)
+    assert L.idol_b200_gs_decoder_create(ctypes.cast(arr, ctypes.c_void_p), 1, ctypes.c_void_p(FAKE), None,
+                                         _view(C, D, D), _view(C, 480, D), ctypes.c_void_p(FAKE), 42, 32,
+                                         ctypes.c_void_p(FAKE), ctypes.c_float(-1.0), bad,
+                                         ctypes.byref(dec)) == C.ERR_INVALID
+    C.check(L.idol_b200_gs_decoder_create(ctypes.cast(arr, ctypes.c_void_p), 1, ctypes.c_void_p(FAKE), None,
+                                          _view(C, D, D), _view(C, 480, D), ctypes.c_void_p(FAKE), 42, 32,
+                                          ctypes.c_void_p(FAKE), ctypes.c_float(-1.0), rep, ctypes.byref(dec)))
+    ws = L.idol_b200_gs_decoder_workspace_bytes(dec, 100, 200)
+    assert L.idol_b200_gs_decoder_features(dec, ctypes.c_void_p(FAKE), 100, None, 200, ctypes.c_void_p(FAKE),
+                                           ctypes.c_void_p(FAKE), ws, None) == C.ERR_INVALID
+    assert L.idol_b200_gs_decoder_features(dec, ctypes.c_void_p(FAKE), 100, ctypes.c_void_p(FAKE), 200,
+                                           ctypes.c_void_p(FAKE), ctypes.c_void_p(FAKE), ws - 256,
+                                           None) == C.ERR_INVALID
+    L.idol_b200_gs_decoder_free(dec)
+    L.idol_b200_gs_block_free(g)
