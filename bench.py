@@ -68,9 +68,9 @@ def peaks():
 
 
 # ------------------------------------------------------------------------------------------------ CPU (reference)
-def cpu_reference_sample(seconds=12.0, m_cap=256):
-    """The reference's gemm_packed float kernel over the sweep with M capped at m_cap rows; returns (TFLOP/s, cores,
-    kind, sample description)."""
+def cpu_reference_runner(m_cap=256):
+    """Builds the reference's gemm_packed float kernel over the sweep with M capped at m_cap rows (operands made
+    once) and returns sample(seconds) -> (TFLOP/s, cores, kind, sample description), each sample at least one pass."""
     from oracle import oracle as O
     kind = "reference" if O.have_ref() else "port"
     cores = os.cpu_count() or 1
@@ -91,18 +91,27 @@ def cpu_reference_sample(seconds=12.0, m_cap=256):
         run = lambda i: O.gemm_q8(cases[i][4], cases[i][3], cases[i][5], cases[i][2], cases[i][1])  # noqa: E731
     for i in range(len(cases)):  # warm-up pass
         run(i)
-    total_flops, passes, t0 = 0.0, 0, time.perf_counter()
-    while True:
-        for i, (mm, k, n, *_) in enumerate(cases):
-            run(i)
-            total_flops += flops(mm, k, n)
-        passes += 1
-        if time.perf_counter() - t0 >= seconds:
-            break
-    dt = time.perf_counter() - t0
-    sample = (f"{passes} passes of the 18-shape sweep with M capped at {m_cap} rows "
-              f"({total_flops / passes / 1e9:.1f} GFLOP per pass), {'OpenMP' if kind == 'reference' else 'scalar'}")
-    return total_flops / dt / 1e12, cores, kind, sample
+
+    def sample(seconds):
+        total_flops, passes, t0 = 0.0, 0, time.perf_counter()
+        while True:
+            for i, (mm, k, n, *_) in enumerate(cases):
+                run(i)
+                total_flops += flops(mm, k, n)
+            passes += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        text = (f"{passes} passes of the 18-shape sweep with M capped at {m_cap} rows "
+                f"({total_flops / passes / 1e9:.1f} GFLOP per pass), {'OpenMP' if kind == 'reference' else 'scalar'}")
+        return total_flops / dt / 1e12, cores, kind, text
+
+    return sample
+
+
+def cpu_reference_sample(seconds=12.0, m_cap=256):
+    """One bounded sample of the reference's CPU kernel over the sweep: (TFLOP/s, cores, kind, description)."""
+    return cpu_reference_runner(m_cap)(seconds)
 
 
 # ------------------------------------------------------------------------------------------------------ clocks
@@ -714,12 +723,15 @@ def measure_mlp(pkg, dev, stream, steps, world):
 def run_reference(args, rank):
     if rank != 0:
         return
-    seconds_per_step = 2.0
+    # Each step is a bounded sample (at least one pass of the capped sweep); the whole run stays within a few minutes
+    # however many steps are asked for.
+    seconds_per_step = min(2.0, 150.0 / max(1, args.steps))
+    sample = cpu_reference_runner()
     vals = []
     for _ in range(args.warmup):
-        cpu_reference_sample(seconds=0.5)
+        sample(0.0)
     for _ in range(args.steps):
-        v, cores, kind, sample = cpu_reference_sample(seconds=seconds_per_step)
+        v, cores, kind, text = sample(seconds_per_step)
         vals.append(v)
     v = statistics.median(vals)
     print(json.dumps({
@@ -727,8 +739,9 @@ def run_reference(args, rank):
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
         "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
-                   "sample": f"M capped at 256 rows per shape, {seconds_per_step:.0f} s of CPU work per step"},
-        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+                   "sample": f"M capped at 256 rows per shape, {seconds_per_step:.2f} s (at least one pass) of CPU "
+                             "work per step"},
+        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": text},
         "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
