@@ -46,7 +46,7 @@ SIGNATURES = {
     "idol_b200_norm_rows": (_i32, [_vp, _i32, _i64, _i32, _i64, ctypes.c_float, _vp, _vp, _vp, _vp, _vp, _i32, _i64,
                                    _vp]),
     "idol_b200_rms_heads": (_i32, [_vp, _i32, _i64, _i64, _i32, _i32, _vp, _vp]),
-    "idol_b200_attention": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _i32, _vp]),
+    "idol_b200_attention": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _i32, _i64, _i32, _vp]),
     "idol_b200_block_create": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.c_float, ctypes.POINTER(_vp)]),
     "idol_b200_block_free": (_i32, [_vp]),
     "idol_b200_block_workspace_bytes": (_i64, [_vp, _i64]),

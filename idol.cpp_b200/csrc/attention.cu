@@ -16,7 +16,7 @@
 //                 loads its S row (then frees the S buffer), updates the running max and sum, writes P (bf16) to TMEM;
 //                 O and the sum are rescaled only when the row maximum grows by more than 2^8 over the one in use
 //                 (P stays <= 256, exact in bf16 range, and the final O / sum cancels the stale maximum), so O stays
-//                 in TMEM with no per-block fold; at the end the row is divided by its sum and stored as bf16.
+//                 in TMEM with no per-block fold; at the end the row is divided by its sum and stored as bf16 (or fp32).
 // The same 128-byte-swizzled K/V tile layout serves as the K-major B operand of Q K^T and the MN-major B operand of
 // P V. Every wait is bounded (ptx.cuh); a timeout raises the sticky device error and the CTA winds down.
 #include <cuda_bf16.h>
@@ -48,6 +48,7 @@ constexpr float kRescaleLog2 = 8.0f;  // rescale O and the sum once the row max 
 struct AttnParams {
     void* out;
     long long ldo;              // output row stride (elements)
+    int out_f32;                // 1: fp32 output rows, 0: bf16
     long long out_img_stride;   // rows of one image in the output = lq
     int lq, lk, heads;
     float scale_log2;           // log2(e) / sqrt(hd)
@@ -313,7 +314,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld16(tt + kColO + c0, *reinterpret_cast<uint32_t(*)[16]>(o + c0));
                 tmem_ld_wait();
                 const int qrow = q0 + t * kQTile + r;
-                if (qrow < p.lq) {
+                if (qrow < p.lq && p.out_f32) {
+                    const float inv = 1.0f / l_run;
+                    float* out = static_cast<float*>(p.out) +
+                                 ((long long)img * p.out_img_stride + qrow) * p.ldo + (long long)h * kHd;
+#pragma unroll
+                    for (int c0 = 0; c0 < kHd; c0 += 4) {
+                        float4 pkt;
+                        pkt.x = __uint_as_float(o[c0 + 0]) * inv;
+                        pkt.y = __uint_as_float(o[c0 + 1]) * inv;
+                        pkt.z = __uint_as_float(o[c0 + 2]) * inv;
+                        pkt.w = __uint_as_float(o[c0 + 3]) * inv;
+                        *reinterpret_cast<float4*>(out + c0) = pkt;
+                    }
+                } else if (qrow < p.lq) {
                     const float inv = 1.0f / l_run;
                     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) +
                                          ((long long)img * p.out_img_stride + qrow) * p.ldo + (long long)h * kHd;
@@ -380,6 +394,7 @@ int attention(const AttentionCall& c) {
     AttnParams p;
     p.out = c.out;
     p.ldo = c.ldo;
+    p.out_f32 = c.out_f32 ? 1 : 0;
     p.out_img_stride = c.lq;
     p.lq = (int)c.lq;
     p.lk = (int)c.lk;

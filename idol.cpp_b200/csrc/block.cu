@@ -539,6 +539,8 @@ int idol_b200_gaussian_mlp_create(const idol_q8_matrix* l0, const idol_q8_matrix
     if (!mlp) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: mlp is NULL");
     *mlp = nullptr;
     if (!l0 || !l1 || !l2) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: NULL");
+    if (l1->m.device != l0->m.device || l2->m.device != l0->m.device)
+        return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: matrices on different devices");
     if (l1->m.k != l0->m.n || l2->m.k != l1->m.n || l2->m.n != 14)
         return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: layer shapes must chain and end in 14 outputs");
     if (l0->m.n % 8 || l1->m.n % 8) return fail(IDOL_ERR_INVALID, "gaussian_mlp_create: hidden widths % 8 != 0");

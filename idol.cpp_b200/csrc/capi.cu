@@ -382,9 +382,11 @@ int idol_b200_rms_heads(void* x, int dtype, int64_t rows, int64_t ld, int heads,
 }
 
 int idol_b200_attention(const void* q, int64_t lq, int64_t ldq, const void* k, const void* v, int64_t lk, int64_t ldkv,
-                        int heads, int head_dim, void* out, int64_t ldo, int batch, void* stream) {
+                        int heads, int head_dim, void* out, int out_dtype, int64_t ldo, int batch, void* stream) {
+    if (out_dtype != IDOL_BF16 && out_dtype != IDOL_F32)
+        return fail(IDOL_ERR_UNSUPPORTED, "attention: the output dtype must be IDOL_BF16 or IDOL_F32");
     idol::AttentionCall c = {q, k, v, out, lq, lk, ldq, ldkv, ldo, heads, head_dim, batch,
-                             static_cast<cudaStream_t>(stream)};
+                             static_cast<cudaStream_t>(stream), out_dtype == IDOL_F32};
     return idol::attention(c);
 }
 

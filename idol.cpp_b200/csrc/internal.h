@@ -111,6 +111,7 @@ struct AttentionCall {
     long long lq, lk, ldq, ldkv, ldo;
     int heads, head_dim, batch;
     cudaStream_t stream;
+    bool out_f32;  // fp32 output rows instead of bf16 (false when left out of an aggregate initialiser)
 };
 int attention(const AttentionCall& c);
 

@@ -50,7 +50,8 @@ def rms_heads_(x: torch.Tensor, heads: int, gamma: torch.Tensor, head_dim: int =
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, batch: int = 1,
               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """softmax(q k^T / sqrt(64)) v per head for `batch` independent sequences stacked along the rows.
-    q: [batch * lq, >= heads*64] bf16 view; k, v: [batch * lk, >= heads*64] views; returns [batch * lq, heads*64]."""
+    q: [batch * lq, >= heads*64] bf16 view; k, v: [batch * lk, >= heads*64] views; returns [batch * lq, heads*64] in
+    bf16, or in fp32 when `out` is an fp32 tensor."""
     for t in (q, k, v):
         if t.dim() != 2 or t.stride(1) != 1 or t.dtype != torch.bfloat16:
             raise ValueError("attention: expected 2-D bf16 views with unit column stride")
@@ -62,6 +63,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, bat
     lq, lk = q.shape[0] // batch, k.shape[0] // batch
     if out is None:
         out = torch.empty((q.shape[0], dim), dtype=torch.bfloat16, device=q.device)
+    if out.dtype not in (torch.bfloat16, torch.float32) or out.dim() != 2 or out.stride(1) != 1:
+        raise ValueError("attention: out must be a 2-D bf16 or fp32 tensor with unit column stride")
     C.check(C.lib().idol_b200_attention(_ptr(q), lq, q.stride(0), _ptr(k), _ptr(v), lk, k.stride(0), heads, 64,
-                                        _ptr(out), out.stride(0), batch, _stream(q.device)))
+                                        _ptr(out), _DTYPES[out.dtype], out.stride(0), batch, _stream(q.device)))
     return out

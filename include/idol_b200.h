@@ -152,12 +152,13 @@ int idol_b200_norm_rows(const void* x, int x_dtype, int64_t rows, int dim, int64
 int idol_b200_rms_heads(void* x, int dtype, int64_t rows, int64_t ld, int heads, int head_dim, const float* gamma,
                         void* stream);
 
-/* Multi-head attention, bf16: for each of `batch` independent sequences (q rows b*lq.., k/v rows b*lk..), per head h
- * out[:, h*hd:(h+1)*hd] = softmax(q_h k_h^T / sqrt(hd)) v_h. Replaces src/kernels.cpp:737-746 attention
+/* Multi-head attention, bf16 q/k/v: for each of `batch` independent sequences (q rows b*lq.., k/v rows b*lk..), per
+ * head h out[:, h*hd:(h+1)*hd] = softmax(q_h k_h^T / sqrt(hd)) v_h. Replaces src/kernels.cpp:737-746 attention
  * (q lq rows ldq apart; k, v lk rows ldkv apart, e.g. k = kv and v = kv + dim as src/decoders.cpp:239 passes them; out
- * rows ldo apart). head_dim 64; pointers 16-byte aligned; strides multiples of 8 elements. */
+ * rows ldo apart). out_dtype IDOL_BF16 (what the next Q8_0 GEMM consumes) or IDOL_F32 (the reference's own output
+ * type). head_dim 64; pointers 16-byte aligned; strides multiples of 8 elements. */
 int idol_b200_attention(const void* q, int64_t lq, int64_t ldq, const void* k, const void* v, int64_t lk, int64_t ldkv,
-                        int heads, int head_dim, void* out, int64_t ldo, int batch, void* stream);
+                        int heads, int head_dim, void* out, int out_dtype, int64_t ldo, int batch, void* stream);
 
 /* ------------------------------------------------------------------------------------------------ compositions */
 
@@ -277,8 +278,10 @@ int64_t idol_b200_gaussian_mlp_workspace_bytes(const idol_gaussian_mlp* mlp, int
 int idol_b200_gaussian_mlp_forward(const idol_gaussian_mlp* mlp, const void* x, int64_t points, int64_t ldx,
                                    void* workspace, int64_t workspace_bytes, float* raw_out, float* out, void* stream);
 /* The same Gaussian MLP forward for callers that cannot allocate device memory at all, not even once for a
- * workspace: code running where CUDA allocation calls are not allowed (for example a host function enqueued on a
- * stream) or in a process whose device memory another allocator has already reserved in full. It allocates nothing:
+ * workspace: a process whose device memory another allocator (a framework's caching pool, an inference server's
+ * arena) has already reserved in full, so a cudaMalloc of its own would fail or fragment that pool. It is a regular
+ * host-side call - it selects the device and launches kernels - so it must not be made from a stream callback
+ * (cudaLaunchHostFunc), where no CUDA call is allowed. It allocates nothing:
  * its scratch is a fixed 8 MiB array in the library's device code, reserved on every GPU that loads the library and
  * held until exit; the caller still passes x, raw_out (or NULL) and out. A batch whose scratch would not fit
  * (idol_b200_gaussian_mlp_workspace_bytes(mlp, points) > 8 MiB: about 3,980 points for 128 -> 512 -> 512 -> 14) is

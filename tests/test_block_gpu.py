@@ -1,8 +1,8 @@
 """GPU parity of the compositions: the denoiser block (scope row A14) and the Gaussian MLP (row A15).
 
 * Small block (2 images x 128 tokens, D 1024, 16 heads, hidden 4096) against the CPU oracle's composition of the
-  pinned reference functions, bar max |y - ref| <= 2e-2 x rms(ref) on the block output; plus the block's update
-  (out - x) at 5e-2 x rms, which each sublayer must get right.
+  pinned reference functions, bar max |y - ref| <= 2e-2 x rms(ref) on the block output and on the block's update
+  (out - x), which each sublayer must get right.
 * Config-3 size (2 x 4096 tokens) against an fp32 torch composition of the same math on the same GPU (dequantised
   weights, fp32 matmuls with TF32 off, fp32 softmax attention).
 * Gaussian MLP at config-4 size (262,144 points): rows are independent, so sampled rows are checked against the
@@ -17,16 +17,14 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 
 
-def _check(y, ref, tol=TOL, what="", ulp_rel=0.0, stored=None):
-    """max |y - ref| <= tol x rms(ref), beyond ulp_rel x |stored| per element (stored defaults to ref): one bf16 ulp,
-    2^-7 of the stored value, where y derives from a bf16 stream that the oracle rounds at the same points, so the
-    two can round one ulp apart."""
+def _check(y, ref, tol=TOL, what=""):
+    """max |y - ref| <= tol x rms(ref); prints the measured ratio."""
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
-    stored = ref if stored is None else np.asarray(stored, np.float64)
     assert np.isfinite(y).all(), what
     rms = np.sqrt((ref ** 2).mean())
-    err = (np.abs(y - ref) - ulp_rel * np.abs(stored)).max()
+    err = np.abs(y - ref).max()
+    print(f"\n{what}: max|err|/rms {err / rms:.3e}")
     assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
 
 
@@ -60,7 +58,7 @@ def test_block_small_against_the_oracle(pkg, oracle, cuda, x_dtype):
     torch.cuda.synchronize()
     y = xt.float().cpu().numpy()
     _check(y, ref, what=f"block output ({x_dtype})")
-    _check(y - x, ref - x, tol=5e-2, what=f"block update ({x_dtype})")
+    _check(y - x, ref - x, what=f"block update ({x_dtype})")
 
 
 def _torch_block(x, ws, heads, eps=1e-6, images=1):
@@ -142,9 +140,8 @@ def test_gaussian_block_with_cross_attention_against_the_oracle(pkg, oracle, cud
     blk.forward_(xt, torch.from_numpy(cond).to(cuda), images=images)
     torch.cuda.synchronize()
     y = xt.float().cpu().numpy()
-    ulp = 2.0 ** -7 if x_dtype == torch.bfloat16 else 0.0
-    _check(y, ref, what=f"Gaussian block output ({x_dtype})", ulp_rel=ulp)
-    _check(y - x, ref - x, tol=5e-2, what=f"Gaussian block update ({x_dtype})", ulp_rel=ulp, stored=ref)
+    _check(y, ref, what=f"Gaussian block output ({x_dtype})")
+    _check(y - x, ref - x, what=f"Gaussian block update ({x_dtype})")
 
 
 def test_gaussian_block_rejects_bad_condition_shapes(pkg, oracle, cuda):
@@ -175,7 +172,7 @@ def test_block_config3_size_against_torch_fp32(pkg, oracle, cuda):
     blk.forward_(y, images=images)
     torch.cuda.synchronize()
     _check(y.cpu().numpy(), ref.cpu().numpy(), what="config-3 block vs torch fp32")
-    _check((y - x).cpu().numpy(), (ref - x).cpu().numpy(), tol=5e-2, what="config-3 block update vs torch fp32")
+    _check((y - x).cpu().numpy(), (ref - x).cpu().numpy(), what="config-3 block update vs torch fp32")
 
 
 def test_gaussian_mlp_config4_sampled_rows(pkg, oracle, cuda):

@@ -95,3 +95,23 @@ def test_gs_block_and_decoder_checks(pkg):
                                            None) == C.ERR_INVALID
     L.idol_b200_gs_decoder_free(dec)
     L.idol_b200_gs_block_free(g)
+
+
+def test_gaussian_mlp_create_refuses_matrices_on_different_devices(pkg):
+    C = pkg._capi
+    L = C.lib()
+
+    def view(out, inp, device):
+        h = ctypes.c_void_p()
+        C.check(L.idol_b200_q8_view(ctypes.c_void_p(FAKE), None, out, inp, device, ctypes.byref(h)))
+        return h
+
+    mlp = ctypes.c_void_p()
+    for devs in ((0, 1, 0), (0, 0, 1)):
+        assert L.idol_b200_gaussian_mlp_create(view(512, 128, devs[0]), view(512, 512, devs[1]),
+                                               view(14, 512, devs[2]), ctypes.byref(mlp)) == C.ERR_INVALID
+        assert b"different devices" in L.idol_b200_last_error()
+        assert not mlp.value
+    C.check(L.idol_b200_gaussian_mlp_create(view(512, 128, 0), view(512, 512, 0), view(14, 512, 0),
+                                            ctypes.byref(mlp)))
+    L.idol_b200_gaussian_mlp_free(mlp)

@@ -1,9 +1,13 @@
 """GPU parity of the norms and attention against the CPU oracle (pinned to the reference's norm_rows, rms_heads and
-attention in tests/test_oracle.py). Bars, bf16 in and out against fp32:
-  norms     : max |y - ref| <= 2e-2 x rms(ref);
-  attention : |y - ref| <= 2e-2 x rms(ref) + 1e-2 x |ref| elementwise. Random unnormalised q and k make some rows
-              peaked, so an output element can be ~60x the output RMS; the bf16 rounding of P and of the output then
-              scales with that element (2^-8 relative), which the pure RMS bar cannot absorb."""
+attention in tests/test_oracle.py). One bar for every check, bf16 inputs against the fp32 oracle:
+max |y - ref| <= 2e-2 x rms(ref).
+
+Attention is checked twice per case: its fp32 output against the oracle, and its bf16 output, which must be the fp32
+output rounded to bf16 bit for bit (the kernel rounds once, at the store). Inputs: the reference's own attention-test
+distribution (uniform in [-1, 1], tests/test_kernels.cpp:184-191) and the blocks' distribution (q and k through
+rms_heads, so each head has norm 8 and its scores have unit spread), where the bf16 output is also held to the bar
+(the rows with one dominant key then carry values near the largest of v, the case the bf16 store can miss; the
+measured ratio is printed)."""
 import numpy as np
 import pytest
 import torch
@@ -23,13 +27,11 @@ def _check(y, ref, tol=TOL, what=""):
     assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
 
 
-def _check_attn(y, ref, what=""):
+def _ratio(y, ref):
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
-    assert np.isfinite(y).all(), what
-    rms = np.sqrt((ref ** 2).mean())
-    excess = np.abs(y - ref) - (TOL * rms + 1e-2 * np.abs(ref))
-    assert excess.max() <= 0, f"{what}: worst excess {excess.max():.3e} (rms {rms:.3e})"
+    assert np.isfinite(y).all()
+    return float(np.abs(y - ref).max() / np.sqrt((ref ** 2).mean()))
 
 
 def _bf(oracle, a):
@@ -85,50 +87,74 @@ def test_rms_heads(pkg, oracle, cuda):
     _check(xt.float().cpu().numpy()[:, 1024:2048], ref[:, 1024:2048], what="rms_heads bf16")
 
 
-def _attention_case(oracle, cuda, lq, lk, heads, batch=1, packed=True, seed=0, rows=None):
+def _draw(oracle, rng, shape, dist, heads=None, qk_cols=0):
+    """bf16-representable inputs: 'uniform' = U(-1, 1) as the reference's attention test; 'blocks' = N(0, 1) with the
+    first qk_cols columns (q or q,k) normalised per 64-wide head to norm 8, as rms_heads leaves them."""
+    if dist == "uniform":
+        return _bf(oracle, rng.uniform(-1, 1, shape))
+    a = rng.normal(0, 1, shape)
+    if qk_cols:
+        h = a[:, :qk_cols].reshape(shape[0], qk_cols // 64, 64)
+        a[:, :qk_cols] = (h * (8.0 / np.linalg.norm(h, axis=2, keepdims=True))).reshape(shape[0], qk_cols)
+    return _bf(oracle, a)
+
+
+def _attention_case(oracle, cuda, lq, lk, heads, batch=1, packed=True, seed=0, rows=None, dist="uniform"):
     from idol_b200 import layers
     rng = np.random.default_rng(seed)
     dim = heads * 64
     if packed:  # self-attention layout: q, k, v are column blocks of one qkv buffer (src/decoders.cpp:301)
         assert lq == lk
-        qkv = _bf(oracle, rng.normal(0, 1, (batch * lq, 3 * dim)))
+        qkv = _draw(oracle, rng, (batch * lq, 3 * dim), dist, qk_cols=2 * dim)
         t = torch.from_numpy(qkv).to(cuda, torch.bfloat16)
         q, k, v = t[:, :dim], t[:, dim:2 * dim], t[:, 2 * dim:]
         qn, kn, vn = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
     else:  # cross-attention layout: q alone (row stride dim + 8), kv packed (src/decoders.cpp:239)
-        qn = _bf(oracle, rng.normal(0, 1, (batch * lq, dim + 8)))
-        kv = _bf(oracle, rng.normal(0, 1, (batch * lk, 2 * dim)))
+        qn = _draw(oracle, rng, (batch * lq, dim + 8), dist, qk_cols=dim)
+        kv = _draw(oracle, rng, (batch * lk, 2 * dim), dist, qk_cols=dim)
         qt = torch.from_numpy(qn).to(cuda, torch.bfloat16)
         kvt = torch.from_numpy(kv).to(cuda, torch.bfloat16)
         q, k, v = qt[:, :dim], kvt[:, :dim], kvt[:, dim:]
         qn, kn, vn = qn[:, :dim], kv[:, :dim], kv[:, dim:]
-    out = layers.attention(q, k, v, heads, batch=batch)
+    out16 = layers.attention(q, k, v, heads, batch=batch)
+    out32 = layers.attention(q, k, v, heads, batch=batch,
+                             out=torch.empty((batch * lq, dim), dtype=torch.float32, device=cuda))
     torch.cuda.synchronize()
-    got = out.float().cpu().numpy()
+    assert torch.equal(out16, out32.to(torch.bfloat16)), "bf16 output is not the fp32 output rounded once"
+    got32, got16 = out32.cpu().numpy(), out16.float().cpu().numpy()
+    worst32 = worst16 = 0.0
     for b in range(batch):
         sel = np.arange(lq) if rows is None else rows
         ref = oracle.attention(np.ascontiguousarray(qn[b * lq:(b + 1) * lq][sel]),
                                np.ascontiguousarray(kn[b * lk:(b + 1) * lk]),
                                np.ascontiguousarray(vn[b * lk:(b + 1) * lk]), heads, 64)
-        _check_attn(got[b * lq:(b + 1) * lq][sel], ref, what=f"attention lq={lq} lk={lk} h={heads} b={b}")
+        worst32 = max(worst32, _ratio(got32[b * lq:(b + 1) * lq][sel], ref))
+        worst16 = max(worst16, _ratio(got16[b * lq:(b + 1) * lq][sel], ref))
+    what = f"attention {dist} lq={lq} lk={lk} h={heads} batch={batch}"
+    print(f"\n{what}: max|err|/rms fp32 out {worst32:.3e}, bf16 out {worst16:.3e}")
+    assert worst32 <= TOL, f"{what}: fp32 output max abs err / rms {worst32:.3e} > {TOL}"
+    assert worst16 <= TOL, f"{what}: bf16 output max abs err / rms {worst16:.3e} > {TOL}"
 
 
+@pytest.mark.parametrize("dist", ["uniform", "blocks"])
 @pytest.mark.parametrize("lq,lk,heads", [(37, 53, 2), (3, 16, 1), (70, 130, 2), (128, 128, 1), (129, 257, 3),
                                          (300, 1000, 4)])
-def test_attention_ragged_cross(pkg, oracle, cuda, lq, lk, heads):
+def test_attention_ragged_cross(pkg, oracle, cuda, lq, lk, heads, dist):
     """The reference's attention test shapes (tests/test_kernels.cpp:221-228) at head dim 64, strided q and kv."""
-    _attention_case(oracle, cuda, lq, lk, heads, packed=False, seed=lq + lk)
+    _attention_case(oracle, cuda, lq, lk, heads, packed=False, seed=lq + lk, dist=dist)
 
 
+@pytest.mark.parametrize("dist", ["uniform", "blocks"])
 @pytest.mark.parametrize("l,heads,batch", [(256, 4, 2), (200, 2, 3), (1000, 16, 1)])
-def test_attention_self_packed_batched(pkg, oracle, cuda, l, heads, batch):
-    _attention_case(oracle, cuda, l, l, heads, batch=batch, packed=True, seed=l)
+def test_attention_self_packed_batched(pkg, oracle, cuda, l, heads, batch, dist):
+    _attention_case(oracle, cuda, l, l, heads, batch=batch, packed=True, seed=l, dist=dist)
 
 
 def test_attention_config3_size_sampled_rows(pkg, oracle, cuda):
-    """4096 tokens x 16 heads x 2 images (config 3's self-attention), queries sampled across every 128-row tile."""
+    """4096 tokens x 16 heads x 2 images (config 3's self-attention, the blocks' distribution), queries sampled
+    across every 128-row tile."""
     rows = np.unique(np.concatenate([np.arange(0, 4096, 97), [0, 127, 128, 4095]]))
-    _attention_case(oracle, cuda, 4096, 4096, 16, batch=2, packed=True, seed=3, rows=rows)
+    _attention_case(oracle, cuda, 4096, 4096, 16, batch=2, packed=True, seed=3, rows=rows, dist="blocks")
 
 
 def test_attention_golden(pkg, cuda):
@@ -137,8 +163,11 @@ def test_attention_golden(pkg, cuda):
     rows, dim, heads, hd, lq, lk = (int(v) for v in z["meta"])
     q = torch.from_numpy(z["att_q"]).to(cuda, torch.bfloat16)
     kv = torch.from_numpy(z["att_kv"]).to(cuda, torch.bfloat16)
-    out = layers.attention(q[:, :dim], kv[:, :dim], kv[:, dim:2 * dim], heads)
-    _check_attn(out.float().cpu().numpy(), z["att_out"], what="golden attention (bf16 inputs)")
+    out = layers.attention(q[:, :dim], kv[:, :dim], kv[:, dim:2 * dim], heads,
+                           out=torch.empty((q.shape[0], dim), dtype=torch.float32, device=cuda))
+    r = _ratio(out.cpu().numpy(), z["att_out"])
+    print(f"\ngolden attention: max|err|/rms fp32 out {r:.3e}")
+    assert r <= TOL, f"golden attention (bf16 inputs): max abs err / rms {r:.3e} > {TOL}"
 
 
 def test_layers_no_timeout(pkg, cuda):

@@ -1,8 +1,8 @@
 """The allocation-free Gaussian MLP entry point (idol_b200_gaussian_mlp_forward_static).
 
-Some callers cannot allocate device memory at all: code that runs where CUDA allocation calls are not allowed, such as
-a host function enqueued on a stream, or a process whose GPU memory another allocator has already reserved in full.
-They cannot hand the regular entry point (idol_b200_gaussian_mlp_forward) a workspace, so this variant keeps its
+Some callers cannot allocate device memory at all: a process whose GPU memory another allocator (a framework's
+caching pool, a server's arena) has already reserved in full, where a cudaMalloc of its own would fail. They cannot
+hand the regular entry point (idol_b200_gaussian_mlp_forward) a workspace, so this variant keeps its
 scratch in a fixed 8 MiB array compiled into the library. This file checks, through the C-ABI, that it gives the same
 output as the regular entry point on two calls in a row, and that a batch too large for the fixed array is refused.
 It is named to be collected last, so a run that stops at the first failure has run every other test first; it also
