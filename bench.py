@@ -2,33 +2,35 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the Q8_0 GEMM shape sweep): one step = one pass over the 18 GEMMs
-M in {1, 16, 128, 1024, 4096, 16384} x (K, N) in {(1024, 3072), (1024, 4096), (4096, 1024)}: bf16 activations ~N(0,1),
-weights ~N(0,0.02) quantized to Q8_0 on the device, fp32 accumulation, bf16 out, seeded synthetic data. Every GEMM of
-a step has its own weights and activations; a step streams ~1.3 GB, so no operand is still in the 126 MB L2 when it
-is used again one step later.
+Headline workload (config 5): the denoiser's stack of 24 transformer blocks over a batch of 64 independent images, each
+image two CFG branches of 4096 tokens (D 1024, 16 heads x 64, Q8_0 QKV/out/MLP 1024->4096->1024 with GELU tanh, fp32
+residual stream, bf16 activations), seeded random weights and inputs. The 64 images are split contiguously across
+the N ranks (one process per GPU, each a full replica of the Q8_0 weights, no collective on the data path), so the
+total work is fixed and the scaling is strong. One step = one pass of the stack over this rank's images.
 
-value      : whole-job TFLOP/s = sum over ranks of 2 M N K per step x K steps / max-over-ranks device time, with all
-             operands resident in HBM (the K steps replay a CUDA graph of the 18 launches; timed by CUDA events).
-e2e        : the same metric through the drop-in API (fused_linear over GGUF Q8_0 bytes) with each step's activations
-             copied host->device from pinned memory and its outputs copied back inside the timed region; the copies of
-             the independent GEMMs are pipelined with their compute over three streams.
-roofline   : the GEMM kernel on the tensor-bound shapes (M >= 4096): 2 M N K per launch / CUDA-event duration, against
-             the measured dense bf16 peak; roofline_small_m: the HBM-bound shapes (M <= 16), algorithmic bytes
-             1.0625 N K + 2 M K + 2 M N + 4 N per launch against the measured HBM bandwidth.
-gpu_baselines: on the same GPU, per shape, the reference's unfused PackedLinear path (torch dequantize + F.linear)
-             and cuBLAS on dense bf16 weights, against the fused kernel's per-launch times (shapes[]).
-cpu_baseline: the reference's own CPU kernel (src/kernels.cpp gemm_packed, float kernel, OpenMP, compiled into
-             oracle/_ref) on a bounded sample (M capped at 256 rows per shape), rank 0 at N=1.
---impl reference: that CPU kernel alone, as the reference arm (rank 0 only under torchrun).
-N > 1: one process per GPU (torchrun), each GPU runs the full sweep on its own data; the path shards by request with
-no collective ("weak" scaling).
+value      : block-steps/s = 24 blocks x 64 images x K steps / max-over-ranks device time of the K steps (inputs
+             resident in HBM; CUDA events on the launching stream). A block-step is one image (its two CFG branches)
+             through one block: 343.6 GFLOP (206.2 in the Q8_0 linears, 137.4 in attention).
+e2e        : the same metric through DenoiserStack.forward_ with the images' residual streams in pinned host memory:
+             each chunk of images is copied host->device, run through the 24 blocks and copied back, the copies of one
+             chunk overlapping the compute of its neighbours; every copy is inside the timed region.
+roofline   : the kernel with the largest share of a block's device time, timed alone on the block's own shapes
+             (algorithmic FLOPs per launch / CUDA-event duration) against the measured dense bf16 peak; `kernels`
+             lists every kernel of the block the same way.
+gemm_sweep : (N = 1) the Q8_0 GEMM shape sweep M in {1, 16, 128, 1024, 4096, 16384} x (K, N) in {(1024, 3072),
+             (1024, 4096), (4096, 1024)}: its own rooflines (tensor-bound M >= 4096, HBM-bound M <= 16), per-shape
+             times and GPU baselines on the same device (the reference's unfused PackedLinear path, dense cuBLAS).
+cpu_baseline, --impl reference: the reference's own CPU functions (src/kernels.cpp gemm_packed float kernel and
+             attention, src/decoders.cpp norm_rows / rms_heads / gelu_tanh; OpenMP over every host thread; compiled into
+             oracle/_ref) composing the same block on the same shapes. One step is one block-step, the bounded sample of
+             the workload; rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -43,8 +45,26 @@ sys.path.insert(0, str(ROOT))
 
 MS = (1, 16, 128, 1024, 4096, 16384)
 KNS = ((1024, 3072), (1024, 4096), (4096, 1024))
-METRIC = "Q8_0 GEMM TFLOP/s (config 2 shape sweep)"
-UNIT = "TFLOP/s"
+SWEEP_METRIC = "Q8_0 GEMM TFLOP/s (config 2 shape sweep)"
+
+BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
+BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
+               + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
+STACK_BLOCKS, STACK_IMAGES, CFG = 24, 64, 2
+CHUNK_IMAGES = 2  # images per pass through the blocks (4 sequences, 32768 rows)
+LAUNCHES_PER_BLOCK = 9  # norm, qkv, rms q, rms k, attention, out + residual, norm, ff1, ff2 + residual
+METRIC = "denoiser-block steps/s (config 5: 24-block stack over 64 images x 2 CFG branches, sharded by image)"
+UNIT = "block-steps/s"
+
+
+def config5(world):
+    """The workload description both arms print (identical for the same N)."""
+    return {"workload": "config5_denoiser_stack", "blocks": STACK_BLOCKS, "images": STACK_IMAGES,
+            "cfg_branches": CFG, "tokens": BLOCK_TOKENS, "dim": BLOCK_D, "heads": BLOCK_HEADS, "hidden": BLOCK_H,
+            "weights": "Q8_0", "residual": "fp32", "activations": "bf16", "gelu": "tanh",
+            "work": "343.6 GFLOP per block-step (206.2 linears + 137.4 attention)",
+            "parallelism": f"dp{world}: images split contiguously over ranks, weights replicated, no collective",
+            "l2": "inputs larger than L2: a rank's residual streams are >= 268 MB and each step rereads them all"}
 
 
 def shapes():
@@ -68,50 +88,94 @@ def peaks():
 
 
 # ------------------------------------------------------------------------------------------------ CPU (reference)
-def cpu_reference_runner(m_cap=256):
-    """Builds the reference's gemm_packed float kernel over the sweep with M capped at m_cap rows (operands made
-    once) and returns sample(seconds) -> (TFLOP/s, cores, kind, sample description), each sample at least one pass."""
+def cpu_info():
+    """Host facts for the CPU baseline: model, usable logical CPUs, physical cores, nominal clock, and the fp32 FMA
+    peak of the AVX2 units (physical cores x GHz x 32 FLOP per cycle: two 8-wide FMA pipes)."""
+    model, phys, cur = "unknown", set(), {}
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines() + [""]:
+            if not line.strip():
+                if cur:
+                    phys.add((cur.get("physical id"), cur.get("core id", cur.get("processor"))))
+                cur = {}
+                continue
+            key, _, val = line.partition(":")
+            cur[key.strip()] = val.strip()
+            if key.strip() == "model name":
+                model = val.strip()
+    except OSError:
+        pass
+    logical = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    physical = min(len(phys), logical) if phys else logical
+    m = re.search(r"@\s*([\d.]+)\s*GHz", model)
+    ghz = float(m.group(1)) if m else None
+    return {"model": model, "logical_cpus": logical, "physical_cores": physical, "ghz": ghz,
+            "avx2_fma_peak_gflops": round(physical * ghz * 32, 1) if ghz else None}
+
+
+def cpu_reference_runner():
+    """One block-step of the config-5 block (one image: 2 CFG branches x 4096 tokens, D 1024) on the reference's own
+    CPU functions (oracle.RefBlock over oracle/_ref, every usable host thread); without oracle/_ref, the C
+    restatement on 2 x 512 tokens, converted to block-steps by its FLOPs. Returns (step() -> block-steps/s, facts)."""
     from oracle import oracle as O
-    kind = "reference" if O.have_ref() else "port"
-    cores = os.cpu_count() or 1
+    info = cpu_info()
     rng = np.random.default_rng(0)
-    cases = []
-    for (m, k, n) in shapes():
-        mm = min(m, m_cap)
-        q8 = O.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32))
-        x = O.f32_to_bf16_round(rng.normal(0, 1, (mm, k)).astype(np.float32))
-        b = np.zeros(n, np.float32)
-        cases.append((mm, k, n, q8, x, b))
-    if kind == "reference":
-        O.ref_threads(cores)
-        lins = [O.RefLinear(q8, b, n, k) for (mm, k, n, q8, x, b) in cases]
-        run = lambda i: lins[i].gemm(cases[i][4], mode=0)  # noqa: E731
+    D, H = BLOCK_D, BLOCK_H
+    layers = {}
+    for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "ff1": (H, D), "ff2": (D, H)}.items():
+        layers[name] = (O.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32)),
+                        rng.normal(0, 0.01, n).astype(np.float32), n, k)
+    layers["q_gamma"] = rng.normal(1, 0.1, D).astype(np.float32)
+    layers["k_gamma"] = rng.normal(1, 0.1, D).astype(np.float32)
+    if O.have_ref():
+        kind, threads, tokens = "reference", O.ref_threads(info["logical_cpus"]), BLOCK_TOKENS
+        blk = O.RefBlock(layers, BLOCK_HEADS)
+        run = lambda x: blk.forward_(x, images=CFG)  # noqa: E731
     else:
-        cores = 1
-        run = lambda i: O.gemm_q8(cases[i][4], cases[i][3], cases[i][5], cases[i][2], cases[i][1])  # noqa: E731
-    for i in range(len(cases)):  # warm-up pass
-        run(i)
+        kind, threads, tokens = "port", 1, 512
+        run = lambda x: O.block_forward(x, layers, BLOCK_HEADS, images=CFG)  # noqa: E731
+    x0 = O.f32_to_bf16_round(rng.normal(0, 1, (CFG * tokens, D)).astype(np.float32))
+    sample_flops = (2.0 * CFG * tokens * (3 * D * D + D * D + 2 * H * D) + 4.0 * tokens ** 2 * D * CFG)
+    unit_flops = BLOCK_FLOPS / BLOCK_IMAGES * CFG
 
-    def sample(seconds):
-        total_flops, passes, t0 = 0.0, 0, time.perf_counter()
-        while True:
-            for i, (mm, k, n, *_) in enumerate(cases):
-                run(i)
-                total_flops += flops(mm, k, n)
-            passes += 1
-            if time.perf_counter() - t0 >= seconds:
-                break
+    def step():
+        x = x0.copy()
+        t0 = time.perf_counter()
+        run(x)
         dt = time.perf_counter() - t0
-        text = (f"{passes} passes of the 18-shape sweep with M capped at {m_cap} rows "
-                f"({total_flops / passes / 1e9:.1f} GFLOP per pass), {'OpenMP' if kind == 'reference' else 'scalar'}")
-        return total_flops / dt / 1e12, cores, kind, text
+        return sample_flops / unit_flops / dt, dt
 
-    return sample
+    facts = dict(info, kind=kind, threads=threads,
+                 sample=(f"one block-step: one image (2 CFG branches x {tokens} tokens, D 1024) through one block on "
+                         + ("the reference's compiled CPU functions, OpenMP" if kind == "reference" else
+                            "the C restatement (no oracle/_ref), scaled by FLOPs to a 4096-token block-step")))
+    return step, facts
 
 
-def cpu_reference_sample(seconds=12.0, m_cap=256):
-    """One bounded sample of the reference's CPU kernel over the sweep: (TFLOP/s, cores, kind, description)."""
-    return cpu_reference_runner(m_cap)(seconds)
+def cpu_baseline_entry(rates, times, facts):
+    v = statistics.median(rates)
+    gflops = v * BLOCK_FLOPS / BLOCK_IMAGES * CFG / 1e9
+    peak = facts.get("avx2_fma_peak_gflops")
+    return {"value": round(v, 4), "unit": UNIT, "cores": facts["threads"], "kind": facts["kind"],
+            "sample": f"{facts['sample']}; median of {len(rates)} timed steps ({statistics.median(times):.2f} s each)",
+            "cpu_model": facts["model"], "physical_cores": facts["physical_cores"],
+            "omp_threads": facts["threads"], "gflops": round(gflops, 1),
+            "avx2_fma_peak_gflops": peak, "frac_of_avx2_peak": round(gflops / peak, 3) if peak else None}
+
+
+def cpu_reference_measure(warmup, steps, budget_s=150.0):
+    """Warm-up steps (at most 2), then up to `steps` timed steps within about budget_s seconds (at least 3)."""
+    step, facts = cpu_reference_runner()
+    t_warm = None
+    for _ in range(max(1, min(warmup, 2))):
+        _, t_warm = step()
+    timed = max(3, min(steps, int(budget_s / max(t_warm, 1e-3))))
+    rates, times = [], []
+    for _ in range(timed):
+        r, t = step()
+        rates.append(r)
+        times.append(t)
+    return rates, times, facts
 
 
 # ------------------------------------------------------------------------------------------------------ clocks
@@ -218,19 +282,13 @@ def measure_gpu_baselines(ops, stream, dev):
     return rows
 
 
-# ------------------------------------------------------------------------------------------------------ ours
-def run_ours(args, rank, world, local_rank):
+# -------------------------------------------------------------------------------------------- the Q8_0 GEMM sweep
+def measure_gemm_sweep(pkg, dev, stream, steps, no_gpu_baselines=False):
+    """Config 2 on this GPU: value (whole sweep from a CUDA graph), per-launch times and rooflines, GPU baselines and
+    an end-to-end pass through fused_linear with host buffers. Returns the sweep's entry of the JSON line."""
     import torch
-    import torch.distributed as dist
-    import __graft_entry__
-
-    pkg = __graft_entry__.load_package()
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     hbm_peak, tc_peak, peak_kind = peaks()
-
-    # Operands: one weight matrix and one activation batch per GEMM, resident in HBM.
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    g = torch.Generator(device=dev).manual_seed(1000)
     ops = []
     for (m, k, n) in shapes():
         w = torch.randn((n, k), device=dev, generator=g) * 0.02
@@ -243,71 +301,42 @@ def run_ours(args, rank, world, local_rank):
         ops.append(dict(m=m, k=k, n=n, packed=packed, tiles=tiles, x=x, bias=bias, y=y,
                         bias_bf16=bias.to(torch.bfloat16)))
     step_flops = sum(flops(o["m"], o["k"], o["n"]) for o in ops)
-    stream = torch.cuda.Stream(device=dev)
 
     def launch_step():
         for o in ops:
             pkg.gemm_into(o["y"], o["x"], o["tiles"], o["bias"], o["n"], o["k"])
 
     with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 1)):
+        for _ in range(3):
             launch_step()
     stream.synchronize()
-    assert pkg._capi.device_status(local_rank) == 0
-
-    # Region A (value): a CUDA graph of G whole steps, replayed; timed by events outside the graph.
-    G = min(10, args.steps)
+    # The whole sweep: a CUDA graph of G steps replayed steps // G times between CUDA events.
+    G = 10
+    steps = max(G, steps - steps % G)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
             for _ in range(G):
                 launch_step()
-    rest = args.steps % G
-    graph_rest = None
-    if rest:
-        graph_rest = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(graph_rest, stream=stream):
-                for _ in range(rest):
-                    launch_step()
-    with torch.cuda.stream(stream):
-        graph.replay()  # warm the graph itself (not timed)
+        graph.replay()
     stream.synchronize()
-    assert pkg._capi.device_status(local_rank) == 0
-
-    clocks = ClockSampler([local_rank] if world == 1 else list(range(world)))
-    if rank == 0:
-        clocks.start()
-        time.sleep(0.5)
-    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    wall0 = time.time()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        t_begin.record(stream)
-        for _ in range(args.steps // G):
+        t0.record(stream)
+        for _ in range(steps // G):
             graph.replay()
-        if graph_rest is not None:
-            graph_rest.replay()
-        t_end.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    wall1 = time.time()
-    ms = t_begin.elapsed_time(t_end)
-    status = pkg._capi.device_status(local_rank)
+        t1.record(stream)
+    stream.synchronize()
+    ms = t0.elapsed_time(t1)
+    del graph
 
-    # Region B (per-launch durations for the roofline): per shape, a graph of R back-to-back launches over R distinct
-    # copies of its operands (R copies total > 256 MB, so each launch reads its operands from HBM), timed by events.
-    mean_ms = []
-    reps = []
+    # Per-launch durations: per shape, a graph of R back-to-back launches over R distinct copies of its operands
+    # (R copies total > 256 MB, so each launch reads its operands from HBM), timed by events.
+    mean_ms, reps = [], []
     for o in ops:
         per_copy = o["tiles"].numel() + o["x"].numel() * 2
         R = int(min(32, max(2, -(-256e6 // per_copy))))
-        copies = []
-        for _ in range(R):
-            copies.append((o["tiles"].clone(), o["x"].clone(), torch.empty_like(o["y"])))
+        copies = [(o["tiles"].clone(), o["x"].clone(), torch.empty_like(o["y"])) for _ in range(R)]
         gs = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             for (t_, x_, y_) in copies[:1]:
@@ -328,32 +357,24 @@ def run_ours(args, rank, world, local_rank):
         reps.append(R)
         del copies, gs
     torch.cuda.empty_cache()
+    base_us = None if no_gpu_baselines else measure_gpu_baselines(ops, stream, dev)
 
-    # GPU baselines on the same device (not part of the timed step): the reference's unfused PackedLinear path and
-    # cuBLAS on dense bf16 weights, per shape.
-    base_us = measure_gpu_baselines(ops, stream, dev) if not args.no_gpu_baselines else None
-
-    # e2e through the drop-in API with host buffers
+    # End to end through the drop-in API with host buffers; the independent ops' copies are pipelined with their
+    # compute over three streams (PCIe is full duplex).
     host_x = [o["x"].cpu().pin_memory() for o in ops]
     host_y = [torch.empty(o["y"].shape, dtype=o["y"].dtype).pin_memory() for o in ops]
     dev_x = [torch.empty_like(o["x"]) for o in ops]
-    e2e_steps = max(1, min(args.steps, 10))
+    e2e_steps = 10
     fused = pkg.fused_linear
     with torch.cuda.stream(stream):
-        for i, o in enumerate(ops):  # warm: builds the tiled copies fused_linear caches
+        for o in ops:  # builds the tiled copies fused_linear caches
             fused(o["x"], o["packed"], (o["n"], o["k"]), 8, o["bias_bf16"])
     stream.synchronize()
-    # The ops are independent, so the copies are pipelined as a user streaming them would: the host->device copy of
-    # op i+1 runs on one stream and the device->host copy of op i-1 on another while op i computes (PCIe is full
-    # duplex). Events order each op's copy-in -> compute -> copy-out; an op's device input is rewritten only after its
-    # previous compute finished. The timed region spans every copy of every step.
     copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     ev_in = [torch.cuda.Event() for _ in ops]
     ev_comp = [torch.cuda.Event() for _ in ops]
     outs = [None] * len(ops)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     copy_in.wait_event(e0)
@@ -381,32 +402,7 @@ def run_ours(args, rank, world, local_rank):
     h2d = sum(t.numel() * t.element_size() for t in host_x)
     d2h = sum(t.numel() * t.element_size() for t in host_y)
 
-    # Config 3 (denoiser-block steps) and config 4 (Gaussian MLP) on this GPU's own data (shard by request).
-    block_steps = max(3, min(args.steps, 30))
-    block_ms = measure_block(pkg, dev, stream, block_steps, world)
-    mlp_steps = max(3, min(args.steps, 30))
-    mlp_ms = measure_mlp(pkg, dev, stream, mlp_steps, world)
-    gs_steps = max(3, min(args.steps, 20))
-    gs_ms = measure_gs_block(pkg, dev, stream, gs_steps, world)
-    dec_steps = max(3, min(args.steps, 5))
-    dec_ms = measure_gs_decoder(pkg, dev, stream, dec_steps, world)
-    full_steps = 3
-    full_ms = measure_decode(pkg, dev, stream, full_steps, world)
-    status = max(status, pkg._capi.device_status(local_rank))
-
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(status), block_ms, mlp_ms, gs_ms, dec_ms, full_ms], device=dev,
-                         dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, status, block_ms, mlp_ms = float(t[0]), float(t[1]), int(t[2]), float(t[3]), float(t[4])
-        gs_ms, dec_ms, full_ms = float(t[5]), float(t[6]), float(t[7])
-    clk = clocks.stop(wall0, wall1) if rank == 0 else None
-    if rank != 0:
-        return
-
-    value = step_flops * args.steps * world / (ms / 1e3) / 1e12
-    e2e_value = step_flops * e2e_steps * world / (e2e_ms / 1e3) / 1e12
-    shape_rows = []
+    rows = []
     for i, o in enumerate(ops):
         t = mean_ms[i] / 1e3
         tf = flops(o["m"], o["k"], o["n"]) / t / 1e12
@@ -417,81 +413,42 @@ def run_ours(args, rank, world, local_rank):
         if base_us is not None:
             row["us_unfused"] = round(base_us[i]["unfused"], 2)
             row["us_cublas_dense"] = round(base_us[i]["cublas"], 2)
-        shape_rows.append(row)
+        rows.append(row)
     big = [i for i, o in enumerate(ops) if o["m"] >= 4096]
     small = [i for i, o in enumerate(ops) if o["m"] <= 16]
-    ach_t = sum(flops(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in big) / (sum(mean_ms[i] for i in big) / 1e3) / 1e12
+    ach_t = sum(flops(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in big) / (sum(mean_ms[i] for i in big) / 1e3)
     ach_b = sum(alg_bytes(ops[i]["m"], ops[i]["k"], ops[i]["n"]) for i in small) / (
-        sum(mean_ms[i] for i in small) / 1e3) / 1e9
-    traffic = None
+        sum(mean_ms[i] for i in small) / 1e3)
+    out = {
+        "metric": SWEEP_METRIC, "value": round(step_flops * steps / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+        "steps": steps, "ms_per_step": round(ms / steps, 4),
+        "timing": f"CUDA graph of {G} sweeps replayed {steps // G} times between CUDA events; operands resident, each "
+                  f"used once per sweep (a sweep streams "
+                  f"{sum(o['x'].numel() * 2 + o['tiles'].numel() + o['y'].numel() * 2 for o in ops) / 1e9:.2f} GB "
+                  "> 126 MB L2)",
+        "e2e": {"value": round(step_flops * e2e_steps / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "fused_linear(value, packed, shape, 8, bias) on host-pinned inputs; per op H2D copy, compute "
+                       "and D2H copy pipelined over three streams"},
+        "roofline": {"bound": "tensor", "achieved": round(ach_t / 1e12, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(ach_t / 1e12 / tc_peak, 3), "peak_source": f"{peak_kind} bf16 burst",
+                     "launches": "M in {4096, 16384}"},
+        "roofline_small_m": {"bound": "hbm", "achieved": round(ach_b / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
+                             "frac": round(ach_b / 1e9 / hbm_peak, 3), "peak_source": f"{peak_kind} copy",
+                             "launches": "M in {1, 16}"},
+        "shapes": rows,
+        "per_launch_timing": "per shape, a CUDA graph of R launches over R operand copies (> 256 MB in total) "
+                             "replayed 3 times between CUDA events",
+    }
     tfile = ROOT / "profiles" / "q8_gemm_traffic.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch_tensor_bound")
-
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
-        "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
-                   "operands": "resident in HBM", "l2": "each operand used once per step; a step streams "
-                   f"{sum(o['x'].numel() * 2 + o['tiles'].numel() + o['y'].numel() * 2 for o in ops) / 1e9:.2f} GB "
-                   "> 126 MB L2", "timing": f"CUDA graph of {G} steps replayed; CUDA events",
-                   "per_launch_timing": "per shape, a CUDA graph of R launches over R operand copies (> 256 MB in "
-                   "total) replayed 3 times between CUDA events; R per shape in shapes[].copies",
-                   "parallelism": f"replicas x{world} (shard by request, no collective)"},
-        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "fused_linear(value, packed, shape, 8, bias) on host-pinned inputs; per op H2D copy, compute and "
-                       "D2H copy pipelined over three streams (the ops are independent)"},
-        "roofline": {"bound": "tensor", "achieved": round(ach_t, 1), "peak": tc_peak, "unit": "TFLOP/s",
-                     "frac": round(ach_t / tc_peak, 3), "traffic": traffic,
-                     "peak_source": f"{peak_kind} bf16 burst", "launches": "M in {4096, 16384}"},
-        "roofline_small_m": {"bound": "hbm", "achieved": round(ach_b, 1), "peak": hbm_peak, "unit": "GB/s",
-                             "frac": round(ach_b / hbm_peak, 3), "peak_source": f"{peak_kind} copy",
-                             "launches": "M in {1, 16}"},
-        "shapes": shape_rows,
-        "gpu_launches": len(ops) * args.steps,
-        "device_status": status,
-        "clocks": clk,
-        "block": {"metric": "denoiser-block steps/s (config 3: 2 images x 4096 tokens, D 1024, 16 heads x 64, "
-                            "Q8_0 QKV/out/MLP 1024->4096->1024, GELU tanh, fp32 residual)",
-                  "value": round(block_steps * world / (block_ms / 1e3), 2), "unit": "block-steps/s",
-                  "ms_per_step": round(block_ms / block_steps, 3), "steps": block_steps,
-                  "tflops": round(BLOCK_FLOPS * block_steps * world / (block_ms / 1e3) / 1e12, 1),
-                  "frac_tensor": round(BLOCK_FLOPS / (block_ms / block_steps / 1e3) / 1e12 / tc_peak, 3),
-                  "scaling": "weak (each GPU runs its own images; no collective)",
-                  "work": "343.6 GFLOP per step (206.2 linears + 137.4 attention)"},
-        "gaussian_block": {"metric": "Gaussian-decoder block steps/s (src/decoders.cpp:296-313: 8192 anchors, "
-                                     "self-attention, cross-attention to 8192 latent tokens x 16 conditions, MLP "
-                                     "1024->4096->1024, D 1024, 16 heads, fp32 residual)",
-                           "value": round(gs_steps * world / (gs_ms / 1e3), 2), "unit": "block-steps/s",
-                           "ms_per_step": round(gs_ms / gs_steps, 3), "steps": gs_steps,
-                           "tflops": round(GS_FLOPS * gs_steps * world / (gs_ms / 1e3) / 1e12, 1),
-                           "work": f"{GS_FLOPS / 1e9:.1f} GFLOP per step"},
-        "gaussian_decoder": {"metric": "Gaussian decodes/s (Decoders::gaussian_features + to_gaussians: 8192 "
-                                       "anchors -> 262,144 Gaussians, 16 blocks, 8192 latent tokens x 16, D 1024)",
-                             "value": round(dec_steps * world / (dec_ms / 1e3), 3), "unit": "decodes/s",
-                             "ms_per_step": round(dec_ms / dec_steps, 3), "steps": dec_steps,
-                             "gaussians_per_s": round(GS_ANCHORS * 32 * dec_steps * world / (dec_ms / 1e3), 0),
-                             "tflops": round(GS_FLOPS * GS_BLOCKS * dec_steps * world / (dec_ms / 1e3) / 1e12, 1)},
-        "decode": {"metric": "Decoders::decode calls/s (latent 8192 x 16 -> sample_anchors to level 7 through the "
-                             "octree decoder, 4 blocks -> Gaussian decoder, 16 blocks -> 262,144 activated Gaussians; "
-                             "D 1024)", "value": round(full_steps * world / (full_ms / 1e3), 3), "unit": "decodes/s",
-                   "ms_per_step": round(full_ms / full_steps, 2), "steps": full_steps,
-                   "reference_published": "36.99 s on 8 threads and 0.34 s with the upstream GPU modules on an RTX "
-                                          "4090, both octree + Gaussian decoders at 262,144 Gaussians "
-                                          "(docs/data/decoder-cpu-vs-gpu.json); context only, other hardware"},
-        "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
-                                   "heads)", "value": round(MLP_POINTS * mlp_steps * world / (mlp_ms / 1e3), 0),
-                         "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
-                         "tflops": round(MLP_FLOPS * mlp_steps * world / (mlp_ms / 1e3) / 1e12, 1)},
-    }
+        out["roofline"]["traffic"] = json.loads(tfile.read_text()).get("bytes_per_launch_tensor_bound")
     if base_us is not None:
         sweep_unfused = sum(r["unfused"] for r in base_us) / 1e6
         sweep_cublas = sum(r["cublas"] for r in base_us) / 1e6
-        sweep_ours = sum(mean_ms) / 1e3
-        line["gpu_baselines"] = {
-            "unit": UNIT, "timing": "per shape, R operand copies in one CUDA graph, CUDA events (as shapes[].us)",
-            "sweep_ours": round(step_flops / sweep_ours / 1e12, 1),
+        out["gpu_baselines"] = {
+            "unit": "TFLOP/s", "timing": "per shape, R operand copies in one CUDA graph, CUDA events (as shapes[].us)",
+            "sweep_ours": round(step_flops / (sum(mean_ms) / 1e3) / 1e12, 1),
             "packedlinear_unfused": {
                 "value": round(step_flops / sweep_unfused / 1e12, 1),
                 "what": "the reference's GPU path without the fused kernel (tools/idol_packed.py:71-79): dequantize "
@@ -500,10 +457,298 @@ def run_ours(args, rank, world, local_rank):
                 "value": round(step_flops / sweep_cublas / 1e12, 1),
                 "what": "F.linear (cuBLAS) on bf16 weights dequantized beforehand: 2 bytes per weight instead of "
                         "1.0625, no dequantization in the call"}}
+    del ops
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------------------------------- config 5, the stack
+def make_stack(dev, blocks=STACK_BLOCKS, seed=4242):
+    """The 24-block denoiser stack with seeded random Q8_0 weights (the same on every rank: replicas)."""
+    import torch
+    from idol_b200.block import DenoiserBlock, DenoiserStack, Q8Weight
+    g = torch.Generator(device=dev).manual_seed(seed)
+    D, H = BLOCK_D, BLOCK_H
+    out = []
+    for _ in range(blocks):
+        w = {}
+        for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "ff1": (H, D), "ff2": (D, H)}.items():
+            w[name] = Q8Weight.from_float(torch.randn((n, k), device=dev, generator=g) * 0.02,
+                                          torch.randn(n, device=dev, generator=g) * 0.01)
+        out.append(DenoiserBlock(w["qkv"], w["out"], w["ff1"], w["ff2"], 1 + 0.1 * torch.randn(D, device=dev, generator=g),
+                                 1 + 0.1 * torch.randn(D, device=dev, generator=g), BLOCK_HEADS))
+    return DenoiserStack(out)
+
+
+def make_images(dev, first, count):
+    """The residual streams of images first .. first + count - 1: [count * 2 * 4096, D] fp32, image i drawn from its
+    own seed, so the union over ranks is the same 64 images for every N."""
+    import torch
+    x = torch.empty((count * CFG * BLOCK_TOKENS, BLOCK_D), device=dev)
+    for j in range(count):
+        g = torch.Generator(device=dev).manual_seed(9000 + first + j)
+        x[j * CFG * BLOCK_TOKENS:(j + 1) * CFG * BLOCK_TOKENS] = torch.randn(
+            (CFG * BLOCK_TOKENS, BLOCK_D), device=dev, generator=g).to(torch.bfloat16).float()
+    return x
+
+
+def block_kernel_times(block, dev, stream, seqs):
+    """Each kernel of one DenoiserBlock.forward_ timed alone on that call's own shapes (seqs sequences of 4096 tokens):
+    per kernel, a CUDA graph of R launches replayed 3 times between CUDA events. Returns rows with the launches per
+    block, mean microseconds per launch and the algorithmic FLOPs (or bytes) per launch."""
+    import torch
+    from idol_b200 import _capi as C
+    from idol_b200 import layers
+    rows, D, H = seqs * BLOCK_TOKENS, BLOCK_D, BLOCK_H
+    qkv_w, out_w, ff1_w, ff2_w = block.weights
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn((rows, D), device=dev, generator=g)
+    h = torch.randn((rows, D), device=dev, generator=g).to(torch.bfloat16)
+    qkv = torch.empty((rows, 3 * D), device=dev, dtype=torch.bfloat16)
+    f1 = torch.empty((rows, H), device=dev, dtype=torch.bfloat16)
+    att = torch.empty((rows, D), device=dev, dtype=torch.bfloat16)
+    qkv_w(h, out=qkv)
+    layers.rms_heads_(qkv[:, :D], BLOCK_HEADS, block.q_gamma)
+    layers.rms_heads_(qkv[:, D:2 * D], BLOCK_HEADS, block.k_gamma)
+    ff1_w(h, act=C.ACT_GELU_TANH, out=f1)
+    kernels = [
+        ("norm_rows (fp32 -> bf16)", 2, lambda: layers.norm_rows(x, 1e-6, out=h), "hbm", rows * D * (4 + 2)),
+        ("q8_gemm qkv 1024->3072", 1, lambda: qkv_w(h, out=qkv), "tensor", 2.0 * rows * 3 * D * D),
+        ("rms_heads (q or k)", 2, lambda: layers.rms_heads_(qkv[:, :D], BLOCK_HEADS, block.q_gamma), "hbm",
+         rows * D * 2 * 2),
+        ("attention", 1, lambda: layers.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], BLOCK_HEADS,
+                                                  batch=seqs, out=att), "tensor",
+         4.0 * BLOCK_TOKENS ** 2 * D * seqs),
+        ("q8_gemm out 1024->1024 + residual", 1, lambda: out_w(att, residual=x, out=x), "tensor", 2.0 * rows * D * D),
+        ("q8_gemm ff1 1024->4096 gelu", 1, lambda: ff1_w(h, act=C.ACT_GELU_TANH, out=f1), "tensor",
+         2.0 * rows * H * D),
+        ("q8_gemm ff2 4096->1024 + residual", 1, lambda: ff2_w(f1, residual=x, out=x), "tensor", 2.0 * rows * D * H),
+    ]
+    R = 10
+    res = []
+    for name, per_block, fn, bound, work in kernels:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()
+            with torch.cuda.graph(gr, stream=stream):
+                for _ in range(R):
+                    fn()
+            gr.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(3):
+                gr.replay()
+            e1.record(stream)
+        stream.synchronize()
+        res.append((name, per_block, e0.elapsed_time(e1) * 1e3 / (3 * R), bound, work))
+        del gr
+    return res
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+    from idol_b200.shard import image_shard
+
+    pkg = __graft_entry__.load_package()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm_peak, tc_peak, peak_kind = peaks()
+    stream = torch.cuda.Stream(device=dev)
+
+    first, count = image_shard(STACK_IMAGES, rank, world)
+    seqs, chunk = count * CFG, CHUNK_IMAGES * CFG
+    stack = make_stack(dev)
+    x = make_images(dev, first, count)
+    host_x = x.cpu().pin_memory()  # the same images, for the end-to-end pass
+    torch.cuda.synchronize()
+
+    def step():
+        stack.forward_(x, seqs, chunk)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    status = pkg._capi.device_status(local_rank)
+
+    clocks = ClockSampler([local_rank] if world == 1 else list(range(world)))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.5)
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        t_begin.record(stream)
+        for _ in range(args.steps):
+            step()
+        t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    wall1 = time.time()
+    ms = t_begin.elapsed_time(t_end)
+    clk = clocks.stop(wall0, wall1) if rank == 0 else None
+    status = max(status, pkg._capi.device_status(local_rank))
+
+    # End to end: the rank's images start and end in pinned host memory. Chunks of CHUNK_IMAGES images go through a
+    # ring of three device buffers: host->device on one stream, the 24 blocks on the compute stream, device->host on a
+    # third, so one chunk's copies overlap its neighbours' compute.
+    host_y = torch.empty(host_x.shape, dtype=host_x.dtype, pin_memory=True)
+    rows_chunk = chunk * BLOCK_TOKENS
+    nchunks = -(-seqs // chunk)
+    ring = [torch.empty((rows_chunk, BLOCK_D), device=dev) for _ in range(min(3, nchunks))]
+    copy_in, copy_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in ring]
+    ev_done = [torch.cuda.Event() for _ in ring]
+    ev_out = [torch.cuda.Event() for _ in ring]
+    used = [False] * len(ring)
+    e2e_steps = max(1, min(args.steps, 3))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    copy_in.wait_event(e0)
+    copy_out.wait_event(e0)
+    for _ in range(e2e_steps):
+        for c in range(nchunks):
+            b = c % len(ring)
+            r0 = c * rows_chunk
+            r1 = min(seqs * BLOCK_TOKENS, r0 + rows_chunk)
+            buf = ring[b][:r1 - r0]
+            with torch.cuda.stream(copy_in):
+                if used[b]:
+                    copy_in.wait_event(ev_out[b])
+                buf.copy_(host_x[r0:r1], non_blocking=True)
+                ev_in[b].record(copy_in)
+            with torch.cuda.stream(stream):
+                stream.wait_event(ev_in[b])
+                stack.forward_(buf, (r1 - r0) // BLOCK_TOKENS, chunk)
+                ev_done[b].record(stream)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(ev_done[b])
+                host_y[r0:r1].copy_(buf, non_blocking=True)
+                ev_out[b].record(copy_out)
+            used[b] = True
+    stream.wait_stream(copy_out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    io_bytes = host_x.numel() * host_x.element_size()
+    status = max(status, pkg._capi.device_status(local_rank))
+
+    # Every kernel of a block on a chunk's shapes, timed alone (for the roofline of the dominant one).
+    kern = block_kernel_times(stack.blocks[0], dev, stream, chunk)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, float(status)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, status = float(t[0]), float(t[1]), int(t[2])
+    if rank != 0:
+        return
+
+    units = STACK_BLOCKS * STACK_IMAGES
+    kernels, block_us = [], sum(us * n for (_, n, us, _, _) in kern)
+    for name, per_block, us, bound, work in kern:
+        if bound == "tensor":
+            ach, peak, unit = work / (us / 1e6) / 1e12, tc_peak, "TFLOP/s"
+        else:
+            ach, peak, unit = work / (us / 1e6) / 1e9, hbm_peak, "GB/s"
+        kernels.append({"kernel": name, "launches_per_block": per_block, "us": round(us, 2),
+                        "share": round(us * per_block / block_us, 3), "bound": bound, "achieved": round(ach, 1),
+                        "unit": unit, "peak": peak, "frac": round(ach / peak, 3),
+                        ("flops" if bound == "tensor" else "bytes"): work})
+    top = max(kernels, key=lambda k: k["share"])
+    line = {
+        "metric": METRIC, "value": round(units * args.steps / (ms / 1e3), 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded normal residual streams, Q8_0 of seeded normal weights)",
+        "config": config5(world),
+        "images_per_s": round(STACK_IMAGES * args.steps / (ms / 1e3), 3),
+        "tflops": round(units * BLOCK_FLOPS * args.steps / (ms / 1e3) / 1e12, 1),
+        "e2e": {"value": round(units * e2e_steps / (e2e_ms / 1e3), 2), "unit": UNIT,
+                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes, "steps": e2e_steps,
+                "api": "DenoiserStack.forward_ per chunk of 2 images from pinned host memory; H2D, compute and D2H "
+                       "on three streams"},
+        "roofline": {"bound": top["bound"], "kernel": top["kernel"], "achieved": top["achieved"],
+                     "peak": top["peak"], "unit": top["unit"], "frac": top["frac"],
+                     "peak_source": f"{peak_kind} {'bf16 burst' if top['bound'] == 'tensor' else 'copy'}",
+                     "traffic": traffic_for(top["kernel"]),
+                     "work_per_launch": f"{top.get('flops', top.get('bytes')):.4g} "
+                                        f"{'FLOP' if top['bound'] == 'tensor' else 'bytes'} "
+                                        f"({chunk} sequences x {BLOCK_TOKENS} tokens)"},
+        "kernels": kernels,
+        "block_us_sum_of_kernels": round(block_us, 1),
+        "block_us_in_stack": round(ms * 1e3 / args.steps / (STACK_BLOCKS * nchunks), 1),
+        "gpu_launches": LAUNCHES_PER_BLOCK * STACK_BLOCKS * nchunks * args.steps,
+        "device_status": status,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_extras:
+        line["gemm_sweep"] = measure_gemm_sweep(pkg, dev, stream, args.sweep_steps, args.no_gpu_baselines)
+        line.update(measure_compositions(pkg, dev, stream, args))
     if world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, sample = cpu_reference_sample()
-        line["cpu_baseline"] = {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample}
+        rates, times, facts = cpu_reference_measure(1, 10, budget_s=20.0)
+        line["cpu_baseline"] = cpu_baseline_entry(rates, times, facts)
     print(json.dumps(line), flush=True)
+
+
+def traffic_for(kernel):
+    """DRAM bytes per launch of a kernel from the committed ncu record, or None."""
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    return json.loads(f.read_text()).get(kernel, {}).get("bytes_per_launch")
+
+
+def measure_compositions(pkg, dev, stream, args):
+    """Config 3 (one block), config 4 (Gaussian MLP) and the decoders at the real model's size, on this GPU."""
+    block_steps = mlp_steps = 30
+    gs_steps, dec_steps, full_steps = 20, 5, 3
+    block_ms = measure_block(pkg, dev, stream, block_steps, 1)
+    mlp_ms = measure_mlp(pkg, dev, stream, mlp_steps, 1)
+    gs_ms = measure_gs_block(pkg, dev, stream, gs_steps, 1)
+    dec_ms = measure_gs_decoder(pkg, dev, stream, dec_steps, 1)
+    full_ms = measure_decode(pkg, dev, stream, full_steps, 1)
+    _, tc_peak, _ = peaks()
+    return {
+        "block": {"metric": "denoiser-block steps/s (config 3: 2 CFG branches x 4096 tokens, D 1024, 16 heads x 64, "
+                            "Q8_0 QKV/out/MLP 1024->4096->1024, GELU tanh, fp32 residual)",
+                  "value": round(block_steps / (block_ms / 1e3), 2), "unit": "block-steps/s",
+                  "ms_per_step": round(block_ms / block_steps, 3), "steps": block_steps,
+                  "tflops": round(BLOCK_FLOPS * block_steps / (block_ms / 1e3) / 1e12, 1),
+                  "frac_tensor": round(BLOCK_FLOPS / (block_ms / block_steps / 1e3) / 1e12 / tc_peak, 3)},
+        "gaussian_block": {"metric": "Gaussian-decoder block steps/s (src/decoders.cpp:296-313: 8192 anchors, "
+                                     "self-attention, cross-attention to 8192 latent tokens x 16 conditions, MLP "
+                                     "1024->4096->1024, D 1024, 16 heads, fp32 residual)",
+                           "value": round(gs_steps / (gs_ms / 1e3), 2), "unit": "block-steps/s",
+                           "ms_per_step": round(gs_ms / gs_steps, 3), "steps": gs_steps,
+                           "tflops": round(GS_FLOPS * gs_steps / (gs_ms / 1e3) / 1e12, 1)},
+        "gaussian_decoder": {"metric": "Gaussian decodes/s (Decoders::gaussian_features + to_gaussians: 8192 "
+                                       "anchors -> 262,144 Gaussians, 16 blocks, 8192 latent tokens x 16, D 1024)",
+                             "value": round(dec_steps / (dec_ms / 1e3), 3), "unit": "decodes/s",
+                             "ms_per_step": round(dec_ms / dec_steps, 3), "steps": dec_steps,
+                             "tflops": round(GS_FLOPS * GS_BLOCKS * dec_steps / (dec_ms / 1e3) / 1e12, 1)},
+        "decode": {"metric": "Decoders::decode calls/s (latent 8192 x 16 -> sample_anchors to level 7 through the "
+                             "octree decoder, 4 blocks -> Gaussian decoder, 16 blocks -> 262,144 activated Gaussians; "
+                             "D 1024)", "value": round(full_steps / (full_ms / 1e3), 3), "unit": "decodes/s",
+                   "ms_per_step": round(full_ms / full_steps, 2), "steps": full_steps,
+                   "reference_published": "36.99 s on 8 threads and 0.34 s with the upstream GPU modules on an RTX "
+                                          "4090, both octree + Gaussian decoders at 262,144 Gaussians "
+                                          "(docs/data/decoder-cpu-vs-gpu.json); context only, other hardware"},
+        "gaussian_mlp": {"metric": "Gaussian MLP points/s (config 4: 262,144 points, Q8_0 128->512->512->14, SiLU, "
+                                   "heads)", "value": round(MLP_POINTS * mlp_steps / (mlp_ms / 1e3), 0),
+                         "unit": "points/s", "ms_per_step": round(mlp_ms / mlp_steps, 3), "steps": mlp_steps,
+                         "tflops": round(MLP_FLOPS * mlp_steps / (mlp_ms / 1e3) / 1e12, 1)},
+    }
 
 
 def run_profile_shape(args):
@@ -542,9 +787,6 @@ def run_profile_shape(args):
                       "tflops": round(flops(m, k, n) / us / 1e6, 1), "device_status": pkg._capi.device_status(0)}))
 
 
-BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4096
-BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
-               + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
 GS_ANCHORS, GS_LATENTS, GS_COND, GS_BLOCKS, OCT_BLOCKS, DECODE_LEVEL = 8192, 8192, 16, 16, 4, 7
 GS_FLOPS = (2.0 * GS_ANCHORS * (3 + 1 + 1 + 1 + 2 * BLOCK_H // BLOCK_D) * BLOCK_D * BLOCK_D
             + 4.0 * GS_ANCHORS * GS_ANCHORS * BLOCK_D + 4.0 * GS_ANCHORS * GS_LATENTS * BLOCK_D
@@ -720,28 +962,20 @@ def measure_mlp(pkg, dev, stream, steps, world):
     return _graph_ms(torch, stream, lambda: mlp(x), steps, world)
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, world):
+    """The reference arm: the block composed of the reference's own CPU functions on one image per step, on every
+    usable host thread; rank 0 alone runs and prints (the other ranks exit without work)."""
     if rank != 0:
         return
-    # Each step is a bounded sample (at least one pass of the capped sweep); the whole run stays within a few minutes
-    # however many steps are asked for.
-    seconds_per_step = min(2.0, 150.0 / max(1, args.steps))
-    sample = cpu_reference_runner()
-    vals = []
-    for _ in range(args.warmup):
-        sample(0.0)
-    for _ in range(args.steps):
-        v, cores, kind, text = sample(seconds_per_step)
-        vals.append(v)
-    v = statistics.median(vals)
+    rates, times, facts = cpu_reference_measure(args.warmup, args.steps)
+    v = statistics.median(rates)
+    base = cpu_baseline_entry(rates, times, facts)
     print(json.dumps({
         "metric": METRIC, "value": round(v, 4), "unit": UNIT, "impl": "reference", "n_gpus": 0, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded normal activations, Q8_0 of normal weights)",
-        "config": {"workload": "config2_q8_0_gemm_sweep", "M": list(MS), "KN": [list(kn) for kn in KNS],
-                   "sample": f"M capped at 256 rows per shape, {seconds_per_step:.2f} s (at least one pass) of CPU "
-                             "work per step"},
-        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": text},
+        "warmup": args.warmup, "ms_per_step": round(statistics.median(times) * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded normal residual streams, Q8_0 of seeded normal weights)",
+        "config": config5(world), "cpu_baseline": base,
         "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -749,11 +983,13 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--sweep-steps", type=int, default=200, help="timed sweeps of the config-2 GEMM sweep (N = 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpu-baselines", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="only the config-5 stack (no sweep or compositions)")
     ap.add_argument("--profile-shape", default=None,
                     help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture; 'block' or 'mlp' "
                          "runs the config-3 block or the config-4 MLP instead")
@@ -764,7 +1000,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if args.profile_shape:
         run_profile_shape(args)

@@ -6,6 +6,8 @@
                      res (src/decoders.cpp:296-313 without the cross-attention), in place on the residual stream.
 * ``GaussianBlock`` - the Gaussian decoder's block (src/decoders.cpp:296-313): the same plus a cross-attention to
                      the latent tokens between the self-attention and the MLP.
+* ``DenoiserStack`` - config 5: a stack of DenoiserBlocks run over many independent images, a chunk of images at
+                     a time through every block, with one workspace shared by the blocks.
 * ``GaussianMLP``  - scope row A15: 128 -> 512 (SiLU) -> 512 (SiLU) -> 14 -> activated heads.
 
 Workspaces are device tensors owned by the Python objects and reused across calls.
@@ -110,6 +112,39 @@ class DenoiserBlock:
             except Exception:
                 pass
             self.handle = None
+
+
+class DenoiserStack:
+    """A stack of DenoiserBlocks (the denoiser's 24 transformer blocks, tools/export_full_gguf.py:311-314) over a
+    batch of independent sequences: each image's CFG branches are separate sequences of `tokens` rows that attend only
+    within themselves (batched CFG, tools/idol_generate.py:153,193). forward_ runs `chunk` sequences at a time through
+    every block (so the workspace is sized by the chunk, not the batch) and shares one workspace across the blocks."""
+
+    def __init__(self, blocks: Sequence[DenoiserBlock]):
+        if not blocks:
+            raise ValueError("DenoiserStack: no blocks")
+        self.blocks = tuple(blocks)
+        self.dim, self.device = self.blocks[0].dim, self.blocks[0].device
+        if any(b.dim != self.dim or b.device != self.device for b in self.blocks):
+            raise ValueError("DenoiserStack: blocks of different widths or devices")
+        self.ws = _Workspace()
+
+    def forward_(self, x: torch.Tensor, sequences: int, chunk: Optional[int] = None) -> torch.Tensor:
+        """In place on x: [sequences * tokens, D] (fp32 or bf16, contiguous), `chunk` sequences per pass through the
+        blocks (all of them by default); launches on the current stream."""
+        if not x.is_contiguous() or x.dim() != 2 or x.shape[1] != self.dim or sequences < 1 or x.shape[0] % sequences:
+            raise ValueError("DenoiserStack: x must be a contiguous [sequences * tokens, D] tensor")
+        tokens = x.shape[0] // sequences
+        chunk = sequences if chunk is None else max(1, min(int(chunk), sequences))
+        lib, st = C.lib(), _stream(x.device)
+        ws = self.ws.get(self.blocks[0].workspace_bytes(chunk * tokens), x.device)
+        for s0 in range(0, sequences, chunk):
+            n = min(chunk, sequences - s0)
+            part = x[s0 * tokens:(s0 + n) * tokens]
+            for b in self.blocks:
+                C.check(lib.idol_b200_block_forward(ctypes.c_void_p(b.handle), _ptr(part), _DTYPES[x.dtype], tokens,
+                                                    n, _ptr(ws), ws.numel(), st))
+        return x
 
 
 class GaussianBlock:

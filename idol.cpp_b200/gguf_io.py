@@ -20,6 +20,8 @@ from __future__ import annotations
 
 import hashlib
 import json
+import re
+from collections import Counter
 from pathlib import Path
 from typing import Dict
 
@@ -42,30 +44,55 @@ def _supported(gguf):
     return {t.F32, t.F16, t.Q8_0, t.Q4_0, t.Q2_K, t.Q4_K, t.Q6_K, t.I8, t.I16, t.I32, t.I64}
 
 
+_TENSOR_NAME = re.compile(r"idol\.([^.]+)\.(.+)")
+_CONFIG_KEYS = ("denoiser", "decoder", "decoder_gs", "image_encoders")
+
+
+def _text_field(reader, key):
+    field = reader.get_field(key)
+    return None if field is None else field.contents()
+
+
+def _container_config(reader) -> dict:
+    """Header rule: the architecture is `idol` and an embedded `idol.config.json` carries the configurations of the
+    denoiser, both decoders and the image encoders."""
+    text = _text_field(reader, "idol.config.json")
+    if _text_field(reader, "general.architecture") != "idol" or text is None:
+        raise ValueError("not an Idol GGUF file with an embedded configuration")
+    config = json.loads(text)
+    if set(_CONFIG_KEYS) - set(config):
+        raise ValueError("incomplete Idol configuration")
+    return config
+
+
+def _components(tensors, encodings) -> Dict[str, Dict]:
+    """Tensor rules: every name is `idol.<component>.<layer name>` with one of the four components; no name twice;
+    only the encodings the reference's loader accepts; each component has at least one tensor. Returns
+    component -> {layer name: tensor}."""
+    keyed = [(_TENSOR_NAME.fullmatch(t.name), t) for t in tensors]
+    stray = next((t.name for m, t in keyed if m is None or m.group(1) not in COMPONENTS), None)
+    if stray is not None:
+        raise ValueError("unexpected tensor in Idol GGUF: " + stray)
+    counts = Counter(t.name for _, t in keyed)
+    bad = next((t.name for _, t in keyed if counts[t.name] > 1 or t.tensor_type not in encodings), None)
+    if bad is not None:
+        raise ValueError("duplicate tensor or unsupported GGUF encoding: " + bad)
+    table = {c: {m.group(2): t for m, t in keyed if m.group(1) == c} for c in COMPONENTS}
+    if not all(table.values()):
+        raise ValueError("Idol GGUF is missing a component")
+    return table
+
+
 class IdolGGUF:
+    """An Idol GGUF file opened with gguf-py and checked against the container rules of tools/idol_gguf.py:114-135
+    (same error messages): `config` is the embedded configuration, `tensors[component][layer name]` the tensors."""
+
     def __init__(self, path):
         gguf = _gguf()
         self.path = Path(path)
         self.reader = gguf.GGUFReader(self.path)
-        arch = self.reader.get_field("general.architecture")
-        config = self.reader.get_field("idol.config.json")
-        if arch is None or arch.contents() != "idol" or config is None:
-            raise ValueError("not an Idol GGUF file with an embedded configuration")
-        self.config = json.loads(config.contents())
-        if not all(k in self.config for k in ("denoiser", "decoder", "decoder_gs", "image_encoders")):
-            raise ValueError("incomplete Idol configuration")
-        supported = _supported(gguf)
-        self.tensors: Dict[str, Dict] = {name: {} for name in COMPONENTS}
-        for tensor in self.reader.tensors:
-            parts = tensor.name.split(".", 2)
-            if len(parts) != 3 or parts[0] != "idol" or parts[1] not in self.tensors or not parts[2]:
-                raise ValueError("unexpected tensor in Idol GGUF: " + tensor.name)
-            group = self.tensors[parts[1]]
-            if parts[2] in group or tensor.tensor_type not in supported:
-                raise ValueError("duplicate tensor or unsupported GGUF encoding: " + tensor.name)
-            group[parts[2]] = tensor
-        if any(not values for values in self.tensors.values()):
-            raise ValueError("Idol GGUF is missing a component")
+        self.config = _container_config(self.reader)
+        self.tensors: Dict[str, Dict] = _components(self.reader.tensors, _supported(gguf))
 
     def packed_linears(self, component: str, bias_dtype=torch.float32) -> Dict[str, PackedLinear]:
         """layer name -> PackedLinear for every 2-D Q8_0 / Q4_0 / Q4_K `<layer>.weight` of the component; a scale

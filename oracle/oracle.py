@@ -419,6 +419,42 @@ class RefLinear:
             self.h = None
 
 
+class RefBlock:
+    """The config-3/5 block composed of the reference's own CPU functions as compiled into _ref (test infrastructure:
+    the timed CPU baseline of the denoiser stack, checked against block_forward): norm_rows (src/decoders.cpp:23-42),
+    gemm_packed with the float kernel (src/kernels.cpp:552-565), rms_heads (src/decoders.cpp:74-86), attention
+    (src/kernels.cpp:737-746) and gelu_tanh (src/decoders.cpp:55-71), in the order of src/decoders.cpp:296-313 without
+    the cross-attention. `layers` as for block_forward."""
+
+    def __init__(self, layers, heads, eps=1e-6):
+        self.lin = {n: RefLinear(*layers[n]) for n in ("qkv", "out", "ff1", "ff2")}
+        self.qg, self.kg = c32(layers["q_gamma"]), c32(layers["k_gamma"])
+        self.heads, self.eps = heads, eps
+
+    def forward_(self, x, images=1):
+        """In place on x: [images * L, D] fp32 C-contiguous."""
+        R = ref()
+        rows, D = x.shape
+        hd, L = D // self.heads, rows // images
+        h = np.empty_like(x)
+        R.ref_norm_rows(_ptr(x), _ptr(h), rows, D, self.eps, None, None, None, None)
+        qkv = self.lin["qkv"].gemm(h)
+        R.ref_rms_heads(_ptr(qkv), rows, 3 * D, self.heads, hd, _ptr(self.qg))
+        R.ref_rms_heads(ctypes.cast(qkv.ctypes.data + 4 * D, _f32p), rows, 3 * D, self.heads, hd, _ptr(self.kg))
+        a = np.empty((rows, D), np.float32)
+        for i in range(images):
+            base = qkv.ctypes.data + 4 * i * L * 3 * D
+            R.ref_attention(ctypes.cast(base, _f32p), L, 3 * D, ctypes.cast(base + 4 * D, _f32p),
+                            ctypes.cast(base + 8 * D, _f32p), L, 3 * D, self.heads, hd,
+                            ctypes.cast(a.ctypes.data + 4 * i * L * D, _f32p), D)
+        x[:] = self.lin["out"].gemm(a, residual=x)
+        R.ref_norm_rows(_ptr(x), _ptr(h), rows, D, self.eps, None, None, None, None)
+        f = self.lin["ff1"].gemm(h)
+        R.ref_gelu_tanh(_ptr(f), f.size)
+        x[:] = self.lin["ff2"].gemm(f, residual=x)
+        return x
+
+
 def ref_threads(n=None):
     if n is None:
         n = os.cpu_count() or 1

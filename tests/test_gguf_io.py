@@ -107,3 +107,23 @@ def test_decoder_cache_identity(pkg, tmp_path):
     (cache / "weights.bin").write_bytes(b"\1" * 64)
     with pytest.raises(ValueError, match="does not match"):
         check_decoder_cache(model, cache)
+
+
+def test_container_checks_configuration_and_encodings(pkg, tmp_path):
+    from idol_b200.gguf_io import IdolGGUF
+    t = _model(np.random.default_rng(2))
+    w = gguf.GGUFWriter(str(tmp_path / "f.gguf"), "idol")
+    w.add_string("idol.config.json", json.dumps({"denoiser": {}, "decoder": {}}))
+    for name, (data, kind) in t.items():
+        w.add_tensor(name, data) if kind is None else w.add_tensor(name, data, raw_shape=data.shape, raw_dtype=kind)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pytest.raises(ValueError, match="incomplete Idol configuration"):
+        IdolGGUF(tmp_path / "f.gguf")
+    t2 = dict(t)
+    t2["idol.octree.odd"] = (np.zeros(44, np.uint8), gguf.GGMLQuantizationType.Q5_0)  # an encoding the loader refuses
+    _write(tmp_path / "g.gguf", t2)
+    with pytest.raises(ValueError, match="unsupported GGUF encoding: idol.octree.odd"):
+        IdolGGUF(tmp_path / "g.gguf")

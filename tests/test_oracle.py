@@ -113,3 +113,23 @@ def test_gaussian_heads(oracle):
     np.testing.assert_allclose(out[:, 6:10], r / np.linalg.norm(r, axis=1, keepdims=True), rtol=1e-5, atol=1e-6)
     np.testing.assert_array_equal(out[0, 6:10], [1, 0, 0, 0])
     np.testing.assert_allclose(out[:, 10:], 1 / (1 + np.exp(-raw[:, 10:])), rtol=1e-6)
+
+
+def test_reference_composed_block_matches_the_oracle_block(oracle):
+    """The denoiser block composed of the reference's own compiled functions (the CPU baseline of the stack) against
+    the oracle's restatement of the same composition."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref not built (no reference checkout)")
+    rng = np.random.default_rng(21)
+    D, heads, H, images, L = 256, 4, 1024, 2, 48
+    layers = {}
+    for name, (n, k) in {"qkv": (3 * D, D), "out": (D, D), "ff1": (H, D), "ff2": (D, H)}.items():
+        layers[name] = (oracle.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32)),
+                        rng.normal(0, 0.01, n).astype(np.float32), n, k)
+    layers["q_gamma"] = rng.normal(1, 0.1, D).astype(np.float32)
+    layers["k_gamma"] = rng.normal(1, 0.1, D).astype(np.float32)
+    x = rng.normal(0, 1, (images * L, D)).astype(np.float32)
+    want = oracle.block_forward(x, layers, heads, images=images)
+    got = oracle.RefBlock(layers, heads).forward_(x.copy(), images=images)
+    rms = np.sqrt((want.astype(np.float64) ** 2).mean())
+    assert np.abs(got - want).max() <= 1e-5 * rms
