@@ -52,7 +52,7 @@ BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOC
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
 STACK_BLOCKS, STACK_IMAGES, CFG = 24, 64, 2
 CHUNK_IMAGES = 2  # images per pass through the blocks (4 sequences, 32768 rows)
-LAUNCHES_PER_BLOCK = 9  # norm, qkv, rms q, rms k, attention, out + residual, norm, ff1, ff2 + residual
+LAUNCHES_PER_BLOCK = 8  # norm, qkv, rms_heads of q and k, attention, out + residual, norm, ff1, ff2 + residual
 METRIC = "denoiser-block steps/s (config 5: 24-block stack over 64 images x 2 CFG branches, sharded by image)"
 UNIT = "block-steps/s"
 
@@ -240,12 +240,31 @@ def dequantize_q8_torch(packed, n, k, dtype):
     return (codes * scale).reshape(n, k).to(dtype)
 
 
+def reference_triton():
+    """The reference's own fused GPU linear (tools/idol_triton.py fused_linear, Triton), staged into baseline/_ref/ by
+    __graft_entry__.build(); None when it is not there or Triton cannot load it."""
+    path = ROOT / "baseline" / "_ref" / "idol_triton.py"
+    if not path.exists():
+        return None
+    try:
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("reference_idol_triton", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod.fused_linear
+    except Exception:
+        return None
+
+
 def measure_gpu_baselines(ops, stream, dev):
     """Per sweep shape, CUDA-event time of (a) the reference's unfused PackedLinear.forward on the GPU (dequantize the
-    GGUF bytes to bf16, then F.linear = cuBLAS) and (b) cuBLAS alone on weights dequantized beforehand, each over R
-    operand copies in one CUDA graph (as the per-launch timing of the fused kernel). Returns per-shape microseconds."""
+    GGUF bytes to bf16, then F.linear = cuBLAS), (b) cuBLAS alone on weights dequantized beforehand, (c) the
+    reference's fused Triton linear (tools/idol_triton.py:94-126) in bf16 and, where its dense branch applies
+    (fp16, M >= 4096), in fp16; each over R operand copies in one CUDA graph, as the fused kernel's per-launch
+    timing. Returns per-shape microseconds (None where a path does not apply or did not run)."""
     import torch
     import torch.nn.functional as F
+    triton_linear = reference_triton()
     rows = []
     for o in ops:
         m, k, n = o["m"], o["k"], o["n"]
@@ -254,30 +273,43 @@ def measure_gpu_baselines(ops, stream, dev):
         xs = [o["x"].clone() for _ in range(R)]
         packs = [o["packed"].clone() for _ in range(R)]
         dense = [dequantize_q8_torch(pk, n, k, torch.bfloat16) for pk in packs]
-        res = {}
-        for name in ("unfused", "cublas"):
-            def run():
-                for r in range(R):
-                    w = dense[r] if name == "cublas" else dequantize_q8_torch(packs[r], n, k, torch.bfloat16)
-                    F.linear(xs[r], w, o["bias_bf16"])
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(stream):
-                run()
-                with torch.cuda.graph(g, stream=stream):
-                    run()
-                g.replay()
-            stream.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                e0.record(stream)
-                for _ in range(3):
+        xs16 = [x.to(torch.float16) for x in xs] if m >= 4096 else None
+        b16 = o["bias"].to(torch.float16)
+        variants = {"unfused": lambda r: F.linear(xs[r], dequantize_q8_torch(packs[r], n, k, torch.bfloat16),
+                                                  o["bias_bf16"]),
+                    "cublas": lambda r: F.linear(xs[r], dense[r], o["bias_bf16"])}
+        if triton_linear is not None:
+            variants["triton"] = lambda r: triton_linear(xs[r], packs[r], (n, k), 8, o["bias_bf16"])
+            if xs16 is not None:
+                variants["triton_fp16"] = lambda r: triton_linear(xs16[r], packs[r], (n, k), 8, b16)
+        res = {"triton": None, "triton_fp16": None}
+        for name, fn in variants.items():
+            try:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(stream):
+                    for r in range(R):
+                        fn(r)
+                    with torch.cuda.graph(g, stream=stream):
+                        for r in range(R):
+                            fn(r)
                     g.replay()
-                e1.record(stream)
-            stream.synchronize()
-            res[name] = e0.elapsed_time(e1) * 1e3 / (3 * R)
-            del g
+                stream.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    e0.record(stream)
+                    for _ in range(3):
+                        g.replay()
+                    e1.record(stream)
+                stream.synchronize()
+                res[name] = e0.elapsed_time(e1) * 1e3 / (3 * R)
+                del g
+            except Exception as exc:  # a baseline that cannot run is reported as absent, not as a failure
+                if name in ("unfused", "cublas"):
+                    raise
+                res[name] = None
+                res.setdefault("error", f"{type(exc).__name__}: {str(exc)[:120]}")
         rows.append(res)
-        del xs, packs, dense
+        del xs, packs, dense, xs16
         torch.cuda.empty_cache()
     return rows
 
@@ -413,6 +445,9 @@ def measure_gemm_sweep(pkg, dev, stream, steps, no_gpu_baselines=False):
         if base_us is not None:
             row["us_unfused"] = round(base_us[i]["unfused"], 2)
             row["us_cublas_dense"] = round(base_us[i]["cublas"], 2)
+            for key in ("triton", "triton_fp16"):
+                if base_us[i].get(key) is not None:
+                    row[f"us_reference_{key}"] = round(base_us[i][key], 2)
         rows.append(row)
     big = [i for i, o in enumerate(ops) if o["m"] >= 4096]
     small = [i for i, o in enumerate(ops) if o["m"] <= 16]
@@ -457,6 +492,15 @@ def measure_gemm_sweep(pkg, dev, stream, steps, no_gpu_baselines=False):
                 "value": round(step_flops / sweep_cublas / 1e12, 1),
                 "what": "F.linear (cuBLAS) on bf16 weights dequantized beforehand: 2 bytes per weight instead of "
                         "1.0625, no dequantization in the call"}}
+        if all(r.get("triton") is not None for r in base_us):
+            out["gpu_baselines"]["reference_triton_fused_linear"] = {
+                "value": round(step_flops / (sum(r["triton"] for r in base_us) / 1e6) / 1e12, 1),
+                "what": "the reference's own fused GPU linear (tools/idol_triton.py:94-126, Triton _linear_kernel, "
+                        "bf16 activations) on the same shapes and operands; per shape in shapes[].us_reference_triton"}
+        else:
+            errs = [r.get("error") for r in base_us if r.get("error")]
+            out["gpu_baselines"]["reference_triton_fused_linear"] = {
+                "value": None, "why": errs[0] if errs else "baseline/_ref/idol_triton.py not staged"}
     del ops
     torch.cuda.empty_cache()
     return out
@@ -508,14 +552,14 @@ def block_kernel_times(block, dev, stream, seqs):
     f1 = torch.empty((rows, H), device=dev, dtype=torch.bfloat16)
     att = torch.empty((rows, D), device=dev, dtype=torch.bfloat16)
     qkv_w(h, out=qkv)
-    layers.rms_heads_(qkv[:, :D], BLOCK_HEADS, block.q_gamma)
-    layers.rms_heads_(qkv[:, D:2 * D], BLOCK_HEADS, block.k_gamma)
+    qk_gamma = torch.cat([block.q_gamma, block.k_gamma])  # the same launch as the block's fused q/k rms_heads
+    layers.rms_heads_(qkv[:, :2 * D], 2 * BLOCK_HEADS, qk_gamma)
     ff1_w(h, act=C.ACT_GELU_TANH, out=f1)
     kernels = [
         ("norm_rows (fp32 -> bf16)", 2, lambda: layers.norm_rows(x, 1e-6, out=h), "hbm", rows * D * (4 + 2)),
         ("q8_gemm qkv 1024->3072", 1, lambda: qkv_w(h, out=qkv), "tensor", 2.0 * rows * 3 * D * D),
-        ("rms_heads (q or k)", 2, lambda: layers.rms_heads_(qkv[:, :D], BLOCK_HEADS, block.q_gamma), "hbm",
-         rows * D * 2 * 2),
+        ("rms_heads (q and k)", 1, lambda: layers.rms_heads_(qkv[:, :2 * D], 2 * BLOCK_HEADS, qk_gamma), "hbm",
+         rows * 2 * D * 2 * 2),
         ("attention", 1, lambda: layers.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], BLOCK_HEADS,
                                                   batch=seqs, out=att), "tensor",
          4.0 * BLOCK_TOKENS ** 2 * D * seqs),
@@ -551,9 +595,9 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import __graft_entry__
-    from idol_b200.shard import image_shard
 
     pkg = __graft_entry__.load_package()
+    from idol_b200.shard import image_shard
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     hbm_peak, tc_peak, peak_kind = peaks()

@@ -170,6 +170,74 @@ __global__ void kv_project_kernel(const float* __restrict__ cond, long long rows
     }
 }
 
+
+// The same projection for the 16-wide condition of the real model, with rms_heads of the key half fused in
+// (src/decoders.cpp:237 then :238): a half-warp owns one 64-column head and a lane four adjacent columns, whose 64
+// weights stay in registers; a CTA covers 1024 columns of 32 rows, the rows' conditions staged in shared memory. Each
+// value is the FMA chain of kv_project_kernel rounded to bf16; a key head is then normalised from those rounded
+// values, x * 8 / max(|x|, 1e-12) * gamma (head dim 64), and rounded again, as rms_heads does to the stored row; each
+// lane stores its four columns as one 8-byte word.
+constexpr int kKv16Rows = 32;
+__global__ void __launch_bounds__(256) kv_project16_kernel(const float* __restrict__ cond, long long rows,
+                                                           const float* __restrict__ w, const float* __restrict__ b,
+                                                           int cols, int key_cols, const float* __restrict__ k_gamma,
+                                                           __nv_bfloat16* __restrict__ kv) {
+    __shared__ float cs[kKv16Rows][16];
+    const long long r0 = (long long)blockIdx.y * kKv16Rows;
+    for (int i = threadIdx.x; i < kKv16Rows * 16; i += blockDim.x) {
+        const long long r = r0 + i / 16;
+        cs[i / 16][i % 16] = r < rows ? cond[r * 16 + i % 16] : 0.0f;
+    }
+    __syncthreads();
+    const int j0 = blockIdx.x * 1024 + threadIdx.x * 4;  // this lane's four columns; a warp's 128 are whole heads
+    if (j0 >= cols) return;
+    float wr[4][16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(w + (long long)(j0 + u) * 16 + c);
+            wr[u][c] = v.x;
+            wr[u][c + 1] = v.y;
+            wr[u][c + 2] = v.z;
+            wr[u][c + 3] = v.w;
+        }
+    float bj[4], gj[4];
+    const bool key = k_gamma != nullptr && j0 < key_cols;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        bj[u] = b ? b[j0 + u] : 0.0f;
+        gj[u] = key ? k_gamma[(j0 + u) % key_cols] : 1.0f;
+    }
+    for (int i = 0; i < kKv16Rows; ++i) {
+        const long long r = r0 + i;
+        if (r >= rows) break;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) acc = fmaf(cs[i][c], wr[u][c], acc);
+            v[u] = __bfloat162float(__float2bfloat16_rn(acc + bj[u]));
+        }
+        // The half-warp holds one head: its sum of squares over the 16 lanes (every lane of the warp takes part in
+        // the shuffles; value heads discard the result).
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (key) {
+            const float mult = 8.0f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = v[u] * mult * gj[u];
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 pkt;
+        pkt.x = *reinterpret_cast<uint32_t*>(&lo);
+        pkt.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(kv + r * cols + j0) = pkt;
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_decoder_input(const float* points, long long rows, int dim, const float* w, const float* b,
@@ -181,12 +249,23 @@ cudaError_t launch_decoder_input(const float* points, long long rows, int dim, c
 }
 
 cudaError_t launch_kv_project(const float* cond, long long rows, int cdim, const float* w, const float* b, int cols,
-                              __nv_bfloat16* kv, cudaStream_t s) {
+                              __nv_bfloat16* kv, cudaStream_t s, const float* k_gamma, int heads) {
     if (rows == 0) return cudaSuccess;
+    const int key_cols = cols / 2;
+    const bool fast = cdim == 16 && cols % 128 == 0 && key_cols % 64 == 0 &&
+                      reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(kv) % 8 == 0 &&
+                      (rows + kKv16Rows - 1) / kKv16Rows <= 65535;
+    if (fast) {
+        const dim3 grid((unsigned)((cols + 1023) / 1024), (unsigned)((rows + kKv16Rows - 1) / kKv16Rows));
+        kv_project16_kernel<<<grid, 256, 0, s>>>(cond, rows, w, b, cols, key_cols, k_gamma, kv);
+        return cudaGetLastError();
+    }
     if (cdim < 1 || cdim > kKvMaxCond || rows > 65535LL * 16) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)((cols + 255) / 256), (unsigned)((rows + 15) / 16));
     kv_project_kernel<<<grid, 256, 0, s>>>(cond, rows, cdim, w, b, cols, kv);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || !k_gamma) return e;
+    return launch_rms_heads(kv, IDOL_BF16, cols, rows, heads, k_gamma, s);
 }
 
 cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long points, long long ld, float* out,
@@ -308,8 +387,7 @@ int idol_b200_block_forward(const idol_block* b, void* x, int x_dtype, int64_t t
                                      nullptr, s));
     int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, 3 * D, rows, b->heads, b->q_gamma, s));
-    IDOL_CUDA(idol::launch_rms_heads(big + D, IDOL_BF16, 3 * D, rows, b->heads, b->k_gamma, s));
+    IDOL_CUDA(idol::launch_rms_heads_qk(big, 3 * D, rows, b->heads, b->q_gamma, b->k_gamma, s));
     idol::AttentionCall ac = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
     rc = idol::attention(ac);
     if (rc != IDOL_OK) return rc;
@@ -393,8 +471,7 @@ int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int
                                      nullptr, s));
     int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, 3 * D, rows, b->heads, b->q_gamma, s));
-    IDOL_CUDA(idol::launch_rms_heads(big + D, IDOL_BF16, 3 * D, rows, b->heads, b->k_gamma, s));
+    IDOL_CUDA(idol::launch_rms_heads_qk(big, 3 * D, rows, b->heads, b->q_gamma, b->k_gamma, s));
     idol::AttentionCall sa = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
     rc = idol::attention(sa);
     if (rc != IDOL_OK) return rc;
@@ -407,12 +484,9 @@ int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int
     rc = gemm(g->cross_q, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, D, s);
     if (rc != IDOL_OK) return rc;
     IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, D, rows, b->heads, g->cq_gamma, s));
-    {
-        const dim3 grid((unsigned)((2 * D + 255) / 256), (unsigned)((crows + 15) / 16));
-        idol::kv_project_kernel<<<grid, 256, 0, s>>>(cond, crows, g->cond_dim, g->kv_w, g->kv_b, 2 * D, kv);
-        IDOL_CUDA(cudaGetLastError());
-    }
-    IDOL_CUDA(idol::launch_rms_heads(kv, IDOL_BF16, 2 * D, crows, b->heads, g->ck_gamma, s));
+    // to_kv of the condition rows with the key half's rms_heads fused in.
+    IDOL_CUDA(idol::launch_kv_project(cond, crows, g->cond_dim, g->kv_w, g->kv_b, 2 * D, kv, s, g->ck_gamma,
+                                      b->heads));
     idol::AttentionCall ca = {big, kv, kv + D, h, tokens, cond_rows, D, 2 * D, D, b->heads, 64, images, s};
     rc = idol::attention(ca);
     if (rc != IDOL_OK) return rc;

@@ -101,6 +101,9 @@ cudaError_t launch_norm_rows(const void* x, int x_dtype, long long ldx, void* y,
                              const float* shift, const float* scale, cudaStream_t s);
 cudaError_t launch_rms_heads(void* x, int dtype, long long ld, long long rows, int heads, const float* gamma,
                              cudaStream_t s);
+// rms_heads of adjacent bf16 q and k blocks (heads x 64 columns each, rows ld apart) in one launch.
+cudaError_t launch_rms_heads_qk(void* x, long long ld, long long rows, int heads, const float* gamma_q,
+                                const float* gamma_k, cudaStream_t s);
 
 // Attention (attention.cu).
 struct AttentionCall {
@@ -125,8 +128,10 @@ cudaError_t launch_gaussian_heads(const void* raw, int raw_dtype, long long poin
 // of the condition rows (block.cu).
 cudaError_t launch_decoder_input(const float* points, long long rows, int dim, const float* w, const float* b,
                                  const float* freqs, int fd, __nv_bfloat16* out, cudaStream_t s);
+// kv = cond w^T + b as bf16 [rows, cols]; with k_gamma, the first cols / 2 columns (the keys) also get rms_heads
+// (heads of 64) with that gamma, fused into the projection when cdim is 16.
 cudaError_t launch_kv_project(const float* cond, long long rows, int cdim, const float* w, const float* b, int cols,
-                              __nv_bfloat16* kv, cudaStream_t s);
+                              __nv_bfloat16* kv, cudaStream_t s, const float* k_gamma = nullptr, int heads = 0);
 
 }  // namespace idol
 

@@ -111,6 +111,59 @@ __global__ void rms_heads_kernel(T* __restrict__ x, long long ld, long long rows
     p[1] = from_f<T>(b * mult * g[1]);
 }
 
+// rms_heads over `total` bf16 heads of a row in one pass, the first `first` heads with gamma_a and the rest with
+// gamma_b (the q and k blocks of a packed projection: first = heads, total = 2 heads). Eight lanes own one 64-wide
+// head (16 bytes each), a warp four heads of one row. total % 4 == 0.
+__global__ void rms_heads_vec_kernel(__nv_bfloat16* __restrict__ x, long long ld, long long rows, int total, int first,
+                                     const float* __restrict__ gamma_a, const float* __restrict__ gamma_b) {
+    const int groups = total / 4;
+    const long long unit = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (unit >= rows * groups) return;
+    const int lane = threadIdx.x % 32;
+    const long long row = unit / groups;
+    const int col = (int)(unit % groups) * 256 + lane * 8;
+    const float* g = col / 64 < first ? gamma_a + col : gamma_b + (col - first * 64);
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + row * ld + col);
+    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(pr[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+    for (int o = 4; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mult = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) = 8
+    const float4 g0 = *reinterpret_cast<const float4*>(g), g1 = *reinterpret_cast<const float4*>(g + 4);
+    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    uint4 out;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 o2 = __floats2bfloat162_rn(v[2 * i] * mult * gg[2 * i], v[2 * i + 1] * mult * gg[2 * i + 1]);
+        po[i] = *reinterpret_cast<const uint32_t*>(&o2);
+    }
+    *reinterpret_cast<uint4*>(x + row * ld + col) = out;
+}
+
+bool rms_vec_ok(const void* x, long long ld, int total, const float* ga, const float* gb) {
+    return total % 4 == 0 && ld % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(ga) % 16 == 0 && reinterpret_cast<uintptr_t>(gb) % 16 == 0;
+}
+
+cudaError_t launch_rms_vec(void* x, long long ld, long long rows, int total, int first, const float* ga,
+                           const float* gb, cudaStream_t s) {
+    const long long units = rows * (total / 4);
+    const int warps = 8;
+    rms_heads_vec_kernel<<<(unsigned)((units + warps - 1) / warps), warps * 32, 0, s>>>(
+        static_cast<__nv_bfloat16*>(x), ld, rows, total, first, ga, gb);
+    return cudaGetLastError();
+}
+
 template <typename TI, typename TO>
 cudaError_t launch_norm(const void* x, long long ldx, void* y, long long ldy, long long rows, int dim, float eps,
                         const float* gamma, const float* beta, const float* shift, const float* scale, cudaStream_t s) {
@@ -164,6 +217,8 @@ cudaError_t launch_rms_heads(void* x, int dtype, long long ld, long long rows, i
                              cudaStream_t s) {
     const long long units = rows * heads;
     if (units == 0) return cudaSuccess;
+    if (dtype == IDOL_BF16 && rms_vec_ok(x, ld, heads, gamma, gamma))
+        return launch_rms_vec(x, ld, rows, heads, heads, gamma, gamma, s);
     const int warps = 8;
     const unsigned grid = (unsigned)((units + warps - 1) / warps);
     if (dtype == IDOL_BF16)
@@ -176,6 +231,16 @@ cudaError_t launch_rms_heads(void* x, int dtype, long long ld, long long rows, i
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();
+}
+
+cudaError_t launch_rms_heads_qk(void* x, long long ld, long long rows, int heads, const float* gamma_q,
+                                const float* gamma_k, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    if (rms_vec_ok(x, ld, 2 * heads, gamma_q, gamma_k))
+        return launch_rms_vec(x, ld, rows, 2 * heads, heads, gamma_q, gamma_k, s);
+    const cudaError_t e = launch_rms_heads(x, IDOL_BF16, ld, rows, heads, gamma_q, s);
+    if (e != cudaSuccess) return e;
+    return launch_rms_heads(static_cast<__nv_bfloat16*>(x) + heads * 64, IDOL_BF16, ld, rows, heads, gamma_k, s);
 }
 
 }  // namespace idol

@@ -159,8 +159,8 @@ int oct_logits(const idol_oct_decoder* d, const float* x, int64_t rows, float re
                                          shift_a, scale_a, s));
         if ((rc = idol::gemm(b->cross_q, w.h, rows, D, IDOL_ACT_NONE, w.big, IDOL_BF16, D, s)) != IDOL_OK) return rc;
         IDOL_CUDA(idol::launch_rms_heads(w.big, IDOL_BF16, D, rows, d->heads, b->cq_gamma, s));
-        IDOL_CUDA(idol::launch_kv_project(cond, cond_rows, b->cond_dim, b->kv_w, b->kv_b, 2 * D, w.kv, s));
-        IDOL_CUDA(idol::launch_rms_heads(w.kv, IDOL_BF16, 2 * D, cond_rows, d->heads, b->ck_gamma, s));
+        IDOL_CUDA(idol::launch_kv_project(cond, cond_rows, b->cond_dim, b->kv_w, b->kv_b, 2 * D, w.kv, s, b->ck_gamma,
+                                          d->heads));
         idol::AttentionCall ac = {w.big, w.kv, w.kv + D, w.h, rows, cond_rows, D, 2 * D, D, d->heads, 64, 1, s};
         if ((rc = idol::attention(ac)) != IDOL_OK) return rc;
         if ((rc = idol::gemm(b->cross_out, w.h, rows, D, IDOL_ACT_NONE, w.tmp, IDOL_F32, D, s)) != IDOL_OK) return rc;

