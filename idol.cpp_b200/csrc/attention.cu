@@ -257,6 +257,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_used = m_blk;
                 rescale = true;
             }
+            // p = exp2(s scale - m) on key pairs (packed FMA), summed in four independent pairs of partial sums and
+            // packed to bf16 in registers (masked keys give exp2(-inf) = 0). This needs nothing from the tensor pipe,
+            // so it runs while P V of block j - 1 may still be reading the P buffer.
+            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+            const float2 nm2 = make_float2(-m_used, -m_used);
+            float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
+            uint32_t pk[kKTile / 2];
+#pragma unroll
+            for (int c = 0; c < kKTile; c += 2) {
+                const float2 x2 = __ffma2_rn(make_float2(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])), sc2, nm2);
+                const float2 e = make_float2(ex2(x2.x), ex2(x2.y));
+                sum2[(c / 2) % 4] = __fadd2_rn(sum2[(c / 2) % 4], e);
+                pk[c / 2] = pack_bf16x2(e.x, e.y);
+            }
             // P_t,j and a rescaled O_t go to TMEM only after P V of block j - 1 has completed.
             if (j >= 1) {
                 got = mbar_wait(&o_full[t], (j - 1) & 1, abort_flag);
@@ -276,25 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // p = exp2(s scale - m) on key pairs (packed FMA), summed in four independent pairs of partial sums,
-            // packed to bf16 and stored 32 keys at a time (masked keys give exp2(-inf) = 0).
-            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-            const float2 nm2 = make_float2(-m_used, -m_used);
-            float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                              make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int c0 = 0; c0 < kKTile; c0 += 32) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    const float2 x2 = __ffma2_rn(make_float2(__uint_as_float(sv[c0 + c]), __uint_as_float(sv[c0 + c + 1])),
-                                                 sc2, nm2);
-                    const float2 e = make_float2(ex2(x2.x), ex2(x2.y));
-                    sum2[(c / 2) % 4] = __fadd2_rn(sum2[(c / 2) % 4], e);
-                    pk[c / 2] = pack_bf16x2(e.x, e.y);
-                }
-                tmem_st16(tt + kColP + c0 / 2, pk);
-            }
+            for (int c0 = 0; c0 < kKTile / 2; c0 += 16)
+                tmem_st16(tt + kColP + c0, *reinterpret_cast<uint32_t(*)[16]>(pk + c0));
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
             const float2 s4 = __fadd2_rn(s01, s23);
             l_run = l_run * alpha + (s4.x + s4.y);
