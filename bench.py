@@ -51,7 +51,7 @@ BLOCK_IMAGES, BLOCK_TOKENS, BLOCK_D, BLOCK_HEADS, BLOCK_H = 2, 4096, 1024, 16, 4
 BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOCK_D * BLOCK_D + 2 * BLOCK_H * BLOCK_D)
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
 STACK_BLOCKS, STACK_IMAGES, CFG = 24, 64, 2
-CHUNK_IMAGES = 2  # images per pass through the blocks (4 sequences, 32768 rows)
+CHUNK_IMAGES = 4  # images per pass through the blocks (8 sequences, 32768 rows)
 LAUNCHES_PER_BLOCK = 8  # norm, qkv, rms_heads of q and k, attention, out + residual, norm, ff1, ff2 + residual
 METRIC = "denoiser-block steps/s (config 5: 24-block stack over 64 images x 2 CFG branches, sharded by image)"
 UNIT = "block-steps/s"
@@ -604,7 +604,7 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(device=dev)
 
     first, count = image_shard(STACK_IMAGES, rank, world)
-    seqs, chunk = count * CFG, CHUNK_IMAGES * CFG
+    seqs, chunk = count * CFG, args.chunk_images * CFG
     stack = make_stack(dev)
     x = make_images(dev, first, count)
     host_x = x.cpu().pin_memory()  # the same images, for the end-to-end pass
@@ -720,8 +720,8 @@ def run_ours(args, rank, world, local_rank):
         "tflops": round(units * BLOCK_FLOPS * args.steps / (ms / 1e3) / 1e12, 1),
         "e2e": {"value": round(units * e2e_steps / (e2e_ms / 1e3), 2), "unit": UNIT,
                 "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes, "steps": e2e_steps,
-                "api": "DenoiserStack.forward_ per chunk of 2 images from pinned host memory; H2D, compute and D2H "
-                       "on three streams"},
+                "api": f"DenoiserStack.forward_ per chunk of {args.chunk_images} images from pinned host memory; "
+                       "H2D, compute and D2H on three streams"},
         "roofline": {"bound": top["bound"], "kernel": top["kernel"], "achieved": top["achieved"],
                      "peak": top["peak"], "unit": top["unit"], "frac": top["frac"],
                      "peak_source": f"{peak_kind} {'bf16 burst' if top['bound'] == 'tensor' else 'copy'}",
@@ -1031,6 +1031,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--sweep-steps", type=int, default=200, help="timed sweeps of the config-2 GEMM sweep (N = 1)")
+    ap.add_argument("--chunk-images", type=int, default=CHUNK_IMAGES,
+                    help="images (of 2 CFG branches) per pass through the 24 blocks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpu-baselines", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the config-5 stack (no sweep or compositions)")

@@ -49,17 +49,25 @@ __device__ __forceinline__ float from_out(OutT v) {
     else return __half2float(v);
 }
 
-// Activations of the epilogue. SiLU is v sigmoid(v) = v / (1 + e^-v); GELU-tanh uses the identity
-// 0.5 v (1 + tanh u) = v sigmoid(2u) = v / (1 + e^-2u) with u = sqrt(2/pi) (v + 0.044715 v^3). Both run on the fast
-// base-2 exponential and approximate division intrinsics (relative error near 2^-21, far below the bf16/fp16 output
-// rounding); e^-v overflowing to +inf gives -0, the correct limit. GELU-erf keeps erff.
+// Activations of the epilogue. SiLU is v sigmoid(v) = v / (1 + e^-v), on the fast base-2 exponential and approximate
+// division intrinsics (relative error near 2^-21; e^-v overflowing to +inf gives -0, the correct limit). GELU-tanh is
+// 0.5 v (1 + tanh u) with u = sqrt(2/pi) v (1 + 0.044715 v^2), the tanh from the special-function unit's tanh.approx
+// (one instruction; absolute error near 2^-11 |tanh u|, so the output's absolute error stays below 2^-12 |v|, far
+// under the tolerance of the layers that consume it). GELU-erf keeps erff.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <int kAct>
 __device__ __forceinline__ float activate_t(float v) {
     if constexpr (kAct == IDOL_ACT_GELU_ERF) {
         return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
     } else if constexpr (kAct == IDOL_ACT_GELU_TANH) {
-        const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-        return __fdividef(v, 1.0f + __expf(-2.0f * u));
+        const float u = (0.7978845608028654f * v) * fmaf(0.044715f, v * v, 1.0f);
+        const float h = 0.5f * v;
+        return fmaf(h, tanh_approx(u), h);
     } else if constexpr (kAct == IDOL_ACT_SILU) {
         return __fdividef(v, 1.0f + __expf(-v));
     } else {
