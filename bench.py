@@ -108,8 +108,17 @@ def cpu_info():
     logical = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     physical = min(len(phys), logical) if phys else logical
     m = re.search(r"@\s*([\d.]+)\s*GHz", model)
-    ghz = float(m.group(1)) if m else None
-    return {"model": model, "logical_cpus": logical, "physical_cores": physical, "ghz": ghz,
+    ghz, source = (float(m.group(1)), "model name") if m else (None, None)
+    if ghz is None:
+        try:  # the highest clock the kernel reports for a CPU
+            khz = int(Path("/sys/devices/system/cpu/cpu0/cpufreq/cpuinfo_max_freq").read_text())
+            ghz, source = khz / 1e6, "cpuinfo_max_freq"
+        except (OSError, ValueError):
+            mhz = [float(l.split(":")[1]) for l in Path("/proc/cpuinfo").read_text().splitlines()
+                   if l.startswith("cpu MHz")] if Path("/proc/cpuinfo").exists() else []
+            if mhz:
+                ghz, source = max(mhz) / 1e3, "cpu MHz"
+    return {"model": model, "logical_cpus": logical, "physical_cores": physical, "ghz": ghz, "ghz_source": source,
             "avx2_fma_peak_gflops": round(physical * ghz * 32, 1) if ghz else None}
 
 
@@ -159,7 +168,8 @@ def cpu_baseline_entry(rates, times, facts):
     return {"value": round(v, 4), "unit": UNIT, "cores": facts["threads"], "kind": facts["kind"],
             "sample": f"{facts['sample']}; median of {len(rates)} timed steps ({statistics.median(times):.2f} s each)",
             "cpu_model": facts["model"], "physical_cores": facts["physical_cores"],
-            "omp_threads": facts["threads"], "gflops": round(gflops, 1),
+            "omp_threads": facts["threads"], "ghz": facts["ghz"], "ghz_source": facts["ghz_source"],
+            "gflops": round(gflops, 1),
             "avx2_fma_peak_gflops": peak, "frac_of_avx2_peak": round(gflops / peak, 3) if peak else None}
 
 
@@ -690,6 +700,7 @@ def run_ours(args, rank, world, local_rank):
 
     # Every kernel of a block on a chunk's shapes, timed alone (for the roofline of the dominant one).
     kern = block_kernel_times(stack.blocks[0], dev, stream, chunk)
+    latency = measure_single_image_latency(stack, dev, stream, world)
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms, float(status)], device=dev, dtype=torch.float64)
@@ -730,6 +741,7 @@ def run_ours(args, rank, world, local_rank):
                                         f"{'FLOP' if top['bound'] == 'tensor' else 'bytes'} "
                                         f"({chunk} sequences x {BLOCK_TOKENS} tokens)"},
         "kernels": kernels,
+        "single_request_latency": latency,
         "block_us_sum_of_kernels": round(block_us, 1),
         "block_us_in_stack": round(ms * 1e3 / args.steps / (STACK_BLOCKS * nchunks), 1),
         "gpu_launches": LAUNCHES_PER_BLOCK * STACK_BLOCKS * nchunks * args.steps,
@@ -743,6 +755,55 @@ def run_ours(args, rank, world, local_rank):
         rates, times, facts = cpu_reference_measure(1, 10, budget_s=20.0)
         line["cpu_baseline"] = cpu_baseline_entry(rates, times, facts)
     print(json.dumps(line), flush=True)
+
+
+def measure_single_image_latency(stack, dev, stream, world, passes=3):
+    """Latency of one request: the 24-block stack over one image (2 CFG branches x 4096 tokens). On N > 1 ranks each
+    block runs shard.column_parallel_block_forward_ (the MLP's ff1 and ff2 split by output features over the ranks,
+    each slice all-gathered by NCCL; the result equals the one-GPU block bit for bit); on one GPU the stack itself.
+    Device time of `passes` passes (CUDA events; max over ranks) and the all-gathers' share of it."""
+    import torch
+    import torch.distributed as dist
+    from idol_b200.shard import column_parallel_block_forward_
+    g = torch.Generator(device=dev).manual_seed(31)
+    x0 = torch.randn((CFG * BLOCK_TOKENS, BLOCK_D), device=dev, generator=g)
+    x = x0.clone()
+    events = []
+
+    def one_pass(record):
+        if world == 1:
+            stack.forward_(x, CFG)
+        else:
+            for b in stack.blocks:
+                column_parallel_block_forward_(b, x, images=CFG, gather_events=events if record else None)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            one_pass(False)
+    stream.synchronize()
+    x.copy_(x0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(passes):
+            one_pass(True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    gather_ms = sum(a.elapsed_time(b) for a, b in events)
+    if world > 1:
+        t = torch.tensor([ms, gather_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, gather_ms = float(t[0]), float(t[1])
+    return {"metric": "single-request latency: the 24-block stack over one image (2 CFG branches x 4096 tokens)",
+            "ms_per_pass": round(ms / passes, 3), "passes": passes,
+            "mode": ("one GPU" if world == 1 else
+                     f"column-parallel MLP over {world} GPUs (ff1/ff2 split by output features, NCCL all-gather of "
+                     "each slice; equal to the one-GPU result bit for bit)"),
+            "all_gather_share": None if world == 1 else round(gather_ms / ms, 3)}
 
 
 def traffic_for(kernel):

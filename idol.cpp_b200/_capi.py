@@ -14,6 +14,7 @@ OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE = 0, 1, 2, 3, 4
 F32, F16, BF16 = 0, 1, 2
 ACT_NONE, ACT_GELU_ERF, ACT_GELU_TANH, ACT_SILU = 0, 1, 2, 3
 EPI_BIAS_AFTER_ROUND = 0x1
+GEMM_WHOLE_K = 0x2
 
 # Every symbol include/idol_b200.h declares, with (restype, argtypes).
 _vp, _i32, _i64, _u32p = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint)

@@ -44,13 +44,20 @@ class Q8Weight:
         return cls(quantize(w.float().contiguous()), w.shape[0], w.shape[1], bias)
 
     def __call__(self, x: torch.Tensor, act: int = C.ACT_NONE, residual: Optional[torch.Tensor] = None,
-                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                 cols: Optional[tuple] = None, flags: int = 0) -> torch.Tensor:
+        """y = x W^T + b (+ residual) (-> act). `cols` = (first, count) computes only output features first ..
+        first + count - 1 (src/kernels.hpp:75-76 gemm_packed's window): `out` and `residual` then hold just those
+        columns. `flags`: IDOL_* GEMM flags (C.GEMM_WHOLE_K keeps a window equal to the full product bit for bit)."""
         x2 = x if (x.stride(-1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
+        first, count = (0, self.out) if cols is None else (int(cols[0]), int(cols[1]))
         if out is None:
-            out = torch.empty((x2.shape[0], self.out), dtype=out_dtype or x.dtype, device=x.device)
+            out = torch.empty((x2.shape[0], count), dtype=out_dtype or x.dtype, device=x.device)
+        if out.dim() != 2 or out.stride(1) != 1 or out.shape[1] < count or out.shape[0] != x2.shape[0]:
+            raise ValueError("Q8Weight: out must be a [rows, >= count] tensor with unit column stride")
         ldr = 0 if residual is None else residual.stride(0)
         C.check(C.lib().idol_b200_q8_gemm(ctypes.c_void_p(self.handle), _ptr(x2), _DTYPES[x2.dtype], x2.shape[0],
-                                          x2.stride(0), 0, self.out, _ptr(residual), ldr, act, 0, _ptr(out),
+                                          x2.stride(0), first, count, _ptr(residual), ldr, act, flags, _ptr(out),
                                           _DTYPES[out.dtype], out.stride(0), _stream(x.device)))
         return out
 
@@ -87,7 +94,7 @@ class DenoiserBlock:
         C.check(C.lib().idol_b200_block_create(*(ctypes.c_void_p(w.handle) for w in self.weights), _ptr(self.q_gamma),
                                                _ptr(self.k_gamma), heads, float(eps), ctypes.byref(h)))
         self.handle = h.value
-        self.dim, self.heads, self.device = out.out, heads, dev
+        self.dim, self.heads, self.device, self.eps = out.out, heads, dev, float(eps)
         self.ws = _Workspace()
 
     def workspace_bytes(self, rows: int) -> int:

@@ -943,6 +943,7 @@ int q8_gemm(const GemmCall& c) {
     const int tiles_n = (c.n_offset + c.n - p.row_begin + kRowsPerTile - 1) / kRowsPerTile;
     int bn = 0, splits = 1;
     choose_tiles(w.device, c.m, tiles_n, p.stages_total, &bn, &splits);
+    if (c.flags & IDOL_GEMM_WHOLE_K) splits = 1;
 
     // The persistent CTA-pair kernel overlaps each tile's epilogue with the next tile's main loop, which pays when the
     // main loop is short: measured on B200, K <= 512 with N >= 256 and M >= 4096 (the Gaussian MLP's 128->512 and

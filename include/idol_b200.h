@@ -40,6 +40,10 @@ extern "C" {
 /* Epilogue flags. */
 #define IDOL_EPI_BIAS_AFTER_ROUND 0x1 /* round the product to the output type before adding the bias, as
                                           tools/idol_triton.py:84-89 does; default adds it in fp32 like finish_tile */
+#define IDOL_GEMM_WHOLE_K 0x2         /* never split K across CTAs: each output is summed in the order the unsplit
+                                          full-width GEMM uses, so a column window (one rank's slice of a
+                                          column-parallel linear) equals those columns of the whole product bit for
+                                          bit whatever its width */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* idol_b200_last_error(void);
