@@ -61,6 +61,26 @@ class Q8Weight:
                                           _DTYPES[out.dtype], out.stride(0), _stream(x.device)))
         return out
 
+    def int8act(self, x: torch.Tensor, act: int = C.ACT_NONE, residual: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+                cols: Optional[tuple] = None) -> torch.Tensor:
+        """The same linear on integer activations, the reference's set_quant_kernel(1) path (src/kernels.cpp:368-479):
+        x (fp32, bf16 or f16) is quantized per (row, 32-group) to int8 and the groups' integer dot products are
+        scaled and summed in the reference's order, so the result equals that kernel's bit for bit."""
+        if x.dim() != 2 or x.stride(1) != 1 or x.dtype not in _DTYPES:
+            raise ValueError("Q8Weight.int8act: x must be a 2-D tensor with unit column stride")
+        first, count = (0, self.out) if cols is None else (int(cols[0]), int(cols[1]))
+        if out is None:
+            out = torch.empty((x.shape[0], count), dtype=out_dtype, device=x.device)
+        nbytes = int(C.lib().idol_b200_q8_gemm_int8act_workspace_bytes(x.shape[0], self.inp))
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+        ldr = 0 if residual is None else residual.stride(0)
+        C.check(C.lib().idol_b200_q8_gemm_int8act(ctypes.c_void_p(self.handle), _ptr(x), _DTYPES[x.dtype], x.shape[0],
+                                                  x.stride(0), first, count, _ptr(residual), ldr, act, _ptr(out),
+                                                  _DTYPES[out.dtype], out.stride(0), _ptr(ws), ws.numel(),
+                                                  _stream(x.device)))
+        return out
+
     def __del__(self):
         h = getattr(self, "handle", None)
         if h:

@@ -350,6 +350,21 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
     return idol::q8_gemm(c);
 }
 
+int64_t idol_b200_q8_gemm_int8act_workspace_bytes(int64_t m, int in) { return idol::int8act_workspace_bytes(m, in); }
+
+int idol_b200_q8_gemm_int8act(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                              int n_offset, int n, const void* residual, int64_t ldr, int act, void* y, int y_dtype,
+                              int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_gemm_int8act: matrix is NULL");
+    if (m < 0 || n < 0) return fail(IDOL_ERR_INVALID, "q8_gemm_int8act: sizes");
+    idol::GemmCall c = {&matrix->m, x, x_dtype, m, ldx, n_offset, n, residual, ldr, act, 0, y, y_dtype, ldy,
+                        static_cast<cudaStream_t>(stream)};
+    const int rc = idol::q8_gemm_int8act_check(c, workspace, workspace_bytes);  // refused before any device call
+    if (rc != IDOL_OK || m == 0 || n == 0) return rc;
+    IDOL_CUDA(cudaSetDevice(matrix->m.device));
+    return idol::q8_gemm_int8act(c, workspace, workspace_bytes);
+}
+
 int idol_b200_norm_rows(const void* x, int x_dtype, int64_t rows, int dim, int64_t ldx, float eps, const float* gamma,
                         const float* beta, const float* shift, const float* scale, void* y, int y_dtype, int64_t ldy,
                         void* stream) {

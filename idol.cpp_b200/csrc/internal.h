@@ -85,6 +85,11 @@ struct GemmCall {
     cudaStream_t stream;
 };
 int q8_gemm(const GemmCall& c);
+// The integer-activation form of the same linear (q8_int8act.cu): flags unused; workspace for the quantized
+// activations (int8act_workspace_bytes).
+int64_t int8act_workspace_bytes(int64_t m, int k);
+int q8_gemm_int8act_check(const GemmCall& c, void* workspace, int64_t workspace_bytes);  // arguments only
+int q8_gemm_int8act(const GemmCall& c, void* workspace, int64_t workspace_bytes);
 
 // Tensor-map creation through the driver entry point (no link-time dependency on libcuda).
 int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const cuuint64_t* dims,

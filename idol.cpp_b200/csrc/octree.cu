@@ -329,7 +329,9 @@ int idol_b200_oct_sampler_step(idol_oct_sampler* s, const float* logits) {
     std::vector<uint32_t> next_coords;
     std::vector<int64_t> next_counts;
     for (int p = 0; p < parents; ++p) {
-        // Softmax over the eight children, then systematic resampling of the cell's points among them.
+        // This cell's points are shared out among its eight child cells: child probabilities from the logits (max
+        // subtracted, exponentiated, normalised), then one uniform draw places an evenly spaced comb of the points
+        // on the cumulative distribution.
         float e[8];
         float mx = logits[(size_t)p * 8];
         for (int c = 1; c < 8; ++c) mx = std::max(mx, logits[(size_t)p * 8 + c]);

@@ -141,6 +141,18 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
                       int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
                       void* stream);
 
+/* The same linear on integer activations: the reference's second CPU kernel (src/kernels.cpp:368-479,
+ * quantize_activations + vnni_task + gemm_quant_int8, chosen there by set_quant_kernel(1)), bit for bit on Q8_0
+ * matrices. x (IDOL_F32, IDOL_BF16 or IDOL_F16, rows ldx apart) is quantized per (row, 32-deep group) to int8 with
+ * scale amax / 127 into the workspace; each output sums the groups' integer dot products scaled as the reference
+ * does, then bias, residual (y_dtype, window layout, may alias y) and act. Output IDOL_F32 (the reference's), IDOL_BF16
+ * or IDOL_F16. workspace: device, 256-byte aligned, >= idol_b200_q8_gemm_int8act_workspace_bytes(m, in). Q4_K
+ * matrices are refused (IDOL_ERR_UNSUPPORTED). */
+int64_t idol_b200_q8_gemm_int8act_workspace_bytes(int64_t m, int in);
+int idol_b200_q8_gemm_int8act(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                              int n_offset, int n, const void* residual, int64_t ldr, int act, void* y, int y_dtype,
+                              int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------ norms and attention */
 
 /* y = LayerNorm(x) per row of `dim` values (eps as given), then optionally * gamma + beta, then optionally

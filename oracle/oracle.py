@@ -46,6 +46,9 @@ def lib():
         L.orc_q8_to_panels.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p]
         L.orc_gemm_q8.argtypes = [_f32p, ctypes.c_int, _u8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, _f32p, ctypes.c_int, _f32p]
+        L.orc_gemm_q8_int8act.argtypes = L.orc_gemm_q8.argtypes
+        L.orc_quantize_activations.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int8),
+                                               _f32p, ctypes.POINTER(ctypes.c_int32)]
         L.orc_activate.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int]
         L.orc_norm_rows.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p, _f32p, _f32p,
                                     _f32p]
@@ -183,6 +186,33 @@ def gemm_q8(a, q8, bias, N, K, n_offset=0, n=None, residual=None, act=ACT_NONE):
     c = np.empty((m, n), np.float32)
     lib().orc_gemm_q8(_ptr(a), m, _ptr(q8, _u8p), _ptr(bias), N, K, n_offset, n, _ptr(residual), act, _ptr(c))
     return c
+
+
+def gemm_q8_int8act(a, q8, bias, N, K, n_offset=0, n=None, residual=None, act=ACT_NONE):
+    """The reference's integer-activation kernel (src/kernels.cpp:368-479): activations quantized per (row, 32-group)
+    to int8, integer dot products per group, the group's float update in the reference's order."""
+    a = c32(a)
+    m = a.shape[0]
+    n = N - n_offset if n is None else n
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    bias = None if bias is None else c32(bias)
+    residual = None if residual is None else c32(residual)
+    c = np.empty((m, n), np.float32)
+    lib().orc_gemm_q8_int8act(_ptr(a), m, _ptr(q8, _u8p), _ptr(bias), N, K, n_offset, n, _ptr(residual), act,
+                              _ptr(c))
+    return c
+
+
+def quantize_activations(a):
+    """(qa int8 [m, K], scale fp32 [m, K/32], qsum int32 [m, K/32]) as src/kernels.cpp:368-402."""
+    a = c32(a)
+    m, K = a.shape
+    qa = np.empty((m, K), np.int8)
+    sc = np.empty((m, K // 32), np.float32)
+    qs = np.empty((m, K // 32), np.int32)
+    lib().orc_quantize_activations(_ptr(a), m, K, qa.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _ptr(sc),
+                                   qs.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+    return qa, sc, qs
 
 
 def activate(x, act):

@@ -309,6 +309,64 @@ void orc_gemm_q8(const float* a, int m, const uint8_t* q8, const float* bias, in
     free(out);
 }
 
+/* ------------------------------------------------------------------------------------------------------------------
+ * The same linear on integer activations: the reference's second CPU kernel (src/kernels.cpp:368-479,
+ * quantize_activations + vnni_task + gemm_quant_int8, chosen there by set_quant_kernel(1)), for Q8_0-derived 8-bit
+ * panels (stored code u = q + 128, minimum -128 d). Activations per (row, 32-group): amax = max |x|, sa = amax / 127,
+ * qa = rint(x * (127 / amax)) (round to nearest even; 0 when amax is 0), qsum = sum qa. Per output the float tile
+ * starts at 0 and takes, group by group in k order, t = fma(float(sum u qa), d * sa, fma(-128 d, sa * float(qsum), t))
+ * (each product rounded, as the reference's vector multiplies are); then bias, residual and the activation as above.
+ * ---------------------------------------------------------------------------------------------------------------- */
+void orc_quantize_activations(const float* a, int m, int K, int8_t* qa, float* scale, int32_t* qsum) {
+    const int ng = K / 32;
+    for (int r = 0; r < m; ++r)
+        for (int g = 0; g < ng; ++g) {
+            const float* x = a + (int64_t)r * K + g * 32;
+            float amax = 0.0f;
+            for (int k = 0; k < 32; ++k) amax = fmaxf(amax, fabsf(x[k]));
+            const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+            int32_t sum = 0;
+            for (int k = 0; k < 32; ++k) {
+                const int32_t q = (int32_t)lrintf(x[k] * inv);
+                qa[(int64_t)r * K + g * 32 + k] = (int8_t)q;
+                sum += q;
+            }
+            scale[(int64_t)r * ng + g] = amax / 127.0f;
+            qsum[(int64_t)r * ng + g] = sum;
+        }
+}
+
+void orc_gemm_q8_int8act(const float* a, int m, const uint8_t* q8, const float* bias, int N, int K, int n_offset,
+                         int n, const float* residual, int act, float* c) {
+    const int ng = K / 32;
+    int8_t* qa = (int8_t*)malloc((size_t)m * K);
+    float* sa = (float*)malloc(sizeof(float) * (size_t)m * ng);
+    int32_t* qs = (int32_t*)malloc(sizeof(int32_t) * (size_t)m * ng);
+    orc_quantize_activations(a, m, K, qa, sa, qs);
+    for (int j = 0; j < n; ++j) {
+        const int col = n_offset + j;
+        if (col >= N) break;
+        for (int i = 0; i < m; ++i) {
+            float t = 0.0f;
+            for (int g = 0; g < ng; ++g) {
+                const uint8_t* blk = q8 + ((int64_t)col * ng + g) * 34;
+                const float d = orc_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+                int32_t acc = 0;
+                for (int k = 0; k < 32; ++k) acc += ((int32_t)(int8_t)blk[2 + k] + 128) * qa[(int64_t)i * K + g * 32 + k];
+                const float s = sa[(int64_t)i * ng + g];
+                const float sq = s * (float)qs[(int64_t)i * ng + g];
+                t = fmaf((float)acc, d * s, fmaf(-128.0f * d, sq, t));
+            }
+            float v = t + (bias ? bias[col] : 0.0f);
+            if (residual) v += residual[(int64_t)i * n + j];
+            c[(int64_t)i * n + j] = apply_act(v, act);
+        }
+    }
+    free(qa);
+    free(sa);
+    free(qs);
+}
+
 /* Elementwise activation in place (the decoders run gelu_tanh / silu as separate passes). */
 void orc_activate(float* x, int64_t count, int act) {
     for (int64_t i = 0; i < count; ++i) x[i] = apply_act(x[i], act);

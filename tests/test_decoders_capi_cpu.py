@@ -115,3 +115,20 @@ def test_gaussian_mlp_create_refuses_matrices_on_different_devices(pkg):
     C.check(L.idol_b200_gaussian_mlp_create(view(512, 128, 0), view(512, 512, 0), view(14, 512, 0),
                                             ctypes.byref(mlp)))
     L.idol_b200_gaussian_mlp_free(mlp)
+
+
+def test_int8_activation_gemm_refusals(pkg):
+    C = pkg._capi
+    L = C.lib()
+    assert L.idol_b200_q8_gemm_int8act_workspace_bytes(10, 1024) >= 10 * 1024 + 2 * 10 * 32 * 4
+    assert L.idol_b200_q8_gemm_int8act_workspace_bytes(10, 100) == -1
+    w = _view(C, 256, 1024)
+    ws = L.idol_b200_q8_gemm_int8act_workspace_bytes(10, 1024)
+    args = lambda x_dtype, n_off, n, act, y_dtype, wsb: (w, ctypes.c_void_p(FAKE), x_dtype, 10, 1024, n_off, n, None,  # noqa: E731
+                                                         0, act, ctypes.c_void_p(FAKE), y_dtype, 256,
+                                                         ctypes.c_void_p(FAKE), wsb, None)
+    assert L.idol_b200_q8_gemm_int8act(*args(C.F32, 0, 256, 0, C.F32, ws - 256)) == C.ERR_INVALID  # workspace
+    assert b"workspace" in L.idol_b200_last_error()
+    assert L.idol_b200_q8_gemm_int8act(*args(C.F32, 200, 100, 0, C.F32, ws)) == C.ERR_INVALID  # window past N
+    assert L.idol_b200_q8_gemm_int8act(*args(C.F32, 0, 256, 9, C.F32, ws)) == C.ERR_INVALID  # activation
+    assert L.idol_b200_q8_gemm_int8act(*args(C.F32, 0, 0, 0, C.F32, ws)) == C.OK  # empty window: nothing to do

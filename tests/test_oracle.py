@@ -133,3 +133,26 @@ def test_reference_composed_block_matches_the_oracle_block(oracle):
     got = oracle.RefBlock(layers, heads).forward_(x.copy(), images=images)
     rms = np.sqrt((want.astype(np.float64) ** 2).mean())
     assert np.abs(got - want).max() <= 1e-5 * rms
+
+
+@pytest.mark.parametrize("m,n,k,n_off,cnt,gelu,res", [(5, 16, 32, 0, 16, 0, 0), (37, 48, 256, 0, 48, 0, 0),
+                                                      (64, 256, 1024, 0, 256, 0, 0), (7, 100, 96, 0, 100, 0, 0),
+                                                      (19, 96, 128, 16, 48, 1, 1), (3, 64, 64, 16, 40, 0, 1)])
+def test_int8_activation_gemm_is_bit_equal_to_the_reference_vnni_kernel(oracle, m, n, k, n_off, cnt, gelu, res):
+    """The restatement of the reference's second kernel (src/kernels.cpp:368-479, set_quant_kernel(1)) against the
+    compiled reference itself: window (on the reference's 16-column panel boundaries, which its windows assume),
+    residual and the erf GELU included."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref not built (no reference checkout)")
+    rng = np.random.default_rng(m * n + k)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+    x = rng.normal(0, 1, (m, k)).astype(np.float32)
+    x[0, :32] = 0.0  # an all-zero group: scale 0, codes 0
+    b = rng.normal(0, 0.01, n).astype(np.float32)
+    r = rng.normal(0, 1, (m, cnt)).astype(np.float32) if res else None
+    mine = oracle.gemm_q8_int8act(x, q8, b, n, k, n_off, cnt, r, oracle.ACT_GELU_ERF if gelu else oracle.ACT_NONE)
+    ref = oracle.RefLinear(q8, b, n, k).gemm(x, n_off, cnt, r, bool(gelu), mode=1)
+    if gelu:
+        np.testing.assert_allclose(mine, ref, rtol=0, atol=2e-6)  # the reference's exp256 vs std::exp, as above
+    else:
+        assert np.array_equal(mine, ref)

@@ -20,16 +20,15 @@ def _bf16(oracle, x):
     return oracle.f32_to_bf16_round(x)
 
 
-def _check(y, ref, tol=TOL, what="", out_rel=0.0):
-    """max |y - ref| <= tol x rms(ref), plus out_rel x |ref| per element for an output rounded to a 2-byte type
-    (half an ulp: 2^-8 for bf16, 2^-11 for fp16), which alone exceeds the first term on outliers 4 x rms wide."""
+def _check(y, ref, tol=TOL, what=""):
+    """max |y - ref| <= tol x rms(ref); prints the measured ratio."""
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     assert np.isfinite(y).all(), what
     rms = np.sqrt((ref ** 2).mean())
-    excess = np.abs(y - ref) - out_rel * np.abs(ref)
-    err = excess.max()
-    assert err <= tol * rms, f"{what}: max abs err {err:.3e} (beyond output rounding) > {tol} x rms {rms:.3e}"
+    err = np.abs(y - ref).max()
+    print(f"\n{what}: max|err|/rms {err / rms:.3e}")
+    assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
 
 
 def _upload(pkg, dev, q8, n, k):
@@ -202,8 +201,7 @@ def test_single_persistent_staged_epilogue(pkg, oracle, cuda, m, n, k, n_off, cn
     rows = np.unique(np.concatenate([np.linspace(0, m - 1, 96).astype(int), np.arange(m - 40, m)]))
     res = res_t.float().cpu().numpy()
     ref = oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], act)
-    _check(got[rows], ref, what=f"staged {m}x{n}x{k} window {n_off}+{cnt} act {act} {out_dtype}",
-           out_rel=2.0 ** -8 if out_dtype == torch.bfloat16 else 2.0 ** -11)
+    _check(got[rows], ref, what=f"staged {m}x{n}x{k} window {n_off}+{cnt} act {act} {out_dtype}")
     if pad:
         assert bool((buf[:, cnt:] == 7.0).all()), "the padding columns were written"
 
@@ -359,3 +357,33 @@ def test_fused_linear_cache_never_serves_a_freed_buffer(pkg, oracle, cuda):
         y = pkg.fused_linear(xt, packed, (n, k), 8).float().cpu().numpy()
         _check(y, oracle.gemm_q8(x, q8, np.zeros(n, np.float32), n, k), what=f"trial {trial}")
         del packed
+
+
+@pytest.mark.parametrize("m,n,k,n_off,cnt,act,res,out_dtype",
+                         [(1, 256, 1024, 0, 256, 0, 0, torch.float32), (37, 384, 256, 0, 384, 0, 0, torch.float32),
+                          (256, 4096, 1024, 0, 4096, 0, 0, torch.float32), (70, 300, 96, 128, 100, 0, 1, torch.float32),
+                          (33, 256, 512, 0, 256, 1, 1, torch.float32), (45, 128, 64, 0, 128, 0, 0, torch.bfloat16)])
+def test_int8_activation_gemm_matches_the_oracle(pkg, oracle, cuda, m, n, k, n_off, cnt, act, res, out_dtype):
+    """Q8Weight.int8act (the reference's set_quant_kernel(1) kernel, src/kernels.cpp:368-479) on fp32 activations
+    against the oracle restatement pinned to the compiled reference: bit for bit for fp32 outputs without an
+    activation; the erf GELU (CUDA erff against the reference's polynomial) and bf16 outputs within 2e-2 x rms."""
+    from idol_b200.block import Q8Weight
+    rng = np.random.default_rng(m + n + k)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+    x = rng.normal(0, 1, (m, k)).astype(np.float32)
+    x[0, :32] = 0.0
+    b = rng.normal(0, 0.01, n).astype(np.float32)
+    r = rng.normal(0, 1, (m, cnt)).astype(np.float32) if res else None
+    ref = oracle.gemm_q8_int8act(x, q8, b, n, k, n_off, cnt, r, act)
+    w = Q8Weight(torch.from_numpy(q8.reshape(-1)).to(cuda), n, k, torch.from_numpy(b))
+    rt = None if r is None else torch.from_numpy(r).to(cuda, out_dtype)
+    y = w.int8act(torch.from_numpy(x).to(cuda), act=act, residual=rt, out_dtype=out_dtype, cols=(n_off, cnt))
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    if act == 0 and out_dtype == torch.float32:
+        assert np.array_equal(got, ref), f"max abs diff {np.abs(got - ref).max()}"
+    else:
+        if out_dtype != torch.float32 and r is not None:
+            ref = oracle.gemm_q8_int8act(x, q8, b, n, k, n_off, cnt, oracle.f32_to_bf16_round(r), act)
+        _check(got, ref, what=f"int8act act={act} {out_dtype}")
+    assert pkg._capi.device_status(0) == 0
