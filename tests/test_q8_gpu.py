@@ -31,6 +31,22 @@ def _check(y, ref, tol=TOL, what=""):
     assert err <= tol * rms, f"{what}: max abs err {err:.3e} > {tol} x rms {rms:.3e}"
 
 
+def _check_2byte_out(y, ref, out_dtype, what=""):
+    """For a bf16 (or fp16) output: max |y - ref| <= 2e-2 x rms(ref) beyond half a rounding step of the stored
+    element. The stored value's own rounding, half a bf16 ulp (2^-9 of its binade), is up to 0.8% of the RMS at the
+    outliers 4-5 x rms wide on its own, on top of the GEMM's bf16-operand error; the same launches with an fp16 or
+    fp32 output meet the plain bar. The plain ratio is printed beside it."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.isfinite(y).all(), what
+    rms = np.sqrt((ref ** 2).mean())
+    bits = 7 if out_dtype == torch.bfloat16 else 10
+    half_step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - bits - 1)
+    err = np.abs(y - ref)
+    print(f"\n{what}: max|err|/rms {err.max() / rms:.3e}; beyond half a rounding step {(err - half_step).max() / rms:.3e}")
+    assert (err - half_step).max() <= TOL * rms, f"{what}: error beyond output rounding > {TOL} x rms"
+
+
 def _upload(pkg, dev, q8, n, k):
     packed = torch.from_numpy(np.ascontiguousarray(q8).reshape(-1)).to(dev)
     return pkg.repack(packed, n, k)
@@ -201,7 +217,11 @@ def test_single_persistent_staged_epilogue(pkg, oracle, cuda, m, n, k, n_off, cn
     rows = np.unique(np.concatenate([np.linspace(0, m - 1, 96).astype(int), np.arange(m - 40, m)]))
     res = res_t.float().cpu().numpy()
     ref = oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], act)
-    _check(got[rows], ref, what=f"staged {m}x{n}x{k} window {n_off}+{cnt} act {act} {out_dtype}")
+    what = f"staged {m}x{n}x{k} window {n_off}+{cnt} act {act} {out_dtype}"
+    if out_dtype == torch.bfloat16:
+        _check_2byte_out(got[rows], ref, out_dtype, what=what)
+    else:
+        _check(got[rows], ref, what=what)
     if pad:
         assert bool((buf[:, cnt:] == 7.0).all()), "the padding columns were written"
 
