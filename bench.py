@@ -862,6 +862,35 @@ def run_profile_shape(args):
     import torch
     import __graft_entry__
     pkg = __graft_entry__.load_package()
+    if args.profile_shape in ("attention", "stack"):
+        # The config-5 chunk (8 sequences x 4096 tokens): the attention kernel alone, or one pass of the 24-block
+        # stack over the chunk, warmup + steps times.
+        dev = torch.device("cuda", 0)
+        seqs = CHUNK_IMAGES * CFG
+        if args.profile_shape == "attention":
+            from idol_b200 import layers
+            g = torch.Generator(device=dev).manual_seed(3)
+            D = BLOCK_D
+            qkv = torch.randn((seqs * BLOCK_TOKENS, 3 * D), device=dev, generator=g).to(torch.bfloat16)
+            out = torch.empty((seqs * BLOCK_TOKENS, D), device=dev, dtype=torch.bfloat16)
+            fn = lambda: layers.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], BLOCK_HEADS,  # noqa: E731
+                                          batch=seqs, out=out)
+        else:
+            stack = make_stack(dev)
+            x = make_images(dev, 0, CHUNK_IMAGES)
+            fn = lambda: stack.forward_(x, seqs)  # noqa: E731
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile": args.profile_shape, "ms_per_step": round(e0.elapsed_time(e1) / args.steps, 3),
+                          "device_status": pkg._capi.device_status(0)}))
+        return
     if args.profile_shape in ("block", "mlp"):
         dev = torch.device("cuda", 0)
         stream = torch.cuda.Stream(device=dev)
@@ -1099,7 +1128,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="only the config-5 stack (no sweep or compositions)")
     ap.add_argument("--profile-shape", default=None,
                     help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture; 'block' or 'mlp' "
-                         "runs the config-3 block or the config-4 MLP instead")
+                         "runs the config-3 block or the config-4 MLP instead, 'attention' or 'stack' the attention "
+                         "kernel or the 24-block stack on one config-5 chunk")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
