@@ -955,7 +955,8 @@ int q8_gemm(const GemmCall& c) {
                                     (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
     // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator, a 2-byte output leaving
     // through a staging tile and TMA stores): measured on B200 it pays at K <= 1024 once the 192-token tiles number
-    // eight or more per SM (M = 16384, K = 1024: 864 -> 910 TFLOP/s at N = 3072, 900 -> 930 at N = 4096). An fp32
+    // 4.5 or more per SM (M = 16384, K = 1024: 864 -> 910 TFLOP/s at N = 3072, 900 -> 930 at N = 4096; 4096 x 1024 x
+    // 4096, 4.75 tiles per SM: 736 -> 770; 4096 x 1024 x 3072, 3.6 per SM: 711 -> 681, so not there). An fp32
     // output (the residual-stream projections) leaves it by direct stores and pays from four tiles per SM, since its
     // epilogue's reads and writes of the fp32 stream then run under the next tile's main loop (16384 x 1024 x 1024
     // with the residual: 81.6 -> 69.8 us); 2-byte direct stores, fewer tiles or longer K (16384 x 4096 x 1024 with
@@ -966,7 +967,7 @@ int q8_gemm(const GemmCall& c) {
     const bool persist1 = q8 && !pair && bn >= 256 &&
                           (forced_persist == 1 ||
                            (forced_persist != 0 && (staged || c.y_dtype == IDOL_F32) && p.stages_total <= 16 &&
-                            tiles192 >= (staged ? 8LL : 4LL) * num_sms(w.device)));
+                            2 * tiles192 >= (staged ? 9LL : 8LL) * num_sms(w.device)));
     if (pair || persist1) {
         const int kind = pair ? 0 : 1;
         const int pbn = kind == 1 ? 192 : bn >= 256 ? 192 : 128;  // two accumulators fit TMEM beside the A slots
