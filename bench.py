@@ -52,7 +52,7 @@ BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOC
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
 STACK_BLOCKS, STACK_IMAGES, CFG = 24, 64, 2
 CHUNK_IMAGES = 4  # images per pass through the blocks (8 sequences, 32768 rows)
-LAUNCHES_PER_BLOCK = 8  # norm, qkv, rms_heads of q and k, attention, out + residual, norm, ff1, ff2 + residual
+LAUNCHES_PER_BLOCK = 7  # norm, qkv with the q/k norm fused, attention, out + residual, norm, ff1, ff2 + residual
 METRIC = "denoiser-block steps/s (config 5: 24-block stack over 64 images x 2 CFG branches, sharded by image)"
 UNIT = "block-steps/s"
 
@@ -562,14 +562,11 @@ def block_kernel_times(block, dev, stream, seqs):
     f1 = torch.empty((rows, H), device=dev, dtype=torch.bfloat16)
     att = torch.empty((rows, D), device=dev, dtype=torch.bfloat16)
     qkv_w(h, out=qkv)
-    qk_gamma = torch.cat([block.q_gamma, block.k_gamma])  # the same launch as the block's fused q/k rms_heads
-    layers.rms_heads_(qkv[:, :2 * D], 2 * BLOCK_HEADS, qk_gamma)
     ff1_w(h, act=C.ACT_GELU_TANH, out=f1)
     kernels = [
         ("norm_rows (fp32 -> bf16)", 2, lambda: layers.norm_rows(x, 1e-6, out=h), "hbm", rows * D * (4 + 2)),
-        ("q8_gemm qkv 1024->3072", 1, lambda: qkv_w(h, out=qkv), "tensor", 2.0 * rows * 3 * D * D),
-        ("rms_heads (q and k)", 1, lambda: layers.rms_heads_(qkv[:, :2 * D], 2 * BLOCK_HEADS, qk_gamma), "hbm",
-         rows * 2 * D * 2 * 2),
+        ("q8_gemm qkv 1024->3072 + rms_heads of q, k", 1,
+         lambda: qkv_w.heads(h, 2 * D, D, block.q_gamma, block.k_gamma, out=qkv), "tensor", 2.0 * rows * 3 * D * D),
         ("attention", 1, lambda: layers.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], BLOCK_HEADS,
                                                   batch=seqs, out=att), "tensor",
          4.0 * BLOCK_TOKENS ** 2 * D * seqs),

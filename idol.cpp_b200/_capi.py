@@ -44,6 +44,7 @@ SIGNATURES = {
     "idol_b200_q8_export": (_i32, [_vp, _vp, _i64, _vp]),
     "idol_b200_q8_gemm": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _vp, _i64, _i32, _i32, _vp, _i32, _i64,
                                  _vp]),
+    "idol_b200_q8_gemm_heads": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _i32, _i32, _vp, _vp, _vp]),
     "idol_b200_q8_gemm_int8act_workspace_bytes": (_i64, [_i64, _i32]),
     "idol_b200_q8_gemm_int8act": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _vp, _i64, _i32, _vp, _i32, _i64,
                                          _vp, _i64, _vp]),

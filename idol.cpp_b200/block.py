@@ -61,6 +61,22 @@ class Q8Weight:
                                           _DTYPES[out.dtype], out.stride(0), _stream(x.device)))
         return out
 
+    def heads(self, x: torch.Tensor, head_cols: int, head_split: int, gamma_a: torch.Tensor,
+              gamma_b: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """bf16 y = x W^T + b, then rms_heads of columns [0, head_split) with gamma_a and [head_split, head_cols) with
+        gamma_b (src/decoders.cpp:234-237, 298-300), the norm fused into the GEMM's epilogue where it can be."""
+        x2 = x if (x.stride(-1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
+        if x2.dtype != torch.bfloat16:
+            raise ValueError("Q8Weight.heads: x must be bf16")
+        if out is None:
+            out = torch.empty((x2.shape[0], self.out), dtype=torch.bfloat16, device=x.device)
+        ga = gamma_a.detach().to(device=x.device, dtype=torch.float32).contiguous()
+        gb = None if gamma_b is None else gamma_b.detach().to(device=x.device, dtype=torch.float32).contiguous()
+        C.check(C.lib().idol_b200_q8_gemm_heads(ctypes.c_void_p(self.handle), _ptr(x2), x2.shape[0], x2.stride(0),
+                                                _ptr(out), out.stride(0), head_cols, head_split, _ptr(ga), _ptr(gb),
+                                                _stream(x.device)))
+        return out
+
     def int8act(self, x: torch.Tensor, act: int = C.ACT_NONE, residual: Optional[torch.Tensor] = None,
                 out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
                 cols: Optional[tuple] = None) -> torch.Tensor:

@@ -332,6 +332,18 @@ int gemm(const idol_q8_matrix* w, const void* x, int64_t m, int64_t ldx, const v
     return idol::q8_gemm(c);
 }
 
+// A projection into bf16 followed by rms_heads (src/decoders.cpp:74-86) of its first `cols` columns: [0, split) with
+// gamma_a, [split, cols) with gamma_b. The norm runs in the GEMM's epilogue where it can, else right after it.
+int gemm_heads(const idol_q8_matrix* w, const void* x, int64_t m, int64_t ldx, void* y, int64_t ldy, int cols, int split,
+               const float* gamma_a, const float* gamma_b, cudaStream_t s) {
+    idol::GemmCall c = {&w->m, x, IDOL_BF16, m, ldx, 0, w->m.n, nullptr, 0, IDOL_ACT_NONE, 0, y, IDOL_BF16, ldy, s};
+    c.head_gamma_a = gamma_a;
+    c.head_gamma_b = gamma_b;
+    c.head_cols = cols;
+    c.head_split = split;
+    return idol::q8_gemm(c);
+}
+
 }  // namespace
 
 extern "C" {
@@ -385,9 +397,8 @@ int idol_b200_block_forward(const idol_block* b, void* x, int x_dtype, int64_t t
 
     IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
                                      nullptr, s));
-    int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
+    int rc = gemm_heads(b->qkv, h, rows, D, big, 3 * D, 2 * D, D, b->q_gamma, b->k_gamma, s);  // with rms q, k
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(idol::launch_rms_heads_qk(big, 3 * D, rows, b->heads, b->q_gamma, b->k_gamma, s));
     idol::AttentionCall ac = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
     rc = idol::attention(ac);
     if (rc != IDOL_OK) return rc;
@@ -469,9 +480,8 @@ int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int
     // Self-attention sublayer.
     IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, nullptr, nullptr, nullptr,
                                      nullptr, s));
-    int rc = gemm(b->qkv, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, 3 * D, s);
+    int rc = gemm_heads(b->qkv, h, rows, D, big, 3 * D, 2 * D, D, b->q_gamma, b->k_gamma, s);  // with rms q, k
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(idol::launch_rms_heads_qk(big, 3 * D, rows, b->heads, b->q_gamma, b->k_gamma, s));
     idol::AttentionCall sa = {big, big + D, big + 2 * D, h, tokens, tokens, 3 * D, 3 * D, D, b->heads, 64, images, s};
     rc = idol::attention(sa);
     if (rc != IDOL_OK) return rc;
@@ -481,9 +491,8 @@ int idol_b200_gs_block_forward(const idol_gs_block* g, void* x, int x_dtype, int
     // Cross-attention sublayer (src/decoders.cpp:304-306, 232-240).
     IDOL_CUDA(idol::launch_norm_rows(x, x_dtype, D, h, IDOL_BF16, D, rows, D, b->eps, g->norm2_gamma, g->norm2_beta,
                                      nullptr, nullptr, s));
-    rc = gemm(g->cross_q, h, rows, D, nullptr, 0, IDOL_ACT_NONE, big, IDOL_BF16, D, s);
+    rc = gemm_heads(g->cross_q, h, rows, D, big, D, D, D, g->cq_gamma, nullptr, s);  // with rms q
     if (rc != IDOL_OK) return rc;
-    IDOL_CUDA(idol::launch_rms_heads(big, IDOL_BF16, D, rows, b->heads, g->cq_gamma, s));
     // to_kv of the condition rows with the key half's rms_heads fused in.
     IDOL_CUDA(idol::launch_kv_project(cond, crows, g->cond_dim, g->kv_w, g->kv_b, 2 * D, kv, s, g->ck_gamma,
                                       b->heads));

@@ -350,6 +350,21 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
     return idol::q8_gemm(c);
 }
 
+int idol_b200_q8_gemm_heads(const idol_q8_matrix* matrix, const void* x, int64_t m, int64_t ldx, void* y, int64_t ldy,
+                            int head_cols, int head_split, const float* gamma_a, const float* gamma_b, void* stream) {
+    if (!matrix) return fail(IDOL_ERR_INVALID, "q8_gemm_heads: matrix is NULL");
+    if (m > 0 && (!x || !y)) return fail(IDOL_ERR_INVALID, "q8_gemm_heads: NULL pointer");
+    if (head_cols < 1) return fail(IDOL_ERR_INVALID, "q8_gemm_heads: head_cols must be >= 64");
+    IDOL_CUDA(cudaSetDevice(matrix->m.device));
+    idol::GemmCall c = {&matrix->m, x, IDOL_BF16, m, ldx, 0, matrix->m.n, nullptr, 0, IDOL_ACT_NONE, 0, y, IDOL_BF16,
+                        ldy, static_cast<cudaStream_t>(stream)};
+    c.head_gamma_a = gamma_a;
+    c.head_gamma_b = gamma_b;
+    c.head_cols = head_cols;
+    c.head_split = head_split;
+    return idol::q8_gemm(c);
+}
+
 int64_t idol_b200_q8_gemm_int8act_workspace_bytes(int64_t m, int in) { return idol::int8act_workspace_bytes(m, in); }
 
 int idol_b200_q8_gemm_int8act(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx,

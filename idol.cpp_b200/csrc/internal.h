@@ -83,6 +83,12 @@ struct GemmCall {
     int y_dtype;
     int64_t ldy;
     cudaStream_t stream;
+    // Optional rms_heads of the output (bf16 or f16, window starting at column 0, no activation or residual):
+    // columns [0, head_split) with head_gamma_a, [head_split, head_cols) with head_gamma_b, heads of 64. Fused into
+    // the epilogue where the GEMM leaves through a staging tile, else a separate launch right after it.
+    const float* head_gamma_a = nullptr;
+    const float* head_gamma_b = nullptr;
+    int head_cols = 0, head_split = 0;
 };
 int q8_gemm(const GemmCall& c);
 // The integer-activation form of the same linear (q8_int8act.cu): flags unused; workspace for the quantized

@@ -28,6 +28,11 @@ struct Params {
     int bias_after_round;
     int stages_per_split, stages_total;
     int y_tma;                // the output tensor map may be used for TMA stores (2-byte output, aligned rows)
+    // Per-head norm of the stored output (src/decoders.cpp:74-86 rms_heads, head dim 64) applied in the staged
+    // epilogue: columns [0, hn_split) with hn_gamma_a, [hn_split, hn_cols) with hn_gamma_b; hn_cols = 0: none.
+    const float* hn_gamma_a;
+    const float* hn_gamma_b;
+    int hn_cols, hn_split;
 };
 
 template <typename OutT>

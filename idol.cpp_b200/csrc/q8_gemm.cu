@@ -460,7 +460,7 @@ struct ConfigPersistent {
     static constexpr int kACol0 = 2 * BN;  // accumulators at columns 0 and BN, then the A slots
     static constexpr int kColsNeeded = kACol0 + SA * 32;
     static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
-    static constexpr int kBarBytes = 8 * (3 * S + SA + 6) + 16;
+    static constexpr int kBarBytes = 8 * (3 * S + SA + 7) + 16;
     static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
     // Dequant groups alternate by stage parity: an even SA keeps each A slot (afull) with one group; an odd S needs
     // the A-slot wait (SA < S) to order the parity waits on a stage slot the two groups share.
@@ -488,6 +488,53 @@ struct PersistentSchedule {
 // staging tile and one TMA store (`ymap`: the output window [n_count features x M tokens]) instead of 96 global
 // stores per lane; the store issuer (epilogue warp 0, lane 0) reports the staging tile free again on sfree once the
 // store has read it.
+// rms_heads (src/decoders.cpp:74-86, head dim 64) of a staged tile in place: BN token rows of 128 features (two heads,
+// 256 bytes per token), features tile_row0 .. tile_row0 + 127 of the output. Eight lanes take one (token, head) row,
+// eight features each, with the reduction of rms_heads_vec_kernel (norms.cu), so a head gets the same bits as that
+// kernel gives the stored row. The epilogue warps share the BN x 2 rows round-robin (BN x 2 is a multiple of 32, so
+// every lane of a warp runs the same iterations); rows past M hold stale values and are normalised too: the TMA store
+// clips them.
+template <int BN>
+__device__ __forceinline__ void head_norm_staged(uint8_t* ys, int tile_row0, const Params& p, int ew, int lane) {
+    static_assert((BN * 2) % (4 * kEpilogueWarps) == 0, "whole rounds of (token, head) rows");
+    const int l8 = lane % 8;
+    for (int task = ew * 4 + lane / 8; task < BN * 2; task += 4 * kEpilogueWarps) {
+        const int tok = task / 2, hh = task % 2;
+        const uint32_t addr = smem_u32(ys) + (uint32_t)(tok * 256 + hh * 128 + l8 * 16);
+        uint4 raw;
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w) : "r"(addr));
+        const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(pr[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float mult = 8.0f / fmaxf(sqrtf(ss), 1e-12f);  // sqrt(64) = 8
+        const int f0 = tile_row0 + hh * 64 + l8 * 8;
+        const float* g = f0 < p.hn_split ? p.hn_gamma_a + f0 : p.hn_gamma_b + (f0 - p.hn_split);
+        const float4 g0 = *reinterpret_cast<const float4*>(g), g1 = *reinterpret_cast<const float4*>(g + 4);
+        const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 o2 =
+                __floats2bfloat162_rn(v[2 * i] * mult * gg[2 * i], v[2 * i + 1] * mult * gg[2 * i + 1]);
+            o[i] = *reinterpret_cast<const uint32_t*>(&o2);
+        }
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[0]), "r"(o[1]), "r"(o[2]),
+                     "r"(o[3])
+                     : "memory");
+    }
+}
+
 template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage>
 __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap, const Params p,
@@ -509,7 +556,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     uint64_t* accempty = accfull + 2;                                               // even CTA: accumulator b drained
     uint64_t* sfull = accempty + 2;                                                 // staging tile written
     uint64_t* sfree = sfull + 1;                                                    // staging tile read by TMA
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sfree + 1);
+    uint64_t* snorm = sfree + 1;                                                    // staged heads normalised
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(snorm + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -533,6 +581,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
         }
         mbar_init(sfull, kEpilogueWarps);  // one arrival per epilogue warp once its share of the staging tile is in
         mbar_init(sfree, 1);               // the store issuer, once the TMA store has read the staging tile
+        mbar_init(snorm, kEpilogueWarps);  // one arrival per epilogue warp once its share of the heads is normalised
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -676,6 +725,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
         constexpr int kHalfCols = BN / 2;
         int lt = 0;
         int ns = 0;  // TMA stores issued so far (staged tiles)
+        int nh = 0;  // staged tiles whose heads were normalised
         for (int t = pair_id; t < total_tiles; t += num_pairs, ++lt) {
             const int b = lt & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&accfull[b], (lt >> 1) & 1, abort_flag));
@@ -718,10 +768,21 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                     mbar_arrive(&accempty[b]);
                     mbar_arrive(sfull);
                 }
+                // rms_heads of the staged tile (tiles lie wholly inside or outside [0, hn_cols): hn_cols is a
+                // multiple of 128): every epilogue warp waits for the whole tile, normalises its share of the
+                // (token, head) rows in place and reports on snorm, which the store then waits for instead of sfull.
+                const bool hn = tile_row0 < p.hn_cols;
+                if (hn) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(sfull, ns & 1, abort_flag))) break;
+                    head_norm_staged<BN>(ys, tile_row0, p, ew, lane);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(snorm);
+                }
                 if (ew == 0) {
                     bool stored = true;
                     if (lane == 0) {
-                        stored = mbar_wait(sfull, ns & 1, abort_flag);
+                        stored = mbar_wait(hn ? snorm : sfull, (hn ? nh : ns) & 1, abort_flag);
                         if (stored) {
                             tma_store_2d(&ymap, ys, tile_row0 - p.n_offset, m0);
                             bulk_commit_group();
@@ -733,6 +794,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                     if (!__shfl_sync(0xffffffffu, stored ? 1 : 0, 0)) break;
                 }
                 ++ns;
+                nh += hn ? 1 : 0;
             } else {
                 epilogue_span<OutT, kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
                 tc_fence_before();
@@ -895,7 +957,7 @@ static void choose_tiles(int device, int64_t m, int tiles_n, int stages_total, i
     *splits = s;
 }
 
-int q8_gemm(const GemmCall& c) {
+static int q8_gemm_impl(const GemmCall& c, bool* head_norm_fused) {
     const Q8Matrix& w = *c.w;
     if (c.m < 0 || c.m > 0x7fffffff) return fail(IDOL_ERR_INVALID, "q8_gemm: m out of range");
     if (c.n < 0 || c.n_offset < 0 || c.n_offset + c.n > w.n) return fail(IDOL_ERR_INVALID, "q8_gemm: column window");
@@ -998,6 +1060,13 @@ int q8_gemm(const GemmCall& c) {
             else
                 ymap = xmap;
         }
+        if (head_norm_fused && p.y_tma && c.y_dtype == IDOL_BF16) {
+            p.hn_gamma_a = c.head_gamma_a;
+            p.hn_gamma_b = c.head_gamma_b;
+            p.hn_cols = c.head_cols;
+            p.hn_split = c.head_split;
+            *head_norm_fused = true;
+        }
         const bool bf16 = c.x_dtype == IDOL_BF16;
         if (c.y_dtype == IDOL_F32)
             return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
@@ -1030,6 +1099,30 @@ int q8_gemm(const GemmCall& c) {
                     : dispatch<false, __nv_bfloat16>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
     return bf16 ? dispatch<true, __half>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream)
                 : dispatch<false, __half>(w.format, bn, xmap, p, tiles_n, tiles_m, splits, c.stream);
+}
+
+int q8_gemm(const GemmCall& c) {
+    if (c.head_cols <= 0) return q8_gemm_impl(c, nullptr);
+    if (c.y_dtype != IDOL_BF16 || c.n_offset != 0 || c.act != IDOL_ACT_NONE || c.residual || c.head_cols % 64 ||
+        c.head_split % 64 || c.head_split > c.head_cols || c.head_cols > c.n || !c.head_gamma_a ||
+        (c.head_split < c.head_cols && !c.head_gamma_b))
+        return fail(IDOL_ERR_INVALID, "q8_gemm: per-head norm wants a bf16 output from column 0 without activation or "
+                                      "residual, whole 64-wide heads and its gammas");
+    // Fused only when the normalised columns are whole 128-row tiles of the staged epilogue.
+    bool fused = false;
+    const int rc = q8_gemm_impl(c, c.head_cols % 128 == 0 ? &fused : nullptr);
+    if (rc != IDOL_OK || fused || c.m == 0) return rc;
+    // The GEMM left through direct stores: the norm runs as its own launch on the stored rows.
+    if (c.head_split * 2 == c.head_cols)
+        IDOL_CUDA(launch_rms_heads_qk(c.y, c.ldy, c.m, c.head_split / 64, c.head_gamma_a, c.head_gamma_b, c.stream));
+    else {
+        if (c.head_split > 0)
+            IDOL_CUDA(launch_rms_heads(c.y, IDOL_BF16, c.ldy, c.m, c.head_split / 64, c.head_gamma_a, c.stream));
+        if (c.head_cols > c.head_split)
+            IDOL_CUDA(launch_rms_heads(static_cast<__nv_bfloat16*>(c.y) + c.head_split, IDOL_BF16, c.ldy, c.m,
+                                       (c.head_cols - c.head_split) / 64, c.head_gamma_b, c.stream));
+    }
+    return IDOL_OK;
 }
 
 }  // namespace idol

@@ -141,6 +141,15 @@ int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, 
                       int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
                       void* stream);
 
+/* A projection followed by the per-head norm of its first head_cols output columns, as the decoders run them
+ * (src/decoders.cpp:234-237 and :298-300: gemm_packed, then rms_heads of q and of k): y[m, 0:n] = bf16(x . W^T + bias),
+ * then columns [0, head_split) normalised per 64-wide head with gamma_a and [head_split, head_cols) with gamma_b
+ * (x * 8 / max(|x|, 1e-12) * gamma on the stored bf16 row). The norm runs in the GEMM's epilogue when the GEMM leaves
+ * through its staging tile and head_cols is a multiple of 128, else as a launch right after it; the result is the
+ * same bits either way. y: bf16, rows ldy apart. gamma_b may be NULL when head_split == head_cols. */
+int idol_b200_q8_gemm_heads(const idol_q8_matrix* matrix, const void* x, int64_t m, int64_t ldx, void* y, int64_t ldy,
+                            int head_cols, int head_split, const float* gamma_a, const float* gamma_b, void* stream);
+
 /* The same linear on integer activations: the reference's second CPU kernel (src/kernels.cpp:368-479,
  * quantize_activations + vnni_task + gemm_quant_int8, chosen there by set_quant_kernel(1)), bit for bit on Q8_0
  * matrices. x (IDOL_F32, IDOL_BF16 or IDOL_F16, rows ldx apart) is quantized per (row, 32-deep group) to int8 with

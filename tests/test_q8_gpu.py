@@ -407,3 +407,26 @@ def test_int8_activation_gemm_matches_the_oracle(pkg, oracle, cuda, m, n, k, n_o
             ref = oracle.gemm_q8_int8act(x, q8, b, n, k, n_off, cnt, oracle.f32_to_bf16_round(r), act)
         _check(got, ref, what=f"int8act act={act} {out_dtype}")
     assert pkg._capi.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,dim,both", [(16384, 1024, True), (16384, 1024, False), (300, 1024, True), (777, 192, True),
+                                        (5000, 256, True)])
+def test_projection_with_head_norm_equals_gemm_then_rms_heads(pkg, cuda, m, dim, both):
+    """Q8Weight.heads (the norm fused into the staged epilogue where the GEMM leaves through it, else launched after
+    it) gives the same bits as the GEMM followed by rms_heads (src/decoders.cpp:234-237)."""
+    from idol_b200 import layers
+    from idol_b200.block import Q8Weight
+    g = torch.Generator(device=cuda).manual_seed(m + dim)
+    n = 3 * dim
+    w = Q8Weight.from_float(torch.randn((n, dim), device=cuda, generator=g) * 0.02,
+                            torch.randn(n, device=cuda, generator=g) * 0.01)
+    x = torch.randn((m, dim), device=cuda, generator=g).to(torch.bfloat16)
+    ga = 1 + 0.1 * torch.randn(dim, device=cuda, generator=g)
+    gb = 1 + 0.1 * torch.randn(dim, device=cuda, generator=g)
+    cols = 2 * dim if both else dim
+    got = w.heads(x, cols, dim, ga, gb if both else None)
+    ref = w(x)
+    layers.rms_heads_(ref[:, :cols], cols // 64, torch.cat([ga, gb]) if both else ga)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref), f"max abs diff {(got.float() - ref.float()).abs().max().item()}"
+    assert pkg._capi.device_status(0) == 0
