@@ -91,7 +91,7 @@ def peaks():
 def cpu_info():
     """Host facts for the CPU baseline: model, usable logical CPUs, physical cores, nominal clock, and the fp32 FMA
     peak of the AVX2 units (physical cores x GHz x 32 FLOP per cycle: two 8-wide FMA pipes)."""
-    model, phys, cur = "unknown", set(), {}
+    model, phys, cur, flags = "unknown", set(), {}, set()
     try:
         for line in Path("/proc/cpuinfo").read_text().splitlines() + [""]:
             if not line.strip():
@@ -103,6 +103,8 @@ def cpu_info():
             cur[key.strip()] = val.strip()
             if key.strip() == "model name":
                 model = val.strip()
+            if key.strip() == "flags":
+                flags = set(val.split())
     except OSError:
         pass
     logical = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
@@ -119,7 +121,7 @@ def cpu_info():
             if mhz:
                 ghz, source = max(mhz) / 1e3, "cpu MHz"
     return {"model": model, "logical_cpus": logical, "physical_cores": physical, "ghz": ghz, "ghz_source": source,
-            "avx2_fma_peak_gflops": round(physical * ghz * 32, 1) if ghz else None}
+            "avx2_fma_peak_gflops": round(physical * ghz * 32, 1) if ghz else None, "flags": flags}
 
 
 def cpu_reference_runner():
@@ -154,6 +156,18 @@ def cpu_reference_runner():
         dt = time.perf_counter() - t0
         return sample_flops / unit_flops / dt, dt
 
+    def vnni_step():
+        """The same block with the reference's integer-activation kernel (set_quant_kernel(1), its default on CPUs
+        with AVX-VNNI); None where the host lacks AVX-VNNI or the reference library is absent."""
+        if kind != "reference" or "avx_vnni" not in info.get("flags", ()):
+            return None
+        x = x0.copy()
+        t0 = time.perf_counter()
+        blk.forward_(x, images=CFG, mode=1)
+        return sample_flops / unit_flops / (time.perf_counter() - t0)
+
+    step.vnni = vnni_step
+
     facts = dict(info, kind=kind, threads=threads,
                  sample=(f"one block-step: one image (2 CFG branches x {tokens} tokens, D 1024) through one block on "
                          + ("the reference's compiled CPU functions, OpenMP" if kind == "reference" else
@@ -170,7 +184,10 @@ def cpu_baseline_entry(rates, times, facts):
             "cpu_model": facts["model"], "physical_cores": facts["physical_cores"],
             "omp_threads": facts["threads"], "ghz": facts["ghz"], "ghz_source": facts["ghz_source"],
             "gflops": round(gflops, 1),
-            "avx2_fma_peak_gflops": peak, "frac_of_avx2_peak": round(gflops / peak, 3) if peak else None}
+            "avx2_fma_peak_gflops": peak, "frac_of_avx2_peak": round(gflops / peak, 3) if peak else None,
+            "vnni_kernel_value": facts.get("vnni"),
+            "vnni_kernel": "the same block with the reference's integer-activation GEMMs (set_quant_kernel(1), its "
+                           "default where AVX-VNNI exists; null when the host lacks it)"}
 
 
 def cpu_reference_measure(warmup, steps, budget_s=150.0):
@@ -185,6 +202,8 @@ def cpu_reference_measure(warmup, steps, budget_s=150.0):
         r, t = step()
         rates.append(r)
         times.append(t)
+    vnni = [v for v in (step.vnni() for _ in range(min(3, timed))) if v is not None]
+    facts["vnni"] = round(statistics.median(vnni), 4) if vnni else None
     return rates, times, facts
 
 

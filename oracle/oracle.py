@@ -462,14 +462,15 @@ class RefBlock:
         self.qg, self.kg = c32(layers["q_gamma"]), c32(layers["k_gamma"])
         self.heads, self.eps = heads, eps
 
-    def forward_(self, x, images=1):
-        """In place on x: [images * L, D] fp32 C-contiguous."""
+    def forward_(self, x, images=1, mode=0):
+        """In place on x: [images * L, D] fp32 C-contiguous. mode 0: the float GEMM kernel (production), 1: the
+        integer-activation kernel."""
         R = ref()
         rows, D = x.shape
         hd, L = D // self.heads, rows // images
         h = np.empty_like(x)
         R.ref_norm_rows(_ptr(x), _ptr(h), rows, D, self.eps, None, None, None, None)
-        qkv = self.lin["qkv"].gemm(h)
+        qkv = self.lin["qkv"].gemm(h, mode=mode)
         R.ref_rms_heads(_ptr(qkv), rows, 3 * D, self.heads, hd, _ptr(self.qg))
         R.ref_rms_heads(ctypes.cast(qkv.ctypes.data + 4 * D, _f32p), rows, 3 * D, self.heads, hd, _ptr(self.kg))
         a = np.empty((rows, D), np.float32)
@@ -478,11 +479,11 @@ class RefBlock:
             R.ref_attention(ctypes.cast(base, _f32p), L, 3 * D, ctypes.cast(base + 4 * D, _f32p),
                             ctypes.cast(base + 8 * D, _f32p), L, 3 * D, self.heads, hd,
                             ctypes.cast(a.ctypes.data + 4 * i * L * D, _f32p), D)
-        x[:] = self.lin["out"].gemm(a, residual=x)
+        x[:] = self.lin["out"].gemm(a, residual=x, mode=mode)
         R.ref_norm_rows(_ptr(x), _ptr(h), rows, D, self.eps, None, None, None, None)
-        f = self.lin["ff1"].gemm(h)
+        f = self.lin["ff1"].gemm(h, mode=mode)
         R.ref_gelu_tanh(_ptr(f), f.size)
-        x[:] = self.lin["ff2"].gemm(f, residual=x)
+        x[:] = self.lin["ff2"].gemm(f, residual=x, mode=mode)
         return x
 
 

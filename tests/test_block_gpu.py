@@ -239,3 +239,29 @@ def test_block_workspace_and_errors(pkg, oracle, cuda):
 def test_compositions_no_timeout(pkg, cuda):
     torch.cuda.synchronize()
     assert pkg._capi.device_status(0) == 0
+
+
+def test_denoiser_stack_chunks_equal_block_by_block(pkg, oracle, cuda):
+    """DenoiserStack (config 5) over 3 images x 2 CFG branches of 512 tokens: any chunking of the sequences gives the
+    same bits as running the blocks one after another over all sequences (each sequence attends only within itself,
+    rows are independent elsewhere), and the stack's first block matches the oracle composition."""
+    from idol_b200.block import DenoiserStack
+    blocks = [_make_block(pkg, oracle, cuda, seed=40 + i)[0] for i in range(2)]
+    _, layers0 = _make_block(pkg, oracle, cuda, seed=40)
+    stack = DenoiserStack(blocks)
+    g = torch.Generator(device=cuda).manual_seed(8)
+    seqs, L = 6, 512
+    x0 = torch.randn((seqs * L, 1024), device=cuda, generator=g)
+    ref = x0.clone()
+    for b in blocks:
+        b.forward_(ref, images=seqs)
+    for chunk in (1, 2, 4, 6):
+        y = x0.clone()
+        stack.forward_(y, seqs, chunk)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref), f"chunk {chunk}: max abs diff {(y - ref).abs().max().item()}"
+    one = x0.clone()
+    DenoiserStack(blocks[:1]).forward_(one, seqs, 2)
+    torch.cuda.synchronize()
+    want = oracle.block_forward(x0.cpu().numpy(), layers0, 16, images=seqs)
+    _check(one.cpu().numpy(), want, what="stack block 0 vs oracle")
