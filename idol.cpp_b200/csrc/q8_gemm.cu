@@ -113,67 +113,111 @@ __device__ __forceinline__ void dequant_stage_q4k(const uint8_t* chunk, int q, i
 
 // Epilogue over `cols` consecutive accumulator columns (tokens m .. m + cols - 1) of one weight row, with the
 // activation fixed at compile time so the per-element loop carries no dispatch.
-// `rv`, when given, holds the residual values of these columns, loaded ahead by the caller.
-template <typename OutT, int kCols, int kAct>
+// kRv: the residual values of these columns are in `rv`, loaded ahead by the caller. A chunk wholly inside M (m is
+// warp-uniform, so every lane takes the same path) then runs as straight-line code with no per-element bounds test:
+// those tests were branches per element that tripled the residual epilogue's branch count and stalled its warps on
+// instruction fetch (ncu: a 16384 x 1024 x 1024 fp32-residual launch took 2.0x the time of the same launch without
+// a residual). The arithmetic and its order are the same on every path.
+template <typename OutT, int kCols, int kAct, bool kRv>
 __device__ __forceinline__ void finish_cols_act(const Params& p, int m, int row, const uint32_t* v, float bias,
                                                 const float* rv) {
     const int col = row - p.n_offset;
     OutT* y = static_cast<OutT*>(p.y) + col;
-    const OutT* res = static_cast<const OutT*>(p.residual);
-    if (!res && !p.bias_after_round && m + kCols <= p.m) {
+    if constexpr (kRv) {
+        const bool round_first = p.bias_after_round != 0;
+        if (m + kCols <= p.m) {
 #pragma unroll
-        for (int j = 0; j < kCols; ++j)
-            y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(__uint_as_float(v[j]) + bias));
-        return;
-    }
+            for (int j = 0; j < kCols; ++j) {
+                const float a = __uint_as_float(v[j]);
+                const float x = ((round_first ? out_round<OutT>(a) : a) + bias) + rv[j];
+                y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
+            }
+            return;
+        }
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) {
-        if (m + j >= p.m) break;
-        const float acc = __uint_as_float(v[j]);
-        float x = p.bias_after_round ? out_round<OutT>(acc) + bias : acc + bias;
-        if (rv) x += rv[j];
-        else if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
-        y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
+        for (int j = 0; j < kCols; ++j) {
+            if (m + j >= p.m) break;
+            const float a = __uint_as_float(v[j]);
+            const float x = ((round_first ? out_round<OutT>(a) : a) + bias) + rv[j];
+            y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
+        }
+    } else {
+        const OutT* res = static_cast<const OutT*>(p.residual);
+        if (!res && !p.bias_after_round && m + kCols <= p.m) {
+#pragma unroll
+            for (int j = 0; j < kCols; ++j)
+                y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(__uint_as_float(v[j]) + bias));
+            return;
+        }
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) {
+            if (m + j >= p.m) break;
+            const float acc = __uint_as_float(v[j]);
+            float x = p.bias_after_round ? out_round<OutT>(acc) + bias : acc + bias;
+            if (res) x += from_out<OutT>(res[(long long)(m + j) * p.ldr + col]);
+            y[(long long)(m + j) * p.ldy] = to_out<OutT>(activate_t<kAct>(x));
+        }
     }
 }
 
-template <typename OutT, int kCols>
+template <typename OutT, int kCols, bool kRv = false>
 __device__ __forceinline__ void finish_cols(const Params& p, int m, int row, const uint32_t* v, float bias,
                                             bool row_ok, const float* rv = nullptr) {
     if (!row_ok) return;
     switch (p.act) {
-        case IDOL_ACT_GELU_ERF: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_ERF>(p, m, row, v, bias, rv); break;
-        case IDOL_ACT_GELU_TANH: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_TANH>(p, m, row, v, bias, rv); break;
-        case IDOL_ACT_SILU: finish_cols_act<OutT, kCols, IDOL_ACT_SILU>(p, m, row, v, bias, rv); break;
-        default: finish_cols_act<OutT, kCols, IDOL_ACT_NONE>(p, m, row, v, bias, rv); break;
+        case IDOL_ACT_GELU_ERF: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_ERF, kRv>(p, m, row, v, bias, rv); break;
+        case IDOL_ACT_GELU_TANH: finish_cols_act<OutT, kCols, IDOL_ACT_GELU_TANH, kRv>(p, m, row, v, bias, rv); break;
+        case IDOL_ACT_SILU: finish_cols_act<OutT, kCols, IDOL_ACT_SILU, kRv>(p, m, row, v, bias, rv); break;
+        default: finish_cols_act<OutT, kCols, IDOL_ACT_NONE, kRv>(p, m, row, v, bias, rv); break;
     }
 }
 
+// L2 prefetch of the residual that the epilogue of an output tile will read: token `token`'s values of the tile's
+// features [row0, row0 + 128) inside the window, one bulk prefetch of the 16-byte aligned part of that row segment
+// (512 bytes for a full fp32 tile). Issued while the tile's main loop runs, so that the epilogue's residual loads,
+// one per token and feature, find their lines in L2 instead of waiting for HBM. Nothing outside the residual rows
+// the epilogue reads is touched.
+template <typename OutT>
+__device__ __forceinline__ void prefetch_residual_row(const Params& p, int row0, int token) {
+    if (p.residual == nullptr || token < 0 || token >= p.m) return;
+    const int c0 = max(row0, p.n_offset) - p.n_offset;
+    const int c1 = min(row0 + kRowsPerTile, p.n_offset + p.n_count) - p.n_offset;
+    if (c1 <= c0) return;
+    const OutT* r = static_cast<const OutT*>(p.residual) + (long long)token * p.ldr;
+    const uintptr_t a = (reinterpret_cast<uintptr_t>(r + c0) + 15) & ~static_cast<uintptr_t>(15);
+    const uintptr_t b = reinterpret_cast<uintptr_t>(r + c1) & ~static_cast<uintptr_t>(15);
+    if (b > a) prefetch_l2_bulk(reinterpret_cast<const void*>(a), (uint32_t)(b - a));
+}
+
 // Epilogue of one weight row (TMEM lane) over kSpan accumulator columns from TMEM address `acc` (tokens m0 ...),
-// 16 (or 8) columns per tcgen05.ld. With a residual, its values are loaded 32 tokens at a time before the columns
-// they meet, so a row waits one memory latency per 32 tokens instead of one per 16. Control flow around the
-// warp-collective tcgen05.ld depends only on warp-uniform values; row_ok gates the per-lane memory accesses.
-template <typename OutT, int kSpan>
+// 16 (or 8) columns per tcgen05.ld. With a residual, its values are loaded kMaxGroup tokens at a time before the
+// columns they meet, so a row waits one memory latency per kMaxGroup tokens instead of one per 16 (as many as the
+// kernel's register budget holds: 16 in the persistent kernels, whose 576 threads have 113 registers each and whose
+// residual rows are prefetched to L2 one tile ahead; 64 in the 320-thread kernel). Control flow around the warp-collective tcgen05.ld depends only on
+// warp-uniform values; row_ok gates the per-lane memory accesses.
+template <typename OutT, int kSpan, int kMaxGroup = 32>
 __device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, uint32_t acc, float bias,
                                               bool row_ok) {
     constexpr int kChunk = kSpan >= 16 ? 16 : 8;
-    constexpr int kGroup = kSpan >= 32 ? 32 : kSpan;
+    constexpr int kGroup = kSpan >= kMaxGroup ? kMaxGroup : kSpan;
     if constexpr (kGroup % 16 == 0) {
         if (p.residual != nullptr) {
-            const OutT* res = static_cast<const OutT*>(p.residual) + (row - p.n_offset);
+            // Unconditional loads from clamped addresses (a lane outside the window reads the window's first column,
+            // a token past M the last token): per-element conditions made predicated or branching loads that cost
+            // more than the loads. Values read for such positions are never used.
+            const OutT* res = static_cast<const OutT*>(p.residual) + (row_ok ? row - p.n_offset : 0);
             for (int g0 = 0; g0 < kSpan && m0 + g0 < p.m; g0 += kGroup) {
                 float rv[kGroup];
 #pragma unroll
                 for (int j = 0; j < kGroup; ++j)
-                    rv[j] = (row_ok && m0 + g0 + j < p.m) ? from_out<OutT>(res[(long long)(m0 + g0 + j) * p.ldr])
-                                                          : 0.0f;
+                    rv[j] = from_out<OutT>(res[(long long)min(m0 + g0 + j, p.m - 1) * p.ldr]);
 #pragma unroll
                 for (int c0 = 0; c0 < kGroup; c0 += 16) {
                     if (m0 + g0 + c0 >= p.m) break;
                     uint32_t v[16];
                     tmem_ld16(acc + g0 + c0, v);
                     tmem_ld_wait();
-                    finish_cols<OutT, 16>(p, m0 + g0 + c0, row, v, bias, row_ok, rv + c0);
+                    finish_cols<OutT, 16, true>(p, m0 + g0 + c0, row, v, bias, row_ok, rv + c0);
                 }
             }
             return;
@@ -193,18 +237,20 @@ __device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, 
 // and a single TMA store later writes the tile. Features outside the output window and tokens past M are written
 // too: the store clips them. The 32 lanes of a warp store 64 contiguous bytes per token (no bank conflict).
 // GELU-erf takes 8 columns per tcgen05.ld: erff on 16 values at once needs more than the 96 registers a thread has.
-template <typename OutT, int kSpan, int kAct>
+template <typename OutT, int kSpan, int kAct, bool kRes>
 __device__ __forceinline__ void epilogue_span_staged(const Params& p, int m0, int row, uint32_t acc, float bias,
                                                      bool row_ok, uint32_t st) {
     constexpr int kC = kAct == IDOL_ACT_GELU_ERF ? 8 : 16;
     static_assert(kSpan % kC == 0 && sizeof(OutT) == 2, "whole chunks of a 2-byte output");
-    const OutT* res = p.residual ? static_cast<const OutT*>(p.residual) + (row - p.n_offset) : nullptr;
+    // kRes: residual loads are unconditional, from clamped addresses, as in epilogue_span (per-element conditions
+    // on 2-byte loads made this path 5x slower than the one without a residual). The path without a residual is
+    // a separate instantiation, so that its code and registers carry nothing of the residual's.
+    const OutT* res = kRes ? static_cast<const OutT*>(p.residual) + (row_ok ? row - p.n_offset : 0) : nullptr;
     for (int c0 = 0; c0 < kSpan && m0 + c0 < p.m; c0 += kC) {
         float rv[kC];
-        if (res) {
+        if constexpr (kRes) {
 #pragma unroll
-            for (int j = 0; j < kC; ++j)
-                rv[j] = (row_ok && m0 + c0 + j < p.m) ? from_out<OutT>(res[(long long)(m0 + c0 + j) * p.ldr]) : 0.0f;
+            for (int j = 0; j < kC; ++j) rv[j] = from_out<OutT>(res[(long long)min(m0 + c0 + j, p.m - 1) * p.ldr]);
         }
         uint32_t v[kC];
         if constexpr (kC == 16) tmem_ld16(acc + c0, v);
@@ -214,12 +260,20 @@ __device__ __forceinline__ void epilogue_span_staged(const Params& p, int m0, in
         for (int j = 0; j < kC; ++j) {
             const float a = __uint_as_float(v[j]);
             float x = p.bias_after_round ? out_round<OutT>(a) + bias : a + bias;
-            if (res) x += rv[j];
+            if constexpr (kRes) x += rv[j];
             const OutT o = to_out<OutT>(activate_t<kAct>(x));
             st_shared_u16(st + (uint32_t)(c0 + j) * (kRowsPerTile * 2),
                           *reinterpret_cast<const uint16_t*>(&o));
         }
     }
+}
+
+// epilogue_span_staged with the residual choice made once per span.
+template <typename OutT, int kSpan, int kAct>
+__device__ __forceinline__ void epilogue_span_staged_any(const Params& p, int m0, int row, uint32_t acc, float bias,
+                                                         bool row_ok, uint32_t st) {
+    if (p.residual != nullptr) epilogue_span_staged<OutT, kSpan, kAct, true>(p, m0, row, acc, bias, row_ok, st);
+    else epilogue_span_staged<OutT, kSpan, kAct, false>(p, m0, row, acc, bias, row_ok, st);
 }
 
 template <int BN, int S, bool kBF16, typename OutT, int kFmt>
@@ -314,6 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        // The tile's residual rows go to L2 while the main loop runs (one token per dequant thread, BN <= 256).
+        if (gridDim.z == 1 && (warp - 2) * 32 + lane < BN)
+            prefetch_residual_row<OutT>(p, row0, m0 + (warp - 2) * 32 + lane);
         // The A buffer of slot s was last read by stage i - S. Its MMA has completed once full[s] completes for stage
         // i: the producer issues stage i's copies only after that MMA's commit (empty[s]), so one wait covers both.
         // With an odd S the two groups alternate on a slot: stage i and stage i - S of slot s belong to different
@@ -352,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
         if (gridDim.z == 1) {
             const bool row_ok = ok && row < p.n && row >= p.n_offset && row < p.n_offset + p.n_count;
             const float bias = (row_ok && p.bias) ? p.bias[row] : 0.0f;
-            epilogue_span<OutT, kHalf>(p, m0 + c_begin, row, tmem + lane_base + c_begin, bias, row_ok);
+            epilogue_span<OutT, kHalf, 64>(p, m0 + c_begin, row, tmem + lane_base + c_begin, bias, row_ok);
         } else {
             // Park the partial tile [token][row] in this CTA's X ring (all loads into it have landed).
             float* red = reinterpret_cast<float*>(xs);
@@ -726,8 +783,18 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
         int lt = 0;
         int ns = 0;  // TMA stores issued so far (staged tiles)
         int nh = 0;  // staged tiles whose heads were normalised
+        // The residual rows of a tile go to L2 one tile ahead of its epilogue (while its main loop runs): one token
+        // per epilogue thread (BN <= 256).
+        auto prefetch_tile = [&](int t) {
+            const int e = ew * 32 + lane;
+            if (t < total_tiles && e < BN)
+                prefetch_residual_row<OutT>(p, p.row_begin + (t % sched.units_n) * kRowsPerUnit +
+                                                   (int)rank * kRowsPerTile, (t / sched.units_n) * BN + e);
+        };
+        prefetch_tile(pair_id);
         for (int t = pair_id; t < total_tiles; t += num_pairs, ++lt) {
             const int b = lt & 1;
+            prefetch_tile(t + num_pairs);
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&accfull[b], (lt >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
@@ -743,22 +810,20 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 // (>= 0 and a multiple of 8: the host stages only windows with n_offset % 128 == 0).
                 if (ns > 0 && !__all_sync(0xffffffffu, mbar_wait(sfree, (ns - 1) & 1, abort_flag))) break;
                 const uint32_t st = smem_u32(ys) + 2u * (uint32_t)(c_begin * kRowsPerTile + 32 * q + lane);
+                const int ms = m0 + c_begin;
+                const uint32_t ac = acc + c_begin;
                 switch (p.act) {
                     case IDOL_ACT_GELU_ERF:
-                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_GELU_ERF>(p, m0 + c_begin, row, acc + c_begin,
-                                                                                bias, row_ok, st);
+                        epilogue_span_staged_any<OutT, kHalfCols, IDOL_ACT_GELU_ERF>(p, ms, row, ac, bias, row_ok, st);
                         break;
                     case IDOL_ACT_GELU_TANH:
-                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_GELU_TANH>(p, m0 + c_begin, row, acc + c_begin,
-                                                                                 bias, row_ok, st);
+                        epilogue_span_staged_any<OutT, kHalfCols, IDOL_ACT_GELU_TANH>(p, ms, row, ac, bias, row_ok, st);
                         break;
                     case IDOL_ACT_SILU:
-                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_SILU>(p, m0 + c_begin, row, acc + c_begin, bias,
-                                                                            row_ok, st);
+                        epilogue_span_staged_any<OutT, kHalfCols, IDOL_ACT_SILU>(p, ms, row, ac, bias, row_ok, st);
                         break;
                     default:
-                        epilogue_span_staged<OutT, kHalfCols, IDOL_ACT_NONE>(p, m0 + c_begin, row, acc + c_begin, bias,
-                                                                            row_ok, st);
+                        epilogue_span_staged_any<OutT, kHalfCols, IDOL_ACT_NONE>(p, ms, row, ac, bias, row_ok, st);
                         break;
                 }
                 tc_fence_before();
@@ -796,7 +861,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 ++ns;
                 nh += hn ? 1 : 0;
             } else {
-                epilogue_span<OutT, kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
+                epilogue_span<OutT, kHalfCols, 16>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {

@@ -241,10 +241,13 @@ def test_compositions_no_timeout(pkg, cuda):
     assert pkg._capi.device_status(0) == 0
 
 
-def test_denoiser_stack_chunks_equal_block_by_block(pkg, oracle, cuda):
-    """DenoiserStack (config 5) over 3 images x 2 CFG branches of 512 tokens: any chunking of the sequences gives the
-    same bits as running the blocks one after another over all sequences (each sequence attends only within itself,
-    rows are independent elsewhere), and the stack's first block matches the oracle composition."""
+def test_denoiser_stack_chunks_equal_block_by_block(pkg, oracle, cuda, monkeypatch):
+    """DenoiserStack (config 5) over 3 images x 2 CFG branches of 512 tokens: each sequence attends only within
+    itself and rows are independent elsewhere, so with K summed unsplit any chunking of the sequences gives the same
+    bits as running the blocks one after another over all sequences. With the default strategy a chunk's GEMMs may
+    split K across a cluster (chosen by the chunk's row count: ff2 at 512 rows does, at 3072 it does not), which
+    changes only the fp32 summation order: those runs are held to the GEMM bar. The stack's first block matches the
+    oracle composition."""
     from idol_b200.block import DenoiserStack
     blocks = [_make_block(pkg, oracle, cuda, seed=40 + i)[0] for i in range(2)]
     _, layers0 = _make_block(pkg, oracle, cuda, seed=40)
@@ -252,14 +255,28 @@ def test_denoiser_stack_chunks_equal_block_by_block(pkg, oracle, cuda):
     g = torch.Generator(device=cuda).manual_seed(8)
     seqs, L = 6, 512
     x0 = torch.randn((seqs * L, 1024), device=cuda, generator=g)
-    ref = x0.clone()
-    for b in blocks:
-        b.forward_(ref, images=seqs)
-    for chunk in (1, 2, 4, 6):
-        y = x0.clone()
-        stack.forward_(y, seqs, chunk)
+
+    def run_all(chunks):
+        ref = x0.clone()
+        for b in blocks:
+            b.forward_(ref, images=seqs)
+        outs = {}
+        for chunk in chunks:
+            y = x0.clone()
+            stack.forward_(y, seqs, chunk)
+            outs[chunk] = y
         torch.cuda.synchronize()
-        assert torch.equal(y, ref), f"chunk {chunk}: max abs diff {(y - ref).abs().max().item()}"
+        return ref, outs
+
+    ref, outs = run_all((1, 2, 4, 6))
+    for chunk, y in outs.items():
+        _check(y.cpu().numpy(), ref.cpu().numpy(), what=f"stack chunk {chunk} vs unchunked")
+    assert torch.equal(outs[6], ref), "one chunk of every sequence must be the unchunked run"
+    monkeypatch.setenv("IDOL_B200_GEMM_SPLITS", "1")  # read at each GEMM call
+    ref, outs = run_all((1, 2, 4, 6))
+    monkeypatch.delenv("IDOL_B200_GEMM_SPLITS")
+    for chunk, y in outs.items():
+        assert torch.equal(y, ref), f"chunk {chunk}, K unsplit: max abs diff {(y - ref).abs().max().item()}"
     one = x0.clone()
     DenoiserStack(blocks[:1]).forward_(one, seqs, 2)
     torch.cuda.synchronize()
