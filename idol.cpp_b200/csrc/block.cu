@@ -715,6 +715,7 @@ int idol_b200_gaussian_mlp_forward_static(const idol_gaussian_mlp* mlp, const vo
     void* scratch = nullptr;
     const int rc = static_scratch(mlp->device, &scratch);
     if (rc != IDOL_OK) return rc;
+    const idol::NoScratchScope no_library_scratch;  // the GEMMs keep the kernels that need no scratch of their own
     return idol_b200_gaussian_mlp_forward(mlp, x, points, ldx, scratch, kStaticMlpScratchBytes, raw_out, out, stream);
 }
 

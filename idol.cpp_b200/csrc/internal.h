@@ -91,6 +91,15 @@ struct GemmCall {
     int head_cols = 0, head_split = 0;
 };
 int q8_gemm(const GemmCall& c);
+// While one of these lives on the calling thread, q8_gemm allocates nothing of its own: calls that would take the
+// large-M dense path (which dequantises into a scratch the library allocates per device and stream) take the fused
+// kernel instead. The allocation-free entry points run their GEMMs inside one.
+struct NoScratchScope {
+    NoScratchScope();
+    ~NoScratchScope();
+    NoScratchScope(const NoScratchScope&) = delete;
+    NoScratchScope& operator=(const NoScratchScope&) = delete;
+};
 // The integer-activation form of the same linear (q8_int8act.cu): flags unused; workspace for the quantized
 // activations (int8act_workspace_bytes).
 int64_t int8act_workspace_bytes(int64_t m, int k);

@@ -25,6 +25,9 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -485,6 +488,43 @@ __global__ void __launch_bounds__(kThreads, 1) q8_gemm_kernel(const __grid_const
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// Dense tile layout: the large-M path dequantises the tiled Q8_0 weights once per call into this layout and runs a
+// GEMM whose weight operand comes from shared memory like the tokens (the reference's own large-M GPU strategy,
+// tools/idol_triton.py:112-117, dequantises into a scratch and calls a dense GEMM). Per (row tile, k stage) one 16 KB
+// tile: 128 rows of 64 operand-type values, 128 bytes per row, the 16-byte units of row r stored in the order of the
+// 128-byte swizzle (unit c at position c ^ (r % 8)), so that one bulk copy puts the tile into shared memory exactly
+// as a TMA load with that swizzle would and the MMA reads it with the same descriptor as the token tile. The values
+// are those the fused kernel forms in registers (dequant16: bf16 or fp16 of the exact fp32 product d q); rows past N
+// and blocks past K are zero because their codes and scales are.
+constexpr int kDenseChunkBytes = kRowsPerTile * kStageK * 2;
+// Smallest M that takes the dense path by default (measured on B200, see q8_gemm_impl).
+constexpr int64_t kDenseMinM = 1024;
+
+template <bool kBF16>
+__global__ void __launch_bounds__(128) q8_dense_tiles_kernel(const uint8_t* __restrict__ tiles,
+                                                             uint8_t* __restrict__ dense) {
+    const uint8_t* src = tiles + (long long)blockIdx.x * kChunkBytes;
+    uint8_t* dst = dense + (long long)blockIdx.x * kDenseChunkBytes;
+    const int r = threadIdx.x, q = r / 32, lane = r % 32;  // thread r: row r of the tile (lane r of quarter q)
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(src + kChunkCodeBytes + q * 128);
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const float d = __half2float(__ushort_as_half(sbase[b * 32 + lane]));
+        const float2 dd = make_float2(d, d);
+        const float2 ncd = make_float2(-32896.0f * d, -32896.0f * d);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t w[8];
+            dequant16<kBF16>(*reinterpret_cast<const uint4*>(src + q * 2048 + b * 1024 + h * 512 + lane * 16), dd, ncd,
+                             w);
+            const int c = 4 * b + 2 * h;  // 16-byte unit of k = 32 b + 16 h within the 128-byte row
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(dst + r * 128 + (((c + 1) ^ (r & 7)) * 16)) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // Persistent CTA-pair variant (cta_group::2) for large M.
 //
 // Two CTAs of a cluster share one MMA of M = 256 weight rows x N = BN tokens: each CTA dequantises its own 128 rows
@@ -509,13 +549,16 @@ constexpr int kEpilogueWarps = 8;   // two per TMEM lane quarter, half of the to
 constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 
 // kYStage: bytes of the shared staging tile the epilogue hands to TMA stores (0: the epilogue stores directly).
-template <int BN, int S, int SA, bool kPair, int kYStage = 0>
+// kDense: the weights of a stage arrive already dequantised (a 16 KB tile of the dense layout, see
+// q8_dense_tiles_kernel) and both MMA operands come from shared memory; no A slots in tensor memory.
+template <int BN, int S, int SA, bool kPair, int kYStage = 0, bool kDense = false>
 struct ConfigPersistent {
     static constexpr int kHalf = kPair ? BN / 2 : BN;  // token rows this CTA loads per stage
     static constexpr int kXBytes = kHalf * 128;
-    static constexpr int kStageBytes = kXBytes + kChunkBytes;
+    static constexpr int kWBytes = kDense ? kDenseChunkBytes : kChunkBytes;  // one stage of weights
+    static constexpr int kStageBytes = kXBytes + kWBytes;
     static constexpr int kACol0 = 2 * BN;  // accumulators at columns 0 and BN, then the A slots
-    static constexpr int kColsNeeded = kACol0 + SA * 32;
+    static constexpr int kColsNeeded = kACol0 + (kDense ? 0 : SA * 32);
     static constexpr int kTmemCols = kColsNeeded <= 256 ? 256 : 512;
     static constexpr int kBarBytes = 8 * (3 * S + SA + 7) + 16;
     static_assert(SA <= S, "an A slot is released by the commit of a stage no later than the one reusing its buffer");
@@ -529,6 +572,7 @@ struct ConfigPersistent {
     static_assert(kSmemUsed <= 227 * 1024, "shared memory budget");
     static_assert(BN % (kPair ? 32 : 16) == 0 && BN >= 64 && BN <= 256, "MMA N");
     static_assert(kXBytes % 1024 == 0, "each token half must stay 1024-aligned for the 128-byte swizzle");
+    static_assert(!kDense || kWBytes % 1024 == 0, "dense: 1024-aligned weight tiles");
     static constexpr int kYStageBytes = kYStage;
     static_assert(kYStage % 1024 == 0, "the staging tile keeps the weight chunks after it 16-byte aligned");
 };
@@ -592,20 +636,20 @@ __device__ __forceinline__ void head_norm_staged(uint8_t* ys, int tile_row0, con
     }
 }
 
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage>
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage, bool kDense>
 __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
-    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap, const Params p,
-    const PersistentSchedule sched) {
-    using C = ConfigPersistent<BN, S, SA, kPair, kYStage>;
-    static_assert(kYStage == 0 || (!kPair && sizeof(OutT) == 2 && kYStage >= BN * kRowsPerTile * 2),
-                  "staging: one CTA, a 2-byte output and room for the whole tile");
+    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+    const __grid_constant__ CUtensorMap wmap, const Params p, const PersistentSchedule sched) {
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense>;
+    static_assert(kYStage == 0 || ((!kPair || kDense) && sizeof(OutT) == 2 && kYStage >= BN * kRowsPerTile * 2),
+                  "staging: one CTA (or a dense pair), a 2-byte output and room for the whole tile");
     constexpr int kRowsPerUnit = kPair ? 2 * kRowsPerTile : kRowsPerTile;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* xs = smem;
     uint8_t* ys = xs + S * C::kXBytes;                                              // output staging (1024-aligned)
-    uint8_t* ws = ys + C::kYStageBytes;                                             // S x 8704 weight chunks
-    uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * kChunkBytes);            // even CTA: both halves landed
+    uint8_t* ws = ys + C::kYStageBytes;                                             // S weight stages
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);             // even CTA: both halves landed
     uint64_t* cfull = xfull + S;                                                    // this CTA's codes landed
     uint64_t* empty = cfull + S;                                                    // both: stage s consumed
     uint64_t* afull = empty + S;                                                    // even CTA: A slot written (both)
@@ -670,17 +714,26 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 for (int ks = 0; ks < nks; ++ks, ++i) {
                     const int s = i % S, u = i / S;
                     if (i >= S && !mbar_wait(&empty[s], (u - 1) & 1, abort_flag)) { ok = false; break; }
-                    const uint8_t* chunk = p.tiles + ((long long)t128 * p.layout_stages + ks) * kChunkBytes;
-                    if constexpr (kPair) {
+                    const uint8_t* chunk = p.tiles + ((long long)t128 * p.layout_stages + ks) * C::kWBytes;
+                    if constexpr (kPair && kDense) {
+                        // Both CTAs' token halves and weight tiles land on the even CTA's barrier (the MMA waits
+                        // there only). The weight tile comes by TMA without swizzle, as the dense layout already
+                        // holds it swizzled; a pair's second tile past N reads zeros.
+                        if (rank == 0) mbar_arrive_expect_tx(&xfull[s], 2 * (C::kXBytes + C::kWBytes));
+                        tma_load_2d_pair(xs + s * C::kXBytes, &xmap, ks * kStageK, m0 + (int)rank * C::kHalf,
+                                         map_to_rank(smem_u32(&xfull[s]), 0));
+                        tma_load_2d_pair(ws + s * C::kWBytes, &wmap, 0, (t128 * p.layout_stages + ks) * kRowsPerTile,
+                                         map_to_rank(smem_u32(&xfull[s]), 0));
+                    } else if constexpr (kPair) {
                         if (rank == 0) mbar_arrive_expect_tx(&xfull[s], 2 * C::kXBytes);
                         tma_load_2d_pair(xs + s * C::kXBytes, &xmap, ks * kStageK, m0 + (int)rank * C::kHalf,
                                          map_to_rank(smem_u32(&xfull[s]), 0));
                         mbar_arrive_expect_tx(&cfull[s], valid ? kChunkBytes : 0);
                         if (valid) bulk_load(ws + s * kChunkBytes, chunk, kChunkBytes, &cfull[s]);
                     } else {
-                        mbar_arrive_expect_tx(&xfull[s], C::kXBytes + kChunkBytes);
+                        mbar_arrive_expect_tx(&xfull[s], C::kXBytes + C::kWBytes);
                         tma_load_2d(xs + s * C::kXBytes, &xmap, ks * kStageK, m0, &xfull[s]);
-                        bulk_load(ws + s * kChunkBytes, chunk, kChunkBytes, &xfull[s]);
+                        bulk_load(ws + s * C::kWBytes, chunk, C::kWBytes, &xfull[s]);
                     }
                 }
             }
@@ -688,7 +741,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
             // on cfull; both CTAs' token halves on the even CTA's xfull (the odd CTA's copies count there too, and
             // the final cluster barrier keeps the odd CTA until the even one has drained).
             for (int j = i - S > 0 ? i - S : 0; j < i; ++j) {
-                if constexpr (kPair) mbar_drain(&cfull[j % S], (j / S) & 1);
+                if constexpr (kPair && !kDense) mbar_drain(&cfull[j % S], (j / S) & 1);
                 if (rank == 0) mbar_drain(&xfull[j % S], (j / S) & 1);
             }
         }
@@ -708,15 +761,27 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                     // they reported the A slot, so afull completing implies the stage's tokens have landed.
                     const int s = i % S;
                     const int a = i % SA, ua = i / SA;
-                    if (!mbar_wait(&afull[a], ua & 1, abort_flag)) { ok = false; break; }
+                    // Dense: the stage's weights and tokens land on xfull; otherwise the A slot's barrier implies both.
+                    if (!(kDense ? mbar_wait(&xfull[s], (i / S) & 1, abort_flag)
+                                 : mbar_wait(&afull[a], ua & 1, abort_flag))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const bool two_blocks = (p.kb - ks * 2) >= 2;
                     const uint32_t xaddr = smem_u32(xs + s * C::kXBytes);
+                    const uint32_t waddr = smem_u32(ws + s * C::kWBytes);
                     const uint32_t a0 = tmem + C::kACol0 + a * 32;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         if (j < 2 || two_blocks) {
-                            if constexpr (kPair)
+                            if constexpr (kDense && kPair)
+                                mma_ss_pair(acc, make_sdesc_sw128(waddr + j * 32), make_sdesc_sw128(xaddr + j * 32),
+                                            idesc, (ks > 0 || j > 0) ? 1u : 0u);
+                            else if constexpr (kDense)
+                                mma_ss(acc, make_sdesc_sw128(waddr + j * 32), make_sdesc_sw128(xaddr + j * 32), idesc,
+                                       (ks > 0 || j > 0) ? 1u : 0u);
+                            else if constexpr (kPair)
                                 mma_ts_pair(acc, a0 + j * 8, make_sdesc_sw128(xaddr + j * 32), idesc,
                                             (ks > 0 || j > 0) ? 1u : 0u);
                             else
@@ -732,6 +797,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
             }
         }
     } else if (warp < 2 + kDequantWarps) {
+      if constexpr (!kDense) {  // dense: the weights arrive dequantised and these warps wait at the final barrier
         // As in the single-CTA kernel: warps 2-5 take the even stages, warps 6-9 the odd ones, both Q8 blocks each.
         const int q = warp % 4;
         const int half = (warp - 2) / 4;
@@ -773,6 +839,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 }
             }
         }
+      }
     } else {
         // Epilogue warps: warp w reads TMEM lanes of quarter w % 4; the two warps of a quarter split the columns.
         const int ew = warp - 2 - kDequantWarps;
@@ -830,7 +897,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 fence_proxy_async_shared();  // this lane's staging writes, before the TMA store reads them
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&accempty[b]);
+                    if (rank == 0) mbar_arrive(&accempty[b]);
+                    else mbar_arrive_remote(map_to_rank(smem_u32(&accempty[b]), 0));
                     mbar_arrive(sfull);
                 }
                 // rms_heads of the staged tile (tiles lie wholly inside or outside [0, hn_cols): hn_cols is a
@@ -884,11 +952,11 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     }
 }
 
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage = 0>
-int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const Params& p, int units_n, int tiles_m,
-                      cudaStream_t stream) {
-    using C = ConfigPersistent<BN, S, SA, kPair, kYStage>;
-    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT, kYStage>;
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage = 0, bool kDense = false>
+int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const CUtensorMap& wmap, const Params& p,
+                      int units_n, int tiles_m, cudaStream_t stream) {
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense>;
+    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT, kYStage, kDense>;
     static unsigned long long configured = 0;
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -912,25 +980,44 @@ int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const Pa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = kPair ? 1 : 0;
-    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, ymap, p, sched));
+    IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, ymap, wmap, p, sched));
     return IDOL_OK;
 }
 
 // kind 0: CTA pair, 128- or 192-token tiles; kind 1: one CTA, 192-token tiles (with p.y_tma through the 48 KB
-// staging tile and TMA stores, with five stages; otherwise six stages and direct stores).
+// staging tile and TMA stores, with five stages; otherwise six stages and direct stores); kind 2: the dense form of
+// kind 1 (p.tiles is the dequantised tile layout; 40 KB stages: four beside the staging tile, five without); kind 3:
+// the dense form on a CTA pair, 256 weight rows x 256 tokens per tile (each CTA loads its 128 weight rows and half of
+// the tokens: 32 KB stages, five beside the 64 KB staging tile, six without), `wmap` the dense layout as rows of 64.
 template <bool kBF16, typename OutT>
-int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtensorMap& ymap, const Params& p,
-                        int units, int tiles_m, cudaStream_t stream) {
+int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtensorMap& ymap, const CUtensorMap& wmap,
+                        const Params& p, int units, int tiles_m, cudaStream_t stream) {
+    if (kind == 3) {
+        if constexpr (sizeof(OutT) == 2) {
+            if (p.y_tma)
+                return launch_persistent<256, 5, 4, true, kBF16, OutT, 256 * kRowsPerTile * 2, true>(
+                    xmap, ymap, wmap, p, units, tiles_m, stream);
+        }
+        return launch_persistent<256, 6, 4, true, kBF16, OutT, 0, true>(xmap, ymap, wmap, p, units, tiles_m, stream);
+    }
+    if (kind == 2) {
+        if constexpr (sizeof(OutT) == 2) {
+            if (p.y_tma)
+                return launch_persistent<192, 4, 4, false, kBF16, OutT, 192 * kRowsPerTile * 2, true>(
+                    xmap, ymap, wmap, p, units, tiles_m, stream);
+        }
+        return launch_persistent<192, 5, 4, false, kBF16, OutT, 0, true>(xmap, ymap, wmap, p, units, tiles_m, stream);
+    }
     if (kind == 1) {
         if constexpr (sizeof(OutT) == 2) {
             if (p.y_tma)
-                return launch_persistent<192, 5, 4, false, kBF16, OutT, 192 * kRowsPerTile * 2>(xmap, ymap, p, units,
-                                                                                              tiles_m, stream);
+                return launch_persistent<192, 5, 4, false, kBF16, OutT, 192 * kRowsPerTile * 2>(xmap, ymap, wmap, p,
+                                                                                              units, tiles_m, stream);
         }
-        return launch_persistent<192, 6, 4, false, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
+        return launch_persistent<192, 6, 4, false, kBF16, OutT>(xmap, ymap, wmap, p, units, tiles_m, stream);
     }
-    if (bn == 128) return launch_persistent<128, 8, 8, true, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
-    return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, ymap, p, units, tiles_m, stream);
+    if (bn == 128) return launch_persistent<128, 8, 8, true, kBF16, OutT>(xmap, ymap, wmap, p, units, tiles_m, stream);
+    return launch_persistent<192, 4, 4, true, kBF16, OutT>(xmap, ymap, wmap, p, units, tiles_m, stream);
 }
 
 template <int BN, int S, bool kBF16, typename OutT, int kFmt>
@@ -995,6 +1082,40 @@ static bool staged_output_ok(const GemmCall& c) {
     return c.y_dtype != IDOL_F32 && c.n >= kRowsPerTile && c.m >= 192 && c.n_offset % kRowsPerTile == 0 &&
            (c.ldy * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(c.y) % 16 == 0 &&
            env_int("IDOL_B200_GEMM_YTMA", 1) != 0;
+}
+
+// ------------------------------------------------------------------------------------------------ dense path
+// Scratch of the dense path, one buffer per (device, stream): a call dequantises its weights into it and the GEMM on
+// the same stream reads them, so calls in stream order may share it and calls on different streams never do. Grown by
+// allocating a larger buffer; the smaller one stays allocated until exit, because a CUDA graph captured earlier may
+// still use it. Never allocated while the calling stream is being captured (the call then takes the fused kernel),
+// nor while a NoScratchScope is active on the calling thread.
+static std::mutex g_dense_mutex;
+static std::map<std::pair<int, uintptr_t>, std::pair<void*, size_t>> g_dense_scratch;
+static thread_local int g_no_scratch_depth = 0;
+
+NoScratchScope::NoScratchScope() { ++g_no_scratch_depth; }
+NoScratchScope::~NoScratchScope() { --g_no_scratch_depth; }
+
+static void* dense_scratch(int device, cudaStream_t stream, size_t bytes) {
+    if (g_no_scratch_depth > 0) return nullptr;
+    std::lock_guard<std::mutex> lock(g_dense_mutex);
+    auto& e = g_dense_scratch[{device, reinterpret_cast<uintptr_t>(stream)}];
+    if (e.first && e.second >= bytes) return e.first;
+    cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &status) != cudaSuccess || status != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    size_t want = e.second ? 2 * e.second : (size_t)16 << 20;
+    while (want < bytes) want *= 2;
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, want) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    e = {ptr, want};
+    return ptr;
 }
 
 // Token-tile width and split-K factor by M (the strategy choice). IDOL_B200_GEMM_BN and IDOL_B200_GEMM_SPLITS force
@@ -1078,7 +1199,40 @@ static int q8_gemm_impl(const GemmCall& c, bool* head_norm_fused) {
     // IDOL_B200_GEMM_PAIR = 1 / 0 forces it on (for 128- or 256-token tiles) / off.
     const int forced_pair = env_int("IDOL_B200_GEMM_PAIR", -1);
     const bool q8 = w.format == kFmtQ8;  // the persistent kernels read Q8_0 tiles only
-    const bool pair = q8 && bn >= 128 && (forced_pair == 1 ||
+    // Large M: dequantise the window's row tiles into the dense layout (one launch, about 3 bytes of traffic per
+    // weight) and run the dense persistent kernel on CTA pairs: its MMA thread no longer shares the SM with eight
+    // dequantising warps and their per-stage barrier traffic, and a 256 x 256 tile per pair halves the token bytes
+    // each CTA loads. Measured on B200 against the fused kernels (CUDA graphs, operands in HBM): 16384 x 1024 x 3072
+    // 113 -> 87 us, 16384 x 1024 x 4096 147 -> 111, 16384 x 4096 x 1024 126 -> 107, 4096 x 1024 x 3072 36 -> 31; the
+    // denoiser block's QKV 214 -> 162, ff1 301 -> 230, ff2 264 -> 227 (32768 tokens); the Gaussian MLP's 512 -> 512
+    // layer 210 -> 181. Where the pairs' tiles do not fill the SM pairs once (4096 x 4096 x 1024: 64 tiles for 74
+    // pairs) the fused kernel's split K stays faster (33 against 35 us), and a window of one 128-row tile (N = 14)
+    // runs the dense kernel on one CTA (56 -> 52 us; a pair would leave half its rows empty: 72). IDOL_B200_GEMM_DENSE
+    // = 0 / 2 forces it off / on for every M > 16.
+    bool dense = false;
+    const int dense_mode = env_int("IDOL_B200_GEMM_DENSE", 1);
+    const int dense_units = (c.n_offset + c.n - p.row_begin + 2 * kRowsPerTile - 1) / (2 * kRowsPerTile);
+    const bool dense_fills = (long long)dense_units * ((c.m + 255) / 256) >= num_sms(w.device) / 2;
+    if (q8 && (dense_mode == 2 || (dense_mode == 1 && c.m >= kDenseMinM && dense_fills))) {
+        void* scratch = dense_scratch(w.device, c.stream,
+                                      (size_t)p.row_tiles * p.layout_stages * (size_t)kDenseChunkBytes);
+        if (scratch) {
+            const int t_first = p.row_begin / kRowsPerTile;
+            const long long chunk0 = (long long)t_first * p.layout_stages;
+            const unsigned grid = (unsigned)((long long)tiles_n * p.layout_stages);
+            uint8_t* dense_tiles = static_cast<uint8_t*>(scratch);
+            if (c.x_dtype == IDOL_BF16)
+                q8_dense_tiles_kernel<true><<<grid, 128, 0, c.stream>>>(w.tiles + chunk0 * kChunkBytes,
+                                                                       dense_tiles + chunk0 * kDenseChunkBytes);
+            else
+                q8_dense_tiles_kernel<false><<<grid, 128, 0, c.stream>>>(w.tiles + chunk0 * kChunkBytes,
+                                                                        dense_tiles + chunk0 * kDenseChunkBytes);
+            IDOL_CUDA(cudaGetLastError());
+            p.tiles = dense_tiles;
+            dense = true;
+        }
+    }
+    const bool pair = !dense && q8 && bn >= 128 && (forced_pair == 1 ||
                                     (forced_pair != 0 && p.stages_total <= 8 && c.n >= 256 && c.m >= 4096));
     // The persistent single-CTA kernel (192-token tiles, double-buffered accumulator, a 2-byte output leaving
     // through a staging tile and TMA stores): measured on B200 it pays at K <= 1024 once the 192-token tiles number
@@ -1091,14 +1245,19 @@ static int q8_gemm_impl(const GemmCall& c, bool* head_norm_fused) {
     const bool staged = staged_output_ok(c);
     const int forced_persist = env_int("IDOL_B200_GEMM_PERSIST", -1);
     const long long tiles192 = (long long)tiles_n * ((c.m + 191) / 192);
-    const bool persist1 = q8 && !pair && bn >= 256 &&
+    const bool persist1 = !dense && q8 && !pair && bn >= 256 &&
                           (forced_persist == 1 ||
                            (forced_persist != 0 && (staged || c.y_dtype == IDOL_F32) && p.stages_total <= 16 &&
                             2 * tiles192 >= (staged ? 9LL : 8LL) * num_sms(w.device)));
-    if (pair || persist1) {
-        const int kind = pair ? 0 : 1;
-        const int pbn = kind == 1 ? 192 : bn >= 256 ? 192 : 128;  // two accumulators fit TMEM beside the A slots
-        const int unit_rows = kind == 0 ? 2 * kRowsPerTile : kRowsPerTile;
+    if (dense || pair || persist1) {
+        // The dense path runs on CTA pairs (kind 3), on one CTA (kind 2) for a window of one 128-row tile or with
+        // IDOL_B200_GEMM_DENSE_PAIR = 0.
+        const int kind = dense ? (tiles_n > 1 && env_int("IDOL_B200_GEMM_DENSE_PAIR", 1) != 0 ? 3 : 2)
+                               : pair ? 0 : 1;
+        const bool two = kind == 0 || kind == 3;  // CTA pairs
+        // Two accumulators fit TMEM: beside the A slots (192 or 128 tokens), or alone (dense pair: 256).
+        const int pbn = kind == 3 ? 256 : kind != 0 ? 192 : bn >= 256 ? 192 : 128;
+        const int unit_rows = two ? 2 * kRowsPerTile : kRowsPerTile;
         p.stages_per_split = p.stages_total;
         const int units = (c.n_offset + c.n - p.row_begin + unit_rows - 1) / unit_rows;
         const int tiles_m = (int)((c.m + pbn - 1) / pbn);
@@ -1108,15 +1267,26 @@ static int q8_gemm_impl(const GemmCall& c, bool* head_norm_fused) {
         const int rc = encode_tmap_2d(&xmap, c.x_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                                       c.x, (uint64_t)w.k, (uint64_t)c.m, (uint64_t)c.ldx * 2, kStageK,
-                                      kind == 0 ? pbn / 2 : pbn, CU_TENSOR_MAP_SWIZZLE_128B);
+                                      two ? pbn / 2 : pbn, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc != IDOL_OK) return rc;
+        // The dense pair's weight tiles: the dense layout as rows of 64 values (128 bytes), one 128-row box per
+        // (row tile, stage), no swizzle (the layout holds it already).
+        CUtensorMap wmap = xmap;
+        if (kind == 3) {
+            const int wrc = encode_tmap_2d(&wmap, c.x_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                           p.tiles, (uint64_t)kStageK,
+                                           (uint64_t)p.row_tiles * p.layout_stages * kRowsPerTile, kStageK * 2,
+                                           kStageK, kRowsPerTile, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (wrc != IDOL_OK) return wrc;
+        }
         // The output tensor map of the staged epilogue (one CTA, 2-byte output): the window [c.n features x M
         // tokens], one 128 x 192 box per tile. A TMA store needs a 16-byte aligned base and row stride, and an x
         // coordinate (tile start - n_offset) that is a non-negative multiple of 8 elements: windows that start on
         // a 128-row tile.
         CUtensorMap ymap = xmap;
         p.y_tma = 0;
-        if (kind == 1 && staged) {
+        if (kind != 0 && staged) {
             if (encode_tmap_2d(&ymap, c.y_dtype == IDOL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                                c.y, (uint64_t)c.n, (uint64_t)c.m, (uint64_t)c.ldy * 2, kRowsPerTile, pbn,
@@ -1133,15 +1303,15 @@ static int q8_gemm_impl(const GemmCall& c, bool* head_norm_fused) {
             *head_norm_fused = true;
         }
         const bool bf16 = c.x_dtype == IDOL_BF16;
+        const cudaStream_t st = c.stream;
         if (c.y_dtype == IDOL_F32)
-            return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
-                        : dispatch_persistent<false, float>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, float>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st)
+                        : dispatch_persistent<false, float>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st);
         if (c.y_dtype == IDOL_BF16)
-            return bf16 ? dispatch_persistent<true, __nv_bfloat16>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
-                        : dispatch_persistent<false, __nv_bfloat16>(kind, pbn, xmap, ymap, p, units, tiles_m,
-                                                                    c.stream);
-        return bf16 ? dispatch_persistent<true, __half>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream)
-                    : dispatch_persistent<false, __half>(kind, pbn, xmap, ymap, p, units, tiles_m, c.stream);
+            return bf16 ? dispatch_persistent<true, __nv_bfloat16>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st)
+                        : dispatch_persistent<false, __nv_bfloat16>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st);
+        return bf16 ? dispatch_persistent<true, __half>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st)
+                    : dispatch_persistent<false, __half>(kind, pbn, xmap, ymap, wmap, p, units, tiles_m, st);
     }
     p.stages_per_split = (p.stages_total + splits - 1) / splits;
     splits = (p.stages_total + p.stages_per_split - 1) / p.stages_per_split;  // every split gets >= 1 stage
