@@ -173,6 +173,7 @@ def test_cta_pair_kernel(pkg, oracle, cuda, kind, bn, env, m, n, k, n_off, cnt, 
     with GELU."""
     monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
     monkeypatch.setenv(env, "1")
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "0")  # the fused kernels (the dense path has its own tests)
     rng = np.random.default_rng(m + n + k + bn)
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
@@ -200,6 +201,7 @@ def test_single_persistent_staged_epilogue(pkg, oracle, cuda, m, n, k, n_off, cn
     row strides; ragged M and N clipped by the store); a window at 64 and a row stride of an odd number of elements
     take the direct-store kernel. Bias, a residual that aliases the output, and every activation."""
     monkeypatch.setenv("IDOL_B200_GEMM_PERSIST", "1")
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "0")
     rng = np.random.default_rng(m + n + k + act)
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
@@ -233,6 +235,7 @@ def test_cta_pair_kernel_many_tiles_per_pair(pkg, oracle, cuda, kind, bn, env, m
     tokens of 96-deep K give up to 7 tiles per pair, two stages each, the second a single 32-deep block)."""
     monkeypatch.setenv("IDOL_B200_GEMM_BN", str(bn))
     monkeypatch.setenv(env, "1")
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "0")
     rng = np.random.default_rng(m + n + k)
     q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
     b = rng.normal(0, 0.5, n).astype(np.float32)
@@ -430,3 +433,72 @@ def test_projection_with_head_norm_equals_gemm_then_rms_heads(pkg, cuda, m, dim,
     torch.cuda.synchronize()
     assert torch.equal(got, ref), f"max abs diff {(got.float() - ref.float()).abs().max().item()}"
     assert pkg._capi.device_status(0) == 0
+
+
+DENSE = [("pair", "1"), ("one CTA", "0")]
+
+
+@pytest.mark.parametrize("kind,pair_env", DENSE)
+@pytest.mark.parametrize("m,n,k,n_off,cnt", [(300, 200, 1056, 0, 200), (4097, 71, 256, 0, 71), (1000, 600, 512, 64, 500),
+                                             (2049, 1024, 4096, 0, 1024), (129, 384, 96, 128, 200),
+                                             (5000, 640, 1024, 128, 384), (3000, 14, 512, 0, 14)])
+def test_dense_path(pkg, oracle, cuda, kind, pair_env, m, n, k, n_off, cnt, monkeypatch):
+    """The large-M dense path (the window's weights dequantised into the dense tile layout, then the persistent
+    dense kernel on CTA pairs or on one CTA): ragged M and N (an odd number of 128-row tiles leaves a pair's second
+    tile past N or outside the window), windows, K ending in a single 32-deep block, a residual with GELU, fp16
+    activations, and a bf16 output in place over its residual through the staged epilogue."""
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "2")
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE_PAIR", pair_env)
+    rng = np.random.default_rng(m + n + k + 7)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    res = rng.normal(0, 1, (m, cnt)).astype(np.float32)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    rows = np.unique(np.concatenate([np.linspace(0, m - 1, 64).astype(int), np.arange(max(0, m - 20), m)]))
+    y = _gemm(pkg, cuda, x, tiles, b, n, k, n_off, cnt, res, act=1)
+    _check(y[rows], oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], 1),
+           what=f"dense {kind} {m}x{n}x{k} window {n_off}+{cnt}")
+    x16 = x.astype(np.float16).astype(np.float32)
+    y16 = _gemm(pkg, cuda, x16, tiles, b, n, k, x_dtype=torch.float16, out_dtype=torch.float16)
+    _check(y16[rows], oracle.gemm_q8(x16[rows], q8, b, n, k), what=f"dense {kind} fp16 {m}x{n}x{k}")
+    yb = torch.from_numpy(res).to(cuda, torch.bfloat16)
+    resb = yb.float().cpu().numpy()
+    pkg.gemm_into(yb, torch.from_numpy(x).to(cuda, torch.bfloat16), tiles, torch.from_numpy(b).to(cuda), n, k, n_off,
+                  cnt, yb, 2, 0)
+    _check_2byte_out(yb.float().cpu().numpy()[rows], oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, resb[rows], 2),
+                     torch.bfloat16, what=f"dense {kind} bf16 in place {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 3072, 1024), (3000, 1000, 4096), (2048, 384, 96)])
+def test_dense_path_equals_the_fused_kernel(pkg, cuda, m, n, k, monkeypatch):
+    """Both paths feed the tensor cores the same operand values (the operand-type rounding of the exact d q) in the
+    same k order, so with K unsplit the dense path reproduces the fused kernel bit for bit."""
+    g = torch.Generator(device=cuda).manual_seed(m + n + k)
+    w = torch.randn((n, k), device=cuda, generator=g) * 0.05
+    tiles = pkg.repack(pkg.quantize(w), n, k)
+    b = torch.randn(n, device=cuda, generator=g) * 0.1
+    x = torch.randn((m, k), device=cuda, generator=g).to(torch.bfloat16)
+    outs = {}
+    for mode in ("0", "2"):
+        monkeypatch.setenv("IDOL_B200_GEMM_DENSE", mode)
+        y = torch.empty((m, n), device=cuda, dtype=torch.float32)
+        pkg.gemm_into(y, x, tiles, b, n, k, flags=2)  # IDOL_GEMM_WHOLE_K
+        outs[mode] = y
+    torch.cuda.synchronize()
+    diff = (outs["0"] - outs["2"]).abs().max().item()
+    assert torch.equal(outs["0"], outs["2"]), f"dense and fused differ by up to {diff}"
+
+
+def test_dense_scratch_grows_and_stays_correct(pkg, oracle, cuda, monkeypatch):
+    """The dense path's per-stream scratch grows when a larger weight comes (the smaller buffer stays valid for
+    graphs captured before): small, large, small again on one stream, each against the oracle."""
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "2")
+    rng = np.random.default_rng(99)
+    for n, k in ((256, 256), (4096, 4096), (256, 256)):
+        q8 = oracle.q8_quantize(rng.normal(0, 0.1, (n, k)).astype(np.float32))
+        x = _bf16(oracle, rng.normal(0, 1, (1100, k)).astype(np.float32))
+        tiles = _upload(pkg, cuda, q8, n, k)
+        y = _gemm(pkg, cuda, x, tiles, None, n, k)
+        rows = np.arange(0, 1100, 37)
+        _check(y[rows], oracle.gemm_q8(x[rows], q8, None, n, k), what=f"dense scratch {n}x{k}")
