@@ -52,7 +52,9 @@ BLOCK_FLOPS = (2.0 * BLOCK_IMAGES * BLOCK_TOKENS * (3 * BLOCK_D * BLOCK_D + BLOC
                + 4.0 * BLOCK_TOKENS ** 2 * BLOCK_D * BLOCK_IMAGES)
 STACK_BLOCKS, STACK_IMAGES, CFG = 24, 64, 2
 CHUNK_IMAGES = 4  # images per pass through the blocks (8 sequences, 32768 rows)
-LAUNCHES_PER_BLOCK = 7  # norm, qkv with the q/k norm fused, attention, out + residual, norm, ff1, ff2 + residual
+# norm, qkv with the q/k norm fused, attention, out + residual, norm, ff1, ff2 + residual, and before each of the four
+# GEMMs the launch that dequantises its weights into the dense layout (the large-M GEMM path)
+LAUNCHES_PER_BLOCK = 11
 METRIC = "denoiser-block steps/s (config 5: 24-block stack over 64 images x 2 CFG branches, sharded by image)"
 UNIT = "block-steps/s"
 

@@ -136,7 +136,13 @@ int idol_b200_q8_export(const idol_q8_matrix* matrix, void* q8_dev, int64_t nbyt
  *   residual : device, y_dtype, rows ldr apart, or NULL. May alias y.
  *   y        : device, y_dtype IDOL_BF16, IDOL_F16 or IDOL_F32, rows ldy apart.
  *   flags    : IDOL_EPI_* bits.
- * m == 0 or n == 0 is a no-op. */
+ * m == 0 or n == 0 is a no-op.
+ * From m = 1024 tokens (when the output tiles fill the GPU's SM pairs) the call dequantises the window's weights into
+ * a scratch buffer and runs a dense GEMM on it: the buffer belongs to the library, one per device and stream, 2 bytes
+ * per weight of the largest matrix used on that stream, allocated on first need (never while the stream is being
+ * captured into a CUDA graph: such a call takes the fused kernel) and kept until the process exits. Calls on one
+ * stream share it in stream order. The environment variable IDOL_B200_GEMM_DENSE=0 turns this path off, so that the
+ * library allocates nothing of its own. */
 int idol_b200_q8_gemm(const idol_q8_matrix* matrix, const void* x, int x_dtype, int64_t m, int64_t ldx, int n_offset,
                       int n, const void* residual, int64_t ldr, int act, int flags, void* y, int y_dtype, int64_t ldy,
                       void* stream);
