@@ -1124,7 +1124,9 @@ static void* dense_scratch(int device, cudaStream_t stream, size_t bytes) {
 // the CTAs cover the SMs; above that a split pays only when K is long (>= 32 stages) and the tiles are few, since the
 // cluster reduction costs about as much as a short main loop.
 static void choose_tiles(int device, int64_t m, int tiles_n, int stages_total, int* bn, int* splits) {
-    int b = m <= 16 ? 16 : m <= 32 ? 32 : m <= 128 ? 64 : 256;
+    // 65-128 tokens: four 32-token tiles split K less deeply than two 64-token tiles for the same CTA count
+    // (128 x 4096 x 1024: 17.9 -> 11.4 us; 128 x 1024 x 3072: 10.1 -> 9.7 us, measured on B200).
+    int b = m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 32 : 256;
     const int forced_bn = env_int("IDOL_B200_GEMM_BN", 0);
     if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) b = forced_bn;
     const int tiles = tiles_n * (int)((m + b - 1) / b);
