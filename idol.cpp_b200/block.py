@@ -161,7 +161,11 @@ class DenoiserStack:
     """A stack of DenoiserBlocks (the denoiser's 24 transformer blocks, tools/export_full_gguf.py:311-314) over a
     batch of independent sequences: each image's CFG branches are separate sequences of `tokens` rows that attend only
     within themselves (batched CFG, tools/idol_generate.py:153,193). forward_ runs `chunk` sequences at a time through
-    every block (so the workspace is sized by the chunk, not the batch) and shares one workspace across the blocks."""
+    every block (so the workspace is sized by the chunk, not the batch). With more than one chunk, consecutive chunks
+    go to `lanes` CUDA streams in turn (the caller's current stream and side streams the stack owns), each with its own
+    workspace: the chunks are independent, and the small memory-bound launches of one (LayerNorms, the GEMMs' weight
+    dequantisation) then run on SMs beside the other's attention or GEMM CTAs. Each chunk's kernels and their order are
+    the same in every lane count, so the result does not depend on it."""
 
     def __init__(self, blocks: Sequence[DenoiserBlock]):
         if not blocks:
@@ -170,23 +174,43 @@ class DenoiserStack:
         self.dim, self.device = self.blocks[0].dim, self.blocks[0].device
         if any(b.dim != self.dim or b.device != self.device for b in self.blocks):
             raise ValueError("DenoiserStack: blocks of different widths or devices")
-        self.ws = _Workspace()
+        self._ws = {}          # CUDA stream handle -> _Workspace (calls on different streams never share one)
+        self._side = []        # side streams of the lanes
 
-    def forward_(self, x: torch.Tensor, sequences: int, chunk: Optional[int] = None) -> torch.Tensor:
+    def _workspace(self, stream: "torch.cuda.Stream", nbytes: int, device) -> torch.Tensor:
+        # Allocated in the lane's stream order, so that the caching allocator hands the memory out again only in that
+        # order once the buffer is replaced.
+        with torch.cuda.stream(stream):
+            return self._ws.setdefault(stream.cuda_stream, _Workspace()).get(nbytes, device)
+
+    def forward_(self, x: torch.Tensor, sequences: int, chunk: Optional[int] = None, lanes: int = 2) -> torch.Tensor:
         """In place on x: [sequences * tokens, D] (fp32 or bf16, contiguous), `chunk` sequences per pass through the
-        blocks (all of them by default); launches on the current stream."""
+        blocks (all of them by default). Launches on the current stream, which waits for the side lanes before this
+        call returns (in stream order: nothing synchronises with the host)."""
         if not x.is_contiguous() or x.dim() != 2 or x.shape[1] != self.dim or sequences < 1 or x.shape[0] % sequences:
             raise ValueError("DenoiserStack: x must be a contiguous [sequences * tokens, D] tensor")
         tokens = x.shape[0] // sequences
         chunk = sequences if chunk is None else max(1, min(int(chunk), sequences))
-        lib, st = C.lib(), _stream(x.device)
-        ws = self.ws.get(self.blocks[0].workspace_bytes(chunk * tokens), x.device)
-        for s0 in range(0, sequences, chunk):
+        starts = list(range(0, sequences, chunk))
+        lanes = max(1, min(int(lanes), len(starts)))
+        lib = C.lib()
+        main = torch.cuda.current_stream(x.device)
+        while len(self._side) < lanes - 1:
+            self._side.append(torch.cuda.Stream(device=x.device))
+        streams = [main] + self._side[:lanes - 1]
+        nbytes = self.blocks[0].workspace_bytes(chunk * tokens)
+        ws = [self._workspace(st, nbytes, x.device) for st in streams]
+        for st in streams[1:]:
+            st.wait_stream(main)  # x and the workspaces were last touched in the main stream's order
+        for i, s0 in enumerate(starts):
+            lane = i % lanes
             n = min(chunk, sequences - s0)
             part = x[s0 * tokens:(s0 + n) * tokens]
             for b in self.blocks:
                 C.check(lib.idol_b200_block_forward(ctypes.c_void_p(b.handle), _ptr(part), _DTYPES[x.dtype], tokens,
-                                                    n, _ptr(ws), ws.numel(), st))
+                                                    n, _ptr(ws[lane]), ws[lane].numel(), streams[lane].cuda_stream))
+        for st in streams[1:]:
+            main.wait_stream(st)
         return x
 
 

@@ -272,6 +272,11 @@ def test_denoiser_stack_chunks_equal_block_by_block(pkg, oracle, cuda, monkeypat
     for chunk, y in outs.items():
         _check(y.cpu().numpy(), ref.cpu().numpy(), what=f"stack chunk {chunk} vs unchunked")
     assert torch.equal(outs[6], ref), "one chunk of every sequence must be the unchunked run"
+    for lanes in (1, 3):  # chunks on one stream, or spread over three: the same kernels per chunk
+        y = x0.clone()
+        stack.forward_(y, seqs, 2, lanes=lanes)
+        torch.cuda.synchronize()
+        assert torch.equal(y, outs[2]), f"chunk 2 on {lanes} lane(s) differs from the default two lanes"
     monkeypatch.setenv("IDOL_B200_GEMM_SPLITS", "1")  # read at each GEMM call
     ref, outs = run_all((1, 2, 4, 6))
     monkeypatch.delenv("IDOL_B200_GEMM_SPLITS")
