@@ -794,7 +794,7 @@ def measure_single_image_latency(stack, dev, stream, world, passes=3):
 
     def one_pass(record):
         if world == 1:
-            stack.forward_(x, CFG)
+            stack.forward_(x, CFG, 1)  # each CFG branch a chunk: the two run on the stack's two lanes
         else:
             for b in stack.blocks:
                 column_parallel_block_forward_(b, x, images=CFG, gather_events=events if record else None)
@@ -822,7 +822,7 @@ def measure_single_image_latency(stack, dev, stream, world, passes=3):
         ms, gather_ms = float(t[0]), float(t[1])
     return {"metric": "single-request latency: the 24-block stack over one image (2 CFG branches x 4096 tokens)",
             "ms_per_pass": round(ms / passes, 3), "passes": passes,
-            "mode": ("one GPU" if world == 1 else
+            "mode": ("one GPU, the two CFG branches on two streams" if world == 1 else
                      f"column-parallel MLP over {world} GPUs (ff1/ff2 split by output features, NCCL all-gather of "
                      "each slice; equal to the one-GPU result bit for bit)"),
             "all_gather_share": None if world == 1 else round(gather_ms / ms, 3)}
