@@ -205,6 +205,17 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// 4-byte asynchronous global -> shared copy (cp.async, tracked by this thread's commit groups).
+__device__ __forceinline__ void cp_async4(uint32_t smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Returns once at most N of this thread's cp.async groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Asks L2 to fetch [src, src + bytes) from global memory (src 16-byte aligned, bytes a multiple of 16). A hint with
 // nothing to wait for; the range must lie inside an allocation.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {

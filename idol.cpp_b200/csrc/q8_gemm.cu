@@ -237,6 +237,50 @@ __device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, 
     }
 }
 
+// epilogue_span for an fp32 output with an fp32 residual, the residual streamed through this warp's ring in shared
+// memory (`ring`: two buffers of kResGroup tokens x 32 lanes of floats): each lane copies its own feature's values of
+// the next group of tokens with 4-byte cp.async while the current group is finished, so the bytes in flight are not
+// bounded by the registers a thread can hold (the residual loads bounded the out projection: 0.45 of the tensor peak).
+// A lane reads only the words it copied, so its own cp.async wait is the only synchronisation. Addresses are clamped as
+// in epilogue_span; values read for positions outside the window or past M are never used.
+constexpr int kResGroup = 32;
+template <int kSpan>
+__device__ __forceinline__ void epilogue_span_res_ring(const Params& p, int m0, int row, uint32_t acc, float bias,
+                                                       bool row_ok, uint32_t ring, int lane) {
+    static_assert(kSpan % kResGroup == 0, "whole groups");
+    const float* res = static_cast<const float*>(p.residual) + (row_ok ? row - p.n_offset : 0);
+    const int groups = min(kSpan, p.m - m0 + kResGroup - 1) / kResGroup;  // groups with at least one token below M
+    auto issue = [&](int g) {
+        const uint32_t dst = ring + (uint32_t)(((g & 1) * kResGroup * 32 + lane) * 4);
+#pragma unroll 8
+        for (int j = 0; j < kResGroup; ++j)
+            cp_async4(dst + (uint32_t)(j * 32 * 4), res + (long long)min(m0 + g * kResGroup + j, p.m - 1) * p.ldr);
+        cp_async_commit();
+    };
+    if (groups > 0) issue(0);
+    for (int g = 0; g < groups; ++g) {
+        if (g + 1 < groups) issue(g + 1);
+        else cp_async_commit();  // an empty group keeps "all but the newest group" meaning group g
+        cp_async_wait<1>();
+        const uint32_t src = ring + (uint32_t)(((g & 1) * kResGroup * 32 + lane) * 4);
+#pragma unroll
+        for (int c0 = 0; c0 < kResGroup; c0 += 16) {
+            float rv[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float v;
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(src + (uint32_t)((c0 + j) * 32 * 4)));
+                rv[j] = v;
+            }
+            uint32_t v[16];
+            tmem_ld16(acc + g * kResGroup + c0, v);
+            tmem_ld_wait();
+            finish_cols<float, 16, true>(p, m0 + g * kResGroup + c0, row, v, bias, row_ok, rv);
+        }
+    }
+    cp_async_wait<0>();
+}
+
 // The staged form of epilogue_span for the TMA-store path: the finished value of token m0 + j goes to shared address
 // st + 256 j of the staging tile (token-major, 128 features of 2 bytes per token; this lane's feature folded into st),
 // and a single TMA store later writes the tile. Features outside the output window and tokens past M are written
@@ -553,7 +597,7 @@ constexpr int kPairThreads = 64 + 32 * kDequantWarps + 32 * kEpilogueWarps;
 // kYStage: bytes of the shared staging tile the epilogue hands to TMA stores (0: the epilogue stores directly).
 // kDense: the weights of a stage arrive already dequantised (a 16 KB tile of the dense layout, see
 // q8_dense_tiles_kernel) and both MMA operands come from shared memory; no A slots in tensor memory.
-template <int BN, int S, int SA, bool kPair, int kYStage = 0, bool kDense = false>
+template <int BN, int S, int SA, bool kPair, int kYStage = 0, bool kDense = false, bool kResRing = false>
 struct ConfigPersistent {
     static constexpr int kHalf = kPair ? BN / 2 : BN;  // token rows this CTA loads per stage
     static constexpr int kXBytes = kHalf * 128;
@@ -567,7 +611,9 @@ struct ConfigPersistent {
     // Dequant groups alternate by stage parity: an even SA keeps each A slot (afull) with one group; an odd S needs
     // the A-slot wait (SA < S) to order the parity waits on a stage slot the two groups share.
     static_assert(SA % 2 == 0 && (S % 2 == 0 || SA < S), "stage and A-slot counts");
-    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kYStage + kBarBytes;
+    // kResRing: each epilogue warp's residual ring (epilogue_span_res_ring), 8 KB per warp.
+    static constexpr int kRingBytes = kResRing ? kEpilogueWarps * 2 * kResGroup * 32 * 4 : 0;
+    static constexpr int kSmemUsed = 1024 + S * kStageBytes + kYStage + kRingBytes + kBarBytes;
     // At least 120 KB: one CTA per SM, so a TMEM allocation of 512 columns never waits on a neighbour.
     static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
     static_assert(kColsNeeded <= 512, "TMEM budget");
@@ -650,11 +696,12 @@ __device__ __forceinline__ void head_norm_staged(uint8_t* ys, int tile_row0, con
     }
 }
 
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage, bool kDense>
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage, bool kDense, bool kResRing>
 __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
     const __grid_constant__ CUtensorMap wmap, const Params p, const PersistentSchedule sched) {
-    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense>;
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense, kResRing>;
+    static_assert(!kResRing || (kYStage == 0 && sizeof(OutT) == 4), "the residual ring serves the fp32 direct path");
     static_assert(kYStage == 0 || ((!kPair || kDense) && sizeof(OutT) == 2 && kYStage >= BN * kRowsPerTile * 2),
                   "staging: one CTA (or a dense pair), a 2-byte output and room for the whole tile");
     constexpr int kRowsPerUnit = kPair ? 2 * kRowsPerTile : kRowsPerTile;
@@ -663,7 +710,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     uint8_t* xs = smem;
     uint8_t* ys = xs + S * C::kXBytes;                                              // output staging (1024-aligned)
     uint8_t* ws = ys + C::kYStageBytes;                                             // S weight stages
-    uint64_t* xfull = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);             // even CTA: both halves landed
+    uint8_t* rs = ws + S * C::kWBytes;                                              // residual rings (kResRing)
+    uint64_t* xfull = reinterpret_cast<uint64_t*>(rs + C::kRingBytes);              // even CTA: both halves landed
     uint64_t* cfull = xfull + S;                                                    // this CTA's codes landed
     uint64_t* empty = cfull + S;                                                    // both: stage s consumed
     uint64_t* afull = empty + S;                                                    // even CTA: A slot written (both)
@@ -943,7 +991,16 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
                 ++ns;
                 nh += hn ? 1 : 0;
             } else {
-                epilogue_span<OutT, kHalfCols, kDense ? 32 : 16>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
+                if constexpr (kResRing) {
+                    if (p.residual != nullptr)
+                        epilogue_span_res_ring<kHalfCols>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok,
+                                                          smem_u32(rs) + (uint32_t)(ew * 2 * kResGroup * 32 * 4), lane);
+                    else
+                        epilogue_span<OutT, kHalfCols, 32>(p, m0 + c_begin, row, acc + c_begin, bias, row_ok);
+                } else {
+                    epilogue_span<OutT, kHalfCols, kDense ? 32 : 16>(p, m0 + c_begin, row, acc + c_begin, bias,
+                                                                     row_ok);
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -966,11 +1023,12 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     }
 }
 
-template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage = 0, bool kDense = false>
+template <int BN, int S, int SA, bool kPair, bool kBF16, typename OutT, int kYStage = 0, bool kDense = false,
+          bool kResRing = false>
 int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const CUtensorMap& wmap, const Params& p,
                       int units_n, int tiles_m, cudaStream_t stream) {
-    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense>;
-    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT, kYStage, kDense>;
+    using C = ConfigPersistent<BN, S, SA, kPair, kYStage, kDense, kResRing>;
+    auto kern = q8_gemm_persistent_kernel<BN, S, SA, kPair, kBF16, OutT, kYStage, kDense, kResRing>;
     static unsigned long long configured = 0;
     int dev = 0;
     IDOL_CUDA(cudaGetDevice(&dev));
@@ -1011,6 +1069,14 @@ int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtenso
             if (p.y_tma)
                 return launch_persistent<256, 5, 4, true, kBF16, OutT, 256 * kRowsPerTile * 2, true>(
                     xmap, ymap, wmap, p, units, tiles_m, stream);
+        }
+        if constexpr (sizeof(OutT) == 4) {
+            // Five stages beside the 64 KB residual rings where the epilogue's residual traffic, not the main loop,
+            // bounds the tile: K <= 1024 (the blocks' out projection 91.2 -> 86.7 us at 32768 tokens); at K = 4096 the
+            // sixth stage is worth more (ff2 221.7 against 224.7 us).
+            if (p.residual != nullptr && p.stages_total <= 16)
+                return launch_persistent<256, 5, 4, true, kBF16, OutT, 0, true, true>(xmap, ymap, wmap, p, units,
+                                                                                    tiles_m, stream);
         }
         return launch_persistent<256, 6, 4, true, kBF16, OutT, 0, true>(xmap, ymap, wmap, p, units, tiles_m, stream);
     }
