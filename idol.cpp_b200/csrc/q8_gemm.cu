@@ -549,6 +549,9 @@ constexpr int64_t kDenseMinM = 1024;
 template <bool kBF16>
 __global__ void __launch_bounds__(128) q8_dense_tiles_kernel(const uint8_t* __restrict__ tiles,
                                                              uint8_t* __restrict__ dense) {
+    // The dense GEMM that follows is a programmatic dependent launch: it may start its set-up now and waits for this
+    // grid to complete (griddepcontrol.wait) before it reads anything from global memory.
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint8_t* src = tiles + (long long)blockIdx.x * kChunkBytes;
     uint8_t* dst = dense + (long long)blockIdx.x * kDenseChunkBytes;
     const int r = threadIdx.x, q = r / 32, lane = r % 32;  // thread r: row r of the tile (lane r of quarter q)
@@ -762,6 +765,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) q8_gemm_persistent_kernel(
     if constexpr (kPair) cluster_sync();  // the peer's barriers exist before anything arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // Dense: launched as a programmatic dependent of the dequantisation kernel, so the set-up above overlapped it;
+    // nothing global (weights, tokens, bias, residual, output) is touched before that grid has completed. A no-op for
+    // an ordinary launch.
+    if constexpr (kDense) asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0) {
         if (lane == 0) {
@@ -1045,13 +1052,22 @@ int launch_persistent(const CUtensorMap& xmap, const CUtensorMap& ymap, const CU
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if constexpr (kPair) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if constexpr (kDense) {  // right after its dequantisation launch on the same stream (q8_gemm_impl)
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = kPair ? 1 : 0;
+    cfg.numAttrs = na;
     IDOL_CUDA(cudaLaunchKernelEx(&cfg, kern, xmap, ymap, wmap, p, sched));
     return IDOL_OK;
 }
