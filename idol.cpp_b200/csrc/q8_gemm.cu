@@ -18,6 +18,11 @@
 // K range into TMEM, parks the partial tile in its own shared memory, and after a cluster barrier every CTA sums a
 // share of the tile's tokens over the cluster through distributed shared memory. No global scratch is used.
 //
+// Large M (from 1024 tokens, when the tiles fill the GPU) takes the dense path instead: q8_dense_tiles_kernel
+// dequantises the window's weights into a per-(device, stream) scratch laid out as pre-swizzled bf16/f16 tiles, and
+// the persistent kernel in dense mode runs on CTA pairs (256 x 256 tiles) with both MMA operands fed by TMA into shared
+// memory, its MMA thread free of the dequantising warps' per-stage hand-offs (see q8_gemm_impl for the measurements).
+//
 // Every spin-wait is bounded (ptx.cuh mbar_wait); a timeout raises a sticky device error bit and the kernel winds
 // down instead of hanging.
 #include <cuda_bf16.h>
