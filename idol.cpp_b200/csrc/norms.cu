@@ -76,7 +76,7 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, TO* __
 #pragma unroll
     for (int i = 0; i < PER / VEC; ++i) {
         const int c = VEC * (lane + 32 * i);
-        TO out[VEC];
+        alignas(16) TO out[VEC];
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
             float t = (v[i * VEC + j] - mean) * inv;
@@ -84,11 +84,16 @@ __global__ void norm_rows_kernel(const TI* __restrict__ x, long long ldx, TO* __
             if (scale) t = t * (1.0f + scale[c + j]) + shift[c + j];
             out[j] = from_f<TO>(t);
         }
-        if constexpr (sizeof(TO) == sizeof(TI)) {
+        // One vector store of the lane's VEC outputs (8, 16 or 32 bytes; the row offset c is a multiple of VEC and
+        // every caller passes 16-byte aligned rows).
+        if constexpr (sizeof(TO) * VEC == 8) {
+            *reinterpret_cast<uint2*>(yr + c) = *reinterpret_cast<const uint2*>(out);
+        } else if constexpr (sizeof(TO) * VEC == 16) {
             *reinterpret_cast<uint4*>(yr + c) = *reinterpret_cast<const uint4*>(out);
         } else {
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) yr[c + j] = out[j];
+            for (int k = 0; k < (int)(sizeof(TO) * VEC / 16); ++k)
+                reinterpret_cast<uint4*>(yr + c)[k] = reinterpret_cast<const uint4*>(out)[k];
         }
     }
 }
