@@ -209,6 +209,10 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
 __device__ __forceinline__ void cp_async4(uint32_t smem_dst, const void* gmem_src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
 }
+// 16-byte asynchronous global -> shared copy through L2 only (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gmem_src) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Returns once at most N of this thread's cp.async groups are still pending.
 template <int N>

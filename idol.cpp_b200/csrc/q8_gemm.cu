@@ -243,30 +243,52 @@ __device__ __forceinline__ void epilogue_span(const Params& p, int m0, int row, 
 }
 
 // epilogue_span for an fp32 output with an fp32 residual, the residual streamed through this warp's ring in shared
-// memory (`ring`: two buffers of kResGroup tokens x 32 lanes of floats): each lane copies its own feature's values of
-// the next group of tokens with 4-byte cp.async while the current group is finished, so the bytes in flight are not
-// bounded by the registers a thread can hold (the residual loads bounded the out projection: 0.45 of the tensor peak).
-// A lane reads only the words it copied, so its own cp.async wait is the only synchronisation. Addresses are clamped as
-// in epilogue_span; values read for positions outside the window or past M are never used.
+// memory (`ring`: two buffers of kResGroup tokens x 32 lanes of floats, token-major: the warp's 32 features of a token
+// are 128 contiguous bytes) while the current group is finished, so the bytes in flight are not bounded by the
+// registers a thread can hold (the residual loads bounded the out projection: 0.45 of the tensor peak). When the
+// warp's 32 features all lie in the window and start on a 16-byte boundary, each 16-byte cp.async copies four
+// features of one token (eight lanes per token, four tokens per instruction): a quarter of the copy instructions and
+// address arithmetic of one 4-byte copy per lane and token, which took issue slots from the MMA thread on the same
+// scheduler (tensor pipe 60% -> 43% active with the residual at 32768 x 1024 x 1024). Lanes then read words that
+// other lanes copied, so each group's wait is followed by a warp barrier, and a warp barrier before each issue keeps
+// a buffer from being refilled while a lane still reads it. Otherwise each lane copies its own feature's values with
+// 4-byte copies. Addresses are clamped as in epilogue_span; values read for positions outside the window or past M
+// are never used.
 constexpr int kResGroup = 32;
 template <int kSpan>
 __device__ __forceinline__ void epilogue_span_res_ring(const Params& p, int m0, int row, uint32_t acc, float bias,
                                                        bool row_ok, uint32_t ring, int lane) {
-    static_assert(kSpan % kResGroup == 0, "whole groups");
-    const float* res = static_cast<const float*>(p.residual) + (row_ok ? row - p.n_offset : 0);
+    static_assert(kSpan % kResGroup == 0 && kResGroup % 4 == 0, "whole groups");
+    const int col0 = row - lane - p.n_offset;  // the window column of the warp's first feature
+    const bool vec = __all_sync(0xffffffffu, row_ok) && col0 % 4 == 0 && p.ldr % 4 == 0 &&
+                     reinterpret_cast<uintptr_t>(p.residual) % 16 == 0;
+    const float* res = static_cast<const float*>(p.residual) + (vec ? col0 + (lane % 8) * 4 : (row_ok ? row - p.n_offset : 0));
     const int groups = min(kSpan, p.m - m0 + kResGroup - 1) / kResGroup;  // groups with at least one token below M
+    // The outputs leave the same way when the output rows allow 16-byte stores and no activation follows.
+    const bool vst = vec && p.act == IDOL_ACT_NONE && p.ldy % 4 == 0 && reinterpret_cast<uintptr_t>(p.y) % 16 == 0;
+    float* yv = static_cast<float*>(p.y) + col0 + (lane % 8) * 4;
     auto issue = [&](int g) {
-        const uint32_t dst = ring + (uint32_t)(((g & 1) * kResGroup * 32 + lane) * 4);
+        if (vec) {
+            const uint32_t dst = ring + (uint32_t)(((g & 1) * kResGroup * 32 + (lane / 8) * 32 + (lane % 8) * 4) * 4);
+#pragma unroll
+            for (int j = 0; j < kResGroup; j += 4)
+                cp_async16(dst + (uint32_t)(j * 32 * 4),
+                           res + (long long)min(m0 + g * kResGroup + j + lane / 8, p.m - 1) * p.ldr);
+        } else {
+            const uint32_t dst = ring + (uint32_t)(((g & 1) * kResGroup * 32 + lane) * 4);
 #pragma unroll 8
-        for (int j = 0; j < kResGroup; ++j)
-            cp_async4(dst + (uint32_t)(j * 32 * 4), res + (long long)min(m0 + g * kResGroup + j, p.m - 1) * p.ldr);
+            for (int j = 0; j < kResGroup; ++j)
+                cp_async4(dst + (uint32_t)(j * 32 * 4), res + (long long)min(m0 + g * kResGroup + j, p.m - 1) * p.ldr);
+        }
         cp_async_commit();
     };
     if (groups > 0) issue(0);
     for (int g = 0; g < groups; ++g) {
+        __syncwarp();  // every lane has finished reading group g - 1, whose buffer group g + 1 refills
         if (g + 1 < groups) issue(g + 1);
         else cp_async_commit();  // an empty group keeps "all but the newest group" meaning group g
         cp_async_wait<1>();
+        __syncwarp();  // group g's copies of every lane have landed
         const uint32_t src = ring + (uint32_t)(((g & 1) * kResGroup * 32 + lane) * 4);
 #pragma unroll
         for (int c0 = 0; c0 < kResGroup; c0 += 16) {
@@ -280,7 +302,32 @@ __device__ __forceinline__ void epilogue_span_res_ring(const Params& p, int m0, 
             uint32_t v[16];
             tmem_ld16(acc + g * kResGroup + c0, v);
             tmem_ld_wait();
-            finish_cols<float, 16, true>(p, m0 + g * kResGroup + c0, row, v, bias, row_ok, rv);
+            if (vst) {
+                // The finished values go back into this lane's words of the ring.
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float a = __uint_as_float(v[j]);
+                    const float x = ((p.bias_after_round ? out_round<float>(a) : a) + bias) + rv[j];
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(src + (uint32_t)((c0 + j) * 32 * 4)), "f"(x));
+                }
+            } else {
+                finish_cols<float, 16, true>(p, m0 + g * kResGroup + c0, row, v, bias, row_ok, rv);
+            }
+        }
+        if (vst) {
+            // Each 16-byte store writes four features of one token (eight lanes per token, four tokens per
+            // instruction) from the ring.
+            __syncwarp();
+            const uint32_t vsrc = ring + (uint32_t)(((g & 1) * kResGroup * 32 + (lane / 8) * 32 + (lane % 8) * 4) * 4);
+#pragma unroll
+            for (int j = 0; j < kResGroup; j += 4) {
+                const int m = m0 + g * kResGroup + j + lane / 8;
+                uint4 w;
+                asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                             : "r"(vsrc + (uint32_t)(j * 32 * 4)));
+                if (m < p.m) *reinterpret_cast<uint4*>(yv + (long long)m * p.ldy) = w;
+            }
         }
     }
     cp_async_wait<0>();
@@ -1092,10 +1139,10 @@ int dispatch_persistent(int kind, int bn, const CUtensorMap& xmap, const CUtenso
                     xmap, ymap, wmap, p, units, tiles_m, stream);
         }
         if constexpr (sizeof(OutT) == 4) {
-            // Five stages beside the 64 KB residual rings where the epilogue's residual traffic, not the main loop,
-            // bounds the tile: K <= 1024 (the blocks' out projection 91.2 -> 86.7 us at 32768 tokens); at K = 4096 the
-            // sixth stage is worth more (ff2 221.7 against 224.7 us).
-            if (p.residual != nullptr && p.stages_total <= 16)
+            // Five stages beside the 64 KB residual rings: with 16-byte residual copies and stores the ring epilogue
+            // takes few enough issue slots that it wins at every K (the blocks' out projection at 32768 tokens
+            // 86.6 -> 79.0 us, ff2 220.8 -> 215.9 us against six stages and register-held residual groups).
+            if (p.residual != nullptr)
                 return launch_persistent<256, 5, 4, true, kBF16, OutT, 0, true, true>(xmap, ymap, wmap, p, units,
                                                                                     tiles_m, stream);
         }

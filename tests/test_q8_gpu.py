@@ -470,6 +470,37 @@ def test_dense_path(pkg, oracle, cuda, kind, pair_env, m, n, k, n_off, cnt, monk
                      torch.bfloat16, what=f"dense {kind} bf16 in place {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k,n_off,cnt,pad", [(4100, 1024, 1024, 0, 1024, 0), (3000, 700, 512, 128, 500, 4),
+                                                 (2500, 640, 256, 2, 600, 1), (2049, 384, 1024, 0, 384, 3),
+                                                 (1500, 300, 1024, 4, 296, 0)])
+def test_dense_fp32_residual_in_place(pkg, oracle, cuda, m, n, k, n_off, cnt, pad, monkeypatch):
+    """The dense pair kernel's fp32 residual epilogue (the denoiser's out projection: fp32 output over its own
+    residual, no activation): 16-byte residual copies and stores where a warp's 32 features lie in the window on a
+    16-byte boundary, 4-byte copies and per-lane stores elsewhere (windows at 2 and 4, a warp half outside the window,
+    padded and odd row strides); ragged M; the padding columns stay untouched."""
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE", "2")
+    monkeypatch.setenv("IDOL_B200_GEMM_DENSE_PAIR", "1")
+    rng = np.random.default_rng(m + n + k + n_off)
+    q8 = oracle.q8_quantize(rng.normal(0, 0.25, (n, k)).astype(np.float32))
+    x = _bf16(oracle, rng.normal(0, 1, (m, k)).astype(np.float32))
+    b = rng.normal(0, 0.5, n).astype(np.float32)
+    res = rng.normal(0, 1, (m, cnt)).astype(np.float32)
+    tiles = _upload(pkg, cuda, q8, n, k)
+    buf = torch.full((m, cnt + pad), 7.0, dtype=torch.float32, device=cuda)
+    y = buf[:, :cnt]
+    y.copy_(torch.from_numpy(res))
+    for _ in range(2):  # the second call reads the first call's output as its residual
+        pkg.gemm_into(y, torch.from_numpy(x).to(cuda, torch.bfloat16), tiles, torch.from_numpy(b).to(cuda), n, k,
+                      n_off, cnt, y, 0, 0)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.linspace(0, m - 1, 64).astype(int), np.arange(m - 20, m)]))
+    once = oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, res[rows], 0)
+    _check(y.cpu().numpy()[rows], oracle.gemm_q8(x[rows], q8, b, n, k, n_off, cnt, once, 0),
+           what=f"dense fp32 residual {m}x{n}x{k} window {n_off}+{cnt} pad {pad}")
+    if pad:
+        assert bool((buf[:, cnt:] == 7.0).all()), "the padding columns were written"
+
+
 @pytest.mark.parametrize("m,n,k", [(4096, 3072, 1024), (3000, 1000, 4096), (2048, 384, 96)])
 def test_dense_path_equals_the_fused_kernel(pkg, cuda, m, n, k, monkeypatch):
     """Both paths feed the tensor cores the same operand values (the operand-type rounding of the exact d q) in the
