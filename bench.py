@@ -921,21 +921,28 @@ def run_profile_shape(args):
         print(json.dumps({"profile": args.profile_shape, "ms_per_step": round(ms / args.steps, 3),
                           "device_status": pkg._capi.device_status(0)}))
         return
-    m, k, n = (int(v) for v in args.profile_shape.split(","))
+    fields = args.profile_shape.split(",")
+    m, k, n = (int(v) for v in fields[:3])
+    in_place = fields[3:] == ["res"]  # M,K,N,res: an fp32 output over its own fp32 residual (the blocks' out, ff2)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(7)
     packed = pkg.quantize(torch.randn((n, k), device=dev, generator=g) * 0.02)
     tiles = pkg.repack(packed, n, k)
     x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
     bias = torch.randn(n, device=dev, generator=g) * 0.01
-    y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    if in_place:
+        y = torch.randn((m, n), device=dev, generator=g)
+        call = lambda: pkg.gemm_into(y, x, tiles, bias, n, k, residual=y)  # noqa: E731
+    else:
+        y = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+        call = lambda: pkg.gemm_into(y, x, tiles, bias, n, k)  # noqa: E731
     for _ in range(args.warmup):
-        pkg.gemm_into(y, x, tiles, bias, n, k)
+        call()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        pkg.gemm_into(y, x, tiles, bias, n, k)
+        call()
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
@@ -1149,7 +1156,8 @@ def main():
     ap.add_argument("--no-gpu-baselines", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the config-5 stack (no sweep or compositions)")
     ap.add_argument("--profile-shape", default=None,
-                    help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture; 'block' or 'mlp' "
+                    help="M,K,N: run only this GEMM (warmup + steps launches) for an ncu capture (M,K,N,res: fp32 "
+                         "output in place over its fp32 residual); 'block' or 'mlp' "
                          "runs the config-3 block or the config-4 MLP instead, 'attention' or 'stack' the attention "
                          "kernel or the 24-block stack on one config-5 chunk")
     args = ap.parse_args()
