@@ -9,7 +9,7 @@
 //               applied in place to `heads` column groups of hd values in each row (rows ld apart).
 //
 // Both are HBM-bound: one read and one write of the activations. One warp per row (norm_rows) or per (row, head)
-// group (rms_heads); 16-byte loads and stores.
+// group (rms_heads); 16-byte loads, and one vector store per lane and chunk (8, 16 or 32 bytes by output type).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
